@@ -1,0 +1,517 @@
+"""SE12 fused decode + GEMV benchmark (B200).
+
+Workload (config 1 of the baseline): the GEMV set of one Gemma-2-2B decode
+step -- 26 decoder layers x (q, k, v, o, gate, up, down) + the 256000-row LM
+head, 183 matrices, 2.61 G weights -- at batch 1. Weights are random-init
+BF16 N(0, 0.02) with 0.01 % of entries scaled x64 and 0.1 % set to +-0
+(synthetic: no checkpoints on the box), packed to SE12 on the GPU by this
+package's encoder; activations are BF16 N(0, 1). One step = one replay of a
+CUDA graph holding the 183 fused GEMVs (programmatic dependent launch
+between them). Every step streams 3.93 GB of SE12 bytes, far more than the
+126 MB L2, so no L2 flush is needed between steps.
+
+Metric: compressed-byte HBM GB/s (1 GB = 1e9 B) = algorithmic SE12 bytes
+per step (five streams + codebook, + x + y) / step time; also BF16-
+equivalent GB/s (2 bytes per weight) and decode tok/s (GEMVs only).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Under torchrun (N > 1) every rank runs its own replica of the step (weak
+scaling, no collective in the data path); value is the sum over ranks of the
+bytes processed divided by the slowest rank's time.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import pathlib
+import statistics
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = pathlib.Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "SE12 decode+GEMV HBM GB/s (compressed bytes)"
+NOMINAL_HBM_GBS = 8000.0
+
+
+def parse_args():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=200)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    p.add_argument("--config", default="gemma2-2b")
+    p.add_argument("--batch", type=int, default=1)
+    p.add_argument("--extra-batches", default="4,16", help="batch sizes timed as extra fields ('' to skip)")
+    p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    p.add_argument("--no-dense", action="store_true", help="skip the dense BF16 comparisons")
+    p.add_argument("--layers", type=int, default=None, help="override the layer count (profiling small cases)")
+    p.add_argument("--no-lm-head", action="store_true")
+    return p.parse_args()
+
+
+# ---------------------------------------------------------------------- helpers
+
+
+def measured_peaks() -> dict:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        return json.loads(path.read_text())
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+class ClockSampler:
+    """Samples SM clock and clock-event reasons through NVML while running."""
+
+    REASONS = {
+        "gpu_idle": 0x1, "applications_clocks_setting": 0x2, "sw_power_cap": 0x4, "hw_slowdown": 0x8,
+        "sync_boost": 0x10, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40, "hw_power_brake_slowdown": 0x80,
+    }
+
+    def __init__(self, device_index: int, interval_s: float = 0.005):
+        self.samples: list = []
+        self.reasons: set = set()
+        self.max_mhz = None
+        self.interval = interval_s
+        self._stop = threading.Event()
+        self._thread = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self._nvml = pynvml
+            self._handle = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._handle, pynvml.NVML_CLOCK_SM)
+        except Exception as exc:  # noqa: BLE001 - clocks are reported as unavailable
+            self._nvml = None
+            self.error = str(exc)
+
+    def _run(self):
+        nv = self._nvml
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self._handle, nv.NVML_CLOCK_SM))
+                mask = nv.nvmlDeviceGetCurrentClocksEventReasons(self._handle)
+                for name, bit in self.REASONS.items():
+                    if mask & bit:
+                        self.reasons.add(name)
+            except Exception:  # noqa: BLE001
+                pass
+            time.sleep(self.interval)
+
+    def __enter__(self):
+        if self._nvml is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join()
+
+    def summary(self) -> dict:
+        if self._nvml is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "note": "NVML unavailable"}
+        med = statistics.median(self.samples) if self.samples else None
+        return {"sm_mhz": med, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons - {"gpu_idle"}),
+                "samples": len(self.samples), "source": "NVML, 5 ms interval, during the timed region"}
+
+
+def synthetic_bf16(torch, rows, cols, seed, device, sigma=0.02, outlier_rate=1e-4, outlier_scale=64.0, zero_rate=1e-3):
+    """Seeded N(0, sigma) BF16 weights with x`outlier_scale` outliers and +-0
+    entries, generated on the GPU (indices drawn with replacement)."""
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    w = torch.empty(rows * cols, dtype=torch.float32, device=device)
+    w.normal_(0.0, sigma, generator=g)
+    n = rows * cols
+    k = int(round(outlier_rate * n))
+    if k:
+        idx = torch.randint(0, n, (k,), device=device, generator=g)
+        w[idx] *= outlier_scale
+    z = int(round(zero_rate * n))
+    if z:
+        idx = torch.randint(0, n, (z,), device=device, generator=g)
+        sign = torch.randint(0, 2, (z,), device=device, generator=g).float()
+        w[idx] = torch.where(sign > 0, torch.tensor(-0.0, device=device), torch.tensor(0.0, device=device))
+    return w.view(rows, cols).to(torch.bfloat16)
+
+
+def dist_info():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+# ---------------------------------------------------------------------- CPU leg (oracle port)
+
+
+def cpu_baseline_sample(shapes, batch: int, steps: int, warmup: int, seed: int = 0, host_streams=None) -> dict:
+    """The reference CPU path (numpy SE12 decode + fp32 BLAS matmul, the
+    oracle port of src/lws/domain/se12/codec.py:144-186) timed on the host
+    cores over one decoder layer's seven matrices per step."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    sys.path.insert(0, str(ROOT / "tests" / "golden"))
+    from concurrent.futures import ThreadPoolExecutor
+
+    import se12_oracle as oracle
+
+    if host_streams is None:
+        import cases
+
+        host_streams = []
+        for i, (_, rows, cols, kind) in enumerate(shapes.layer_matrices()):
+            bits, r, c = cases.synthetic_weights(rows, cols, seed=seed + i)
+            host_streams.append((oracle.encode(bits, r, c), kind))
+    rng = np.random.default_rng(1)
+    xs = {kind: oracle.bits_to_float32(oracle.bf16_round(rng.normal(0, 1, size=(batch, shapes.input_width(kind))).astype(np.float32)))
+          for kind in ("hidden", "attn", "mlp")}
+    total_bytes = sum(oracle.byte_size(s) + batch * s.cols * 2 + batch * s.rows * 4 for s, _ in host_streams)
+    threads = min(len(host_streams), os.cpu_count() or 1)
+
+    def one(item):
+        s, kind = item
+        return oracle.gemv_reference_cpu(s, xs[kind])
+
+    times = []
+    with ThreadPoolExecutor(max_workers=threads) as pool:
+        for i in range(warmup + steps):
+            t0 = time.perf_counter()
+            list(pool.map(one, host_streams))
+            dt = time.perf_counter() - t0
+            if i >= warmup:
+                times.append(dt)
+    mean = sum(times) / len(times)
+    return {
+        "value": total_bytes / mean / 1e9,
+        "unit": "GB/s",
+        "cores": threads,
+        "kind": "port",
+        "sample": f"1 {shapes.name} decoder layer per step (7 matrices, {total_bytes / 1e6:.1f} MB SE12+x+y), "
+        f"numpy decode + fp32 BLAS matmul, {threads} threads (os.cpu_count()={os.cpu_count()}), {steps} steps",
+        "seconds_per_step": mean,
+        "bytes_per_step": total_bytes,
+    }
+
+
+def run_reference(args) -> None:
+    world, rank, _ = dist_info()
+    if rank != 0:
+        return
+    from se12_b200.shapes import CONFIGS
+
+    shapes = CONFIGS[args.config]
+    res = cpu_baseline_sample(shapes, args.batch, max(1, args.steps), max(0, args.warmup))
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": res["value"],
+        "unit": "GB/s",
+        "n_gpus": args.gpus,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": res["seconds_per_step"] * 1e3,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "fp32",
+        "data": "synthetic",
+        "config": {"workload": f"{shapes.name} decode-step GEMV set, sampled: one decoder layer per step", "batch": args.batch},
+        "cpu_baseline": {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "e2e": {"value": res["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------- GPU leg
+
+
+def build_stack(torch, shapes, batch, device, layers, lm_head, keep_dense):
+    from se12_b200.codec import encode_device
+
+    mats, dense = [], []
+    specs = []
+    for layer in range(layers):
+        for j, (name, rows, cols, kind) in enumerate(shapes.layer_matrices()):
+            specs.append((f"layers.{layer}.{name}", rows, cols, kind, 1000 * layer + j))
+    if lm_head:
+        name, rows, cols, kind = shapes.lm_head()
+        specs.append((name, rows, cols, kind, 999_999))
+    for name, rows, cols, kind, seed in specs:
+        w = synthetic_bf16(torch, rows, cols, seed, device)
+        m = encode_device(w)
+        mats.append((name, m, kind))
+        dense.append(w if keep_dense else None)
+        del w
+    torch.cuda.synchronize()
+    return mats, dense
+
+
+def time_stack(torch, stack, steps, warmup, device, sampler=None):
+    stack.capture()
+    for _ in range(warmup):
+        stack.replay()
+    torch.cuda.synchronize()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    ctx = sampler if sampler is not None else _Null()
+    with ctx:
+        start.record()
+        for _ in range(steps):
+            stack.replay()
+        end.record()
+        torch.cuda.synchronize()
+    return start.elapsed_time(end)  # ms over `steps`
+
+
+class _Null:
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        return False
+
+
+def run_ours(args) -> None:
+    import torch
+
+    world, rank, local = dist_info()
+    if world > 1:
+        import torch.distributed as dist
+
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=120), device_id=torch.device("cuda", local))
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+
+    from se12_b200 import _build
+    from se12_b200.device import device_status
+    from se12_b200.shapes import CONFIGS
+    from se12_b200.stack import GemvStack
+
+    if rank == 0:
+        _build.build()
+    if world > 1:
+        torch.distributed.barrier()
+    shapes = CONFIGS[args.config]
+    layers = args.layers if args.layers is not None else shapes.layers
+    batch = args.batch
+    t_setup = time.perf_counter()
+    mats, dense = build_stack(torch, shapes, batch, device, layers, not args.no_lm_head, keep_dense=not args.no_dense)
+    setup_s = time.perf_counter() - t_setup
+
+    gen = torch.Generator(device=device)
+    gen.manual_seed(1)
+
+    def inputs_for(b):
+        return {kind: torch.randn(b, shapes.input_width(kind), generator=gen, device=device).to(torch.bfloat16)
+                for kind in ("hidden", "attn", "mlp")}
+
+    def stack_for(b, use_dense=False, cublas=False):
+        xs = inputs_for(b)
+        st = GemvStack(device)
+        outs = []
+        for (name, m, kind), w in zip(mats, dense):
+            y = torch.empty(b, m.rows, dtype=torch.float32, device=device)
+            outs.append(y)
+            if use_dense:
+                st.add_dense(w, xs[kind], y)
+            else:
+                st.add(m, xs[kind], y)
+        return st, xs, outs
+
+    def step_bytes(b):
+        return sum(m.byte_size + b * m.cols * 2 + b * m.rows * 4 for _, m, _ in mats)
+
+    weights = sum(m.rows * m.cols for _, m, _ in mats)
+    se12_bytes = sum(m.byte_size for _, m, _ in mats)
+
+    # ----------------------------------------------------------- headline
+    stack, xs, outs = stack_for(batch)
+    sampler = ClockSampler(local)
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    elapsed_ms = time_stack(torch, stack, args.steps, args.warmup, device, sampler)
+    if world > 1:
+        torch.distributed.barrier()
+        t = torch.tensor([elapsed_ms], device=device, dtype=torch.float64)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        elapsed_ms = float(t.item())
+    ms_per_step = elapsed_ms / args.steps
+    bytes_per_step = step_bytes(batch)
+    value = world * bytes_per_step / (ms_per_step * 1e-3) / 1e9
+    launches = stack.launches
+
+    peaks = measured_peaks()
+    peak = float(peaks["hbm_gbs"])
+    achieved = bytes_per_step / (ms_per_step * 1e-3) / 1e9
+
+    extra = {}
+    # ----------------------------------------------------------- other batch sizes
+    for b in [int(v) for v in args.extra_batches.split(",") if v.strip()]:
+        if b == batch:
+            continue
+        st_b, _, _ = stack_for(b)
+        ms = time_stack(torch, st_b, max(3, args.steps // 4), 3, device) / max(3, args.steps // 4)
+        extra[f"batch{b}"] = {"ms_per_step": ms, "gbs": step_bytes(b) / (ms * 1e-3) / 1e9,
+                              "bf16_equiv_gbs": (2 * weights + b * sum(m.cols * 2 + m.rows * 4 for _, m, _ in mats)) / (ms * 1e-3) / 1e9,
+                              "tok_s": b / (ms * 1e-3)}
+        del st_b
+    # ----------------------------------------------------------- dense BF16 comparisons
+    dense_info = None
+    if not args.no_dense:
+        st_d, _, _ = stack_for(batch, use_dense=True)
+        ms_d = time_stack(torch, st_d, max(3, args.steps // 4), 3, device) / max(3, args.steps // 4)
+        del st_d
+        # cuBLAS through torch (F.linear), same shapes, one CUDA graph
+        xs_c = inputs_for(batch)
+        g = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream(device)
+        s.wait_stream(torch.cuda.current_stream(device))
+        outs_c = []
+        with torch.cuda.stream(s):
+            for (name, m, kind), w in zip(mats, dense):
+                outs_c.append(torch.nn.functional.linear(xs_c[kind], w))
+        s.synchronize()
+        with torch.cuda.graph(g, stream=s):
+            for (name, m, kind), w in zip(mats, dense):
+                torch.nn.functional.linear(xs_c[kind], w)
+        for _ in range(3):
+            g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n_c = max(3, args.steps // 4)
+        e0.record()
+        for _ in range(n_c):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        ms_c = e0.elapsed_time(e1) / n_c
+        dense_bytes = 2 * weights + batch * sum(m.cols * 2 + m.rows * 4 for _, m, _ in mats)
+        dense_info = {
+            "bf16_gemv_same_pipeline": {"ms_per_step": ms_d, "gbs": dense_bytes / (ms_d * 1e-3) / 1e9},
+            "cublas_bf16_F_linear": {"ms_per_step": ms_c, "gbs": dense_bytes / (ms_c * 1e-3) / 1e9},
+            "se12_speedup_vs_best_dense": min(ms_d, ms_c) / ms_per_step,
+        }
+        del g, outs_c
+    # ----------------------------------------------------------- e2e through the public API
+    e2e_stack, e2e_xs, e2e_outs = stack_for(batch)
+    e2e_stack.capture()
+    host_in = {k: torch.empty(v.shape, dtype=v.dtype, pin_memory=True).copy_(v.cpu()) for k, v in e2e_xs.items()}
+    logits = e2e_outs[-1]
+    host_out = torch.empty(logits.shape, dtype=logits.dtype, pin_memory=True)
+    h2d = sum(v.numel() * v.element_size() for v in host_in.values())
+    d2h = host_out.numel() * host_out.element_size()
+    s_e2e = e2e_stack.stream
+
+    def e2e_step():
+        with torch.cuda.stream(s_e2e):
+            for k, v in host_in.items():
+                e2e_xs[k].copy_(v, non_blocking=True)
+            e2e_stack.graph.replay()
+            host_out.copy_(logits, non_blocking=True)
+        s_e2e.synchronize()
+
+    for _ in range(args.warmup):
+        e2e_step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        e2e_step()
+    e2e_s = (time.perf_counter() - t0) / args.steps
+    e2e_value = world * bytes_per_step / e2e_s / 1e9
+
+    status = device_status()
+    if status:
+        raise RuntimeError(f"device status word is {status}: a kernel reported an error")
+
+    # ----------------------------------------------------------- CPU baseline (rank 0)
+    cpu = None
+    if rank == 0 and not args.no_cpu:
+        sys.path.insert(0, str(ROOT / "oracle"))
+        import se12_oracle as oracle
+
+        host_streams = []
+        for (name, m, kind) in mats[:7]:
+            t = m.to_tensor()
+            host_streams.append((oracle.Streams(rows=t.rows, cols=t.cols, codebook=t.codebook, sm=t.sm, ec=t.ec, esc=t.esc,
+                                                fallback_bitmap=t.fallback_bitmap, fallback_raw=t.fallback_raw), kind))
+        res = cpu_baseline_sample(shapes, batch, steps=2, warmup=1, host_streams=host_streams)
+        cpu = {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC,
+            "value": value,
+            "unit": "GB/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": ms_per_step,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic",
+            "config": {
+                "workload": f"{shapes.name} decode-step GEMV set: {layers} layers x (q,k,v,o,gate,up,down)"
+                + ("" if args.no_lm_head else " + lm_head") + f", batch {batch}",
+                "batch": batch,
+                "matrices": len(mats),
+                "weights": weights,
+                "se12_bytes": se12_bytes,
+                "bits_per_weight": 8 * se12_bytes / weights,
+                "bytes_per_step": bytes_per_step,
+                "l2": "inputs larger than L2 (every step streams all SE12 bytes once)",
+                "graph": "one CUDA graph per step, programmatic dependent launch between GEMVs",
+                "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                "setup_seconds": setup_s,
+            },
+            "bf16_equiv_gbs": world * (2 * weights + batch * sum(m.cols * 2 + m.rows * 4 for _, m, _ in mats)) / (ms_per_step * 1e-3) / 1e9,
+            "tok_s": batch / (ms_per_step * 1e-3),
+            "frac_of_measured_hbm": achieved / peak,
+            "frac_of_nominal_8000": achieved / NOMINAL_HBM_GBS,
+            "roofline": {
+                "bound": "hbm",
+                "achieved": achieved,
+                "peak": peak,
+                "unit": "GB/s",
+                "frac": achieved / peak,
+                "traffic": None,
+                "kernel": "se12::gemv_kernel<1,false> (all 183 launches of the step)",
+                "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)" if "source" not in peaks else "fallback",
+            },
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "ms_per_step": e2e_s * 1e3, "api": "se12_b200.stack.GemvStack graph replay, pinned H2D inputs, D2H logits, sync per step"},
+            "gpu_launches": launches * args.steps,
+            "clocks": sampler.summary(),
+            "other_batches": extra,
+            "dense": dense_info,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,166 @@
+/*
+ * se12.h -- C ABI of the B200-native SE12 decode + GEMV library
+ * (libse12_b200.so, built for sm_100a).
+ *
+ * SE12 stores every BF16 weight losslessly in about 12 bits: one
+ * sign|mantissa byte plus a 4-bit code into a 15-entry exponent codebook,
+ * per 16x256 tile up to 16 escaped exponents, and raw storage for tiles with
+ * more escapes. These entry points replace the reference implementation's
+ * GPU path (Acaua-Rangel/se12, package `lws`); each declaration cites the
+ * reference interface it replaces as file:line within that project.
+ *
+ * Conventions
+ *  - All pointers named *_dev or documented "device" are CUDA device
+ *    pointers; `stream` is a cudaStream_t passed as void* (NULL = default).
+ *  - Functions return an se12_status (0 = SE12_OK). On failure
+ *    se12_last_error() returns a message for the calling thread.
+ *  - No entry point allocates device memory or synchronises the stream:
+ *    every buffer (outputs, workspaces, derived tables) is caller-owned.
+ *    Launches are asynchronous on `stream`.
+ *  - BF16 values travel as their uint16 bit patterns.
+ */
+#ifndef SE12_B200_H
+#define SE12_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SE12_TILE_ROWS 16
+#define SE12_TILE_COLS 256
+#define SE12_ESCAPE_BUDGET 16
+#define SE12_CODEBOOK_SIZE 15
+#define SE12_FORMAT_VERSION 1
+#define SE12_MAX_BATCH 16
+
+typedef enum se12_status {
+  SE12_OK = 0,
+  SE12_ERR_INVALID_ARGUMENT = 1,
+  SE12_ERR_UNSUPPORTED_FORMAT = 2, /* tile shape, escape budget or format version (container.py:21-27) */
+  SE12_ERR_MISALIGNED = 3,         /* a pointer / leading dimension breaks the alignment rule */
+  SE12_ERR_WORKSPACE_TOO_SMALL = 4,
+  SE12_ERR_CUDA = 5,               /* a CUDA runtime/driver call failed */
+  SE12_ERR_UNSUPPORTED_DEVICE = 6, /* not a compute capability 10.0 (B200) device */
+  SE12_ERR_DEVICE_FAULT = 7        /* a kernel recorded an error in the device status word */
+} se12_status;
+
+/*
+ * The five SE12 streams of one matrix, already in device memory, exactly as
+ * lws.pack writes them (src/lws/adapters/safetensors/packed_store.py:70-107):
+ *   sm [T*4096] u8, ec [T*2048] u8, esc [T*16] u8,
+ *   fallback_bitmap [ceil(T/8)] u8, fallback_raw [F*4096] i16,
+ * with T = ceil(rows/16) * ceil(cols/256) tiles and F fallback tiles.
+ * escape_pos and fallback_index are derived tables (sizes from
+ * se12_escape_pos_bytes / se12_fallback_index_bytes) that
+ * se12_matrix_prepare fills.
+ * All stream pointers must be 16-byte aligned.
+ */
+typedef struct se12_streams {
+  int32_t rows, cols;
+  int32_t tile_rows, tile_cols; /* format metadata: must be 16 and 256 */
+  int32_t escape_budget;        /* must be 16 */
+  int32_t format_version;       /* must be 1 */
+  uint8_t codebook[SE12_CODEBOOK_SIZE];
+  const uint8_t* sm;
+  const uint8_t* ec;
+  const uint8_t* esc;
+  const uint8_t* fallback_bitmap;
+  const int16_t* fallback_raw;
+  uint16_t* escape_pos;   /* derived, caller-allocated: [T*16] */
+  int32_t* fallback_index; /* derived, caller-allocated: [T] */
+} se12_streams;
+
+/* Opaque host-side handle: device pointers plus TMA descriptors. Immutable
+ * after creation, so concurrent calls on different streams are safe. */
+typedef struct se12_matrix se12_matrix;
+
+/* Bytes of the two derived tables for a rows x cols matrix. */
+size_t se12_escape_pos_bytes(int rows, int cols);
+size_t se12_fallback_index_bytes(int rows, int cols);
+
+/* Validates the streams' format and builds the handle (host only, no GPU work).
+ * Replaces the upload / host precompute of Se12MatVecKernel.__init__ and
+ * _upload_se12_streams (src/lws/adapters/cuda/gemv.py:183-194, 229-264). */
+int se12_matrix_create(const se12_streams* streams, se12_matrix** out);
+
+/* Fills escape_pos and fallback_index on the device (once per matrix).
+ * Replaces the host prefix sums fallback_offsets / row_escape_offset
+ * (src/lws/adapters/cuda/gemv.py:47-77). */
+int se12_matrix_prepare(const se12_matrix* m, void* stream);
+
+void se12_matrix_destroy(se12_matrix* m);
+
+/* Workspace of se12_gemv for this matrix and batch size. The workspace must
+ * be zeroed once (se12_workspace_clear) before first use; every completed
+ * call leaves it ready for the next. One workspace per stream. */
+size_t se12_gemv_workspace_bytes(const se12_matrix* m, int batch);
+int se12_workspace_clear(void* workspace_dev, size_t bytes, void* stream);
+
+/*
+ * Fused decode + GEMV:  y[b, n] = sum_k W[n, k] * x[b, k],  fp32 accumulate,
+ * fp32 output. x: device BF16 [batch, ldx], y: device fp32 [batch, ldy].
+ * 1 <= batch <= SE12_MAX_BATCH; x 16-byte aligned, ldx % 8 == 0 and
+ * ldx >= cols rounded up to 8 (x[b, cols..ldx) may hold anything); ldy >= rows.
+ * Replaces Se12MatVecKernel.multiply (src/lws/adapters/cuda/gemv.py:196-226)
+ * and the kernel lws_gemv_se12 (src/lws/adapters/cuda/kernels/gemv_se12.cu:50-64).
+ */
+int se12_gemv(const se12_matrix* m, const uint16_t* x_dev, int batch, int ldx, float* y_dev, int ldy,
+              void* workspace_dev, size_t workspace_bytes, void* stream);
+
+/* Exact BF16 bits of the whole matrix, row-major [rows, ldo] (ldo >= cols).
+ * Replaces CudaSe12WeightDecoder.decode / decode_to_device and the kernel
+ * lws_se12_decode (src/lws/adapters/cuda/se12_decoder.py:54-76,
+ * src/lws/adapters/cuda/kernels/se12_decode.cu:12-22). */
+int se12_decode(const se12_matrix* m, uint16_t* out_dev, int ldo, void* stream);
+
+/* Exact BF16 bits of the requested rows (device int32 [nrows], any order,
+ * repeats allowed) into out[i, :] (row-major [nrows, ldo]). An out-of-range
+ * row index sets SE12_ERR_DEVICE_FAULT in the device status.
+ * Replaces CudaSe12WeightDecoder.decode_rows (src/lws/adapters/cuda/se12_decoder.py:64-70). */
+int se12_decode_rows(const se12_matrix* m, const int32_t* rows_dev, int nrows, uint16_t* out_dev, int ldo,
+                     void* stream);
+
+/* Dense BF16 GEMV baseline over a row-major BF16 matrix W [rows, ldw] with
+ * the same pipeline and output contract as se12_gemv (ldw % 8 == 0, W
+ * 16-byte aligned). Replaces RawBf16MatVecKernel.multiply and lws_gemv_raw_bf16
+ * (src/lws/adapters/cuda/gemv.py:143-172, src/lws/adapters/cuda/kernels/gemv_raw_bf16.cu:18-25). */
+size_t bf16_gemv_workspace_bytes(int rows, int cols, int batch);
+int bf16_gemv(const uint16_t* w_dev, int rows, int cols, int ldw, const uint16_t* x_dev, int batch, int ldx,
+              float* y_dev, int ldy, void* workspace_dev, size_t workspace_bytes, void* stream);
+
+/*
+ * Encoder (packer), byte-identical to the reference encode_tensor
+ * (src/lws/domain/se12/codec.py:111-141). Input: device BF16 [rows, ldw].
+ *  1. se12_encode_histogram: 256 exponent counts (device u32[256]).
+ *  2. se12_codebook_from_counts: host, the 15 most frequent exponents,
+ *     ties to the larger exponent (src/lws/domain/se12/codebook.py:41-59).
+ *  3. se12_encode_tiles: sm, ec, esc and a per-tile fallback flag (u8[T]).
+ *  4. se12_encode_bitmap: fallback bitmap, fallback_index [T] (-1 for
+ *     non-fallback tiles) and the fallback tile count (device int32).
+ *  5. se12_encode_raw: raw bits of the fallback tiles (fallback_raw [F*4096]).
+ */
+int se12_encode_histogram(const uint16_t* w_dev, int rows, int cols, int ldw, uint32_t* counts_dev, void* stream);
+int se12_codebook_from_counts(const uint32_t* counts_host, uint8_t* codebook_out);
+int se12_encode_tiles(const uint16_t* w_dev, int rows, int cols, int ldw, const uint8_t* codebook_host,
+                      uint8_t* sm_dev, uint8_t* ec_dev, uint8_t* esc_dev, uint8_t* tile_fallback_dev, void* stream);
+int se12_encode_bitmap(const uint8_t* tile_fallback_dev, int tiles, uint8_t* bitmap_dev, int32_t* fallback_index_dev,
+                       int32_t* fallback_count_dev, void* stream);
+int se12_encode_raw(const uint16_t* w_dev, int rows, int cols, int ldw, const int32_t* fallback_index_dev,
+                    int16_t* raw_dev, void* stream);
+
+/* Device status word (bit 0: a bounded wait timed out, bit 1: bad argument
+ * seen by a kernel). Reading it synchronises with the device. */
+int se12_device_status(unsigned* status_out, int clear);
+
+const char* se12_status_string(int status);
+const char* se12_last_error(void);
+int se12_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SE12_B200_H */

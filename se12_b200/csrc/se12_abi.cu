@@ -1,0 +1,382 @@
+// C-ABI layer of libse12_b200.so: argument validation, TMA descriptor
+// encoding, the fixed launch table, and error reporting. See include/se12.h.
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include <cudaTypedefs.h>
+
+#include "../../include/se12.h"
+#include "se12_internal.h"
+
+struct se12_matrix {
+  se12::MatrixView view;
+  alignas(64) CUtensorMap sm_map;
+  alignas(64) CUtensorMap ec_map;
+  int device;
+  int sm_count;
+};
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int status, const std::string& message) {
+  g_last_error = message;
+  return status;
+}
+
+int cuda_fail(cudaError_t err, const char* what) {
+  return fail(SE12_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(err));
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+int encode_2d(CUtensorMap* map, CUtensorMapDataType type, const void* base, uint64_t inner, uint64_t outer,
+              uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer) {
+  auto fn = tensor_map_encoder();
+  if (!fn) return fail(SE12_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estride[2] = {1, 1};
+  CUresult r = fn(map, type, 2, const_cast<void*>(base), dims, strides, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(SE12_ERR_CUDA, "cuTensorMapEncodeTiled failed with code " + std::to_string(int(r)));
+  return SE12_OK;
+}
+
+int current_device_info(int* device, int* sm_count) {
+  cudaError_t err = cudaGetDevice(device);
+  if (err != cudaSuccess) return cuda_fail(err, "cudaGetDevice");
+  int major = 0, minor = 0;
+  cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, *device);
+  cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, *device);
+  if (major != 10 || minor != 0)
+    return fail(SE12_ERR_UNSUPPORTED_DEVICE, "libse12_b200 is built for sm_100a; device has compute capability " +
+                                                 std::to_string(major) + "." + std::to_string(minor));
+  err = cudaDeviceGetAttribute(sm_count, cudaDevAttrMultiProcessorCount, *device);
+  if (err != cudaSuccess) return cuda_fail(err, "cudaDeviceGetAttribute");
+  return SE12_OK;
+}
+
+int tiles_of(int rows, int cols) {
+  return ((rows + SE12_TILE_ROWS - 1) / SE12_TILE_ROWS) * ((cols + SE12_TILE_COLS - 1) / SE12_TILE_COLS);
+}
+
+// ------------------------------------------------------------------ launch table
+//
+// The fixed per-shape tile table that replaces the reference's run-time
+// tuner (lws.tune, src/lws/tune.py:34-57). The kernel tile is fixed by the
+// format (16x256); what varies is the pipeline depth (stages) and the
+// number of CTAs per SM. Two CTAs per SM whenever the shared memory allows
+// it; the stream-K grid is then 2 x SM count (one wave), capped at the tile
+// count. Entries were set from ncu measurements on B200 (see the profiles).
+struct LaunchConfig {
+  int grid;
+  int stages;
+  int nblocks;
+  size_t smem;
+};
+
+constexpr size_t kSmemPerSm = 228 * 1024;
+constexpr size_t kSmemReservedPerCta = 1024;
+
+LaunchConfig choose_config(bool raw, int tiles, int batch, int sm_count) {
+  LaunchConfig c{};
+  c.nblocks = batch <= 8 ? 1 : 2;
+  int ctas_per_sm = 2;
+  int stages = 8;
+  const size_t budget = kSmemPerSm / ctas_per_sm - kSmemReservedPerCta;
+  while (stages > 2 && se12::gemv_smem_bytes(raw, stages, c.nblocks, batch) > budget) --stages;
+  c.stages = stages;
+  c.smem = se12::gemv_smem_bytes(raw, stages, c.nblocks, batch);
+  c.grid = std::max(1, std::min(tiles, ctas_per_sm * sm_count));
+  return c;
+}
+
+size_t workspace_bytes_for(int tile_rows, const LaunchConfig& c) {
+  size_t counters = (static_cast<size_t>(tile_rows) * 4 + 255) / 256 * 256;
+  size_t partials = static_cast<size_t>(c.grid) * 2 * 16 * 8 * c.nblocks * 4;
+  return counters + partials;
+}
+
+}  // namespace
+
+extern "C" {
+
+int se12_abi_version(void) { return 1; }
+
+const char* se12_last_error(void) { return g_last_error.c_str(); }
+
+const char* se12_status_string(int status) {
+  switch (status) {
+    case SE12_OK: return "ok";
+    case SE12_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case SE12_ERR_UNSUPPORTED_FORMAT: return "unsupported SE12 format";
+    case SE12_ERR_MISALIGNED: return "misaligned pointer or leading dimension";
+    case SE12_ERR_WORKSPACE_TOO_SMALL: return "workspace too small";
+    case SE12_ERR_CUDA: return "CUDA error";
+    case SE12_ERR_UNSUPPORTED_DEVICE: return "unsupported device (needs sm_100)";
+    case SE12_ERR_DEVICE_FAULT: return "a kernel reported an error";
+    default: return "unknown status";
+  }
+}
+
+size_t se12_escape_pos_bytes(int rows, int cols) {
+  return static_cast<size_t>(tiles_of(rows, cols)) * SE12_ESCAPE_BUDGET * sizeof(uint16_t);
+}
+
+size_t se12_fallback_index_bytes(int rows, int cols) {
+  return static_cast<size_t>(tiles_of(rows, cols)) * sizeof(int32_t);
+}
+
+int se12_matrix_create(const se12_streams* s, se12_matrix** out) {
+  if (!s || !out) return fail(SE12_ERR_INVALID_ARGUMENT, "null argument");
+  *out = nullptr;
+  if (s->tile_rows != SE12_TILE_ROWS || s->tile_cols != SE12_TILE_COLS || s->escape_budget != SE12_ESCAPE_BUDGET)
+    return fail(SE12_ERR_UNSUPPORTED_FORMAT, "tile shape must be 16x256 with an escape budget of 16, got " +
+                                                 std::to_string(s->tile_rows) + "x" + std::to_string(s->tile_cols) +
+                                                 " / " + std::to_string(s->escape_budget));
+  if (s->format_version != SE12_FORMAT_VERSION)
+    return fail(SE12_ERR_UNSUPPORTED_FORMAT,
+                "found format version " + std::to_string(s->format_version) + ", supported: 1");
+  if (s->rows <= 0 || s->cols <= 0) return fail(SE12_ERR_INVALID_ARGUMENT, "rows and cols must be positive");
+  if (!s->sm || !s->ec || !s->esc || !s->fallback_bitmap || !s->escape_pos || !s->fallback_index)
+    return fail(SE12_ERR_INVALID_ARGUMENT, "null stream pointer");
+  if (!aligned16(s->sm) || !aligned16(s->ec) || !aligned16(s->esc) || !aligned16(s->escape_pos) ||
+      (s->fallback_raw && !aligned16(s->fallback_raw)))
+    return fail(SE12_ERR_MISALIGNED, "SE12 streams must be 16-byte aligned");
+  int device = 0, sm_count = 0;
+  int st = current_device_info(&device, &sm_count);
+  if (st != SE12_OK) return st;
+
+  se12_matrix* m = new se12_matrix();
+  se12::MatrixView& v = m->view;
+  v.sm = s->sm;
+  v.ec = s->ec;
+  v.esc = s->esc;
+  v.bitmap = s->fallback_bitmap;
+  v.fallback_raw = reinterpret_cast<const uint16_t*>(s->fallback_raw);
+  v.escape_pos = s->escape_pos;
+  v.fallback_index = s->fallback_index;
+  v.rows = s->rows;
+  v.cols = s->cols;
+  v.tile_rows = (s->rows + SE12_TILE_ROWS - 1) / SE12_TILE_ROWS;
+  v.tile_cols = (s->cols + SE12_TILE_COLS - 1) / SE12_TILE_COLS;
+  v.tiles = v.tile_rows * v.tile_cols;
+  std::memset(v.codebook, 0, sizeof(v.codebook));
+  std::memcpy(v.codebook, s->codebook, SE12_CODEBOOK_SIZE);
+  m->device = device;
+  m->sm_count = sm_count;
+  const uint64_t rows16 = static_cast<uint64_t>(v.tiles) * SE12_TILE_ROWS;
+  st = encode_2d(&m->sm_map, CU_TENSOR_MAP_DATA_TYPE_UINT8, v.sm, 256, rows16, 256, 128, 16);
+  if (st == SE12_OK) st = encode_2d(&m->ec_map, CU_TENSOR_MAP_DATA_TYPE_UINT8, v.ec, 128, rows16, 128, 128, 16);
+  if (st != SE12_OK) {
+    delete m;
+    return st;
+  }
+  *out = m;
+  return SE12_OK;
+}
+
+int se12_matrix_prepare(const se12_matrix* m, void* stream) {
+  if (!m) return fail(SE12_ERR_INVALID_ARGUMENT, "null matrix");
+  cudaError_t err = se12::launch_prepare(m->view, const_cast<uint16_t*>(m->view.escape_pos),
+                                         const_cast<int32_t*>(m->view.fallback_index),
+                                         static_cast<cudaStream_t>(stream));
+  if (err != cudaSuccess) return cuda_fail(err, "se12_matrix_prepare launch");
+  return SE12_OK;
+}
+
+void se12_matrix_destroy(se12_matrix* m) { delete m; }
+
+size_t se12_gemv_workspace_bytes(const se12_matrix* m, int batch) {
+  if (!m || batch < 1 || batch > SE12_MAX_BATCH) return 0;
+  const LaunchConfig c = choose_config(false, m->view.tiles, batch, m->sm_count);
+  return workspace_bytes_for(m->view.tile_rows, c);
+}
+
+int se12_workspace_clear(void* workspace, size_t bytes, void* stream) {
+  if (!workspace && bytes) return fail(SE12_ERR_INVALID_ARGUMENT, "null workspace");
+  cudaError_t err = cudaMemsetAsync(workspace, 0, bytes, static_cast<cudaStream_t>(stream));
+  if (err != cudaSuccess) return cuda_fail(err, "cudaMemsetAsync");
+  return SE12_OK;
+}
+
+static int check_gemv_io(int rows, int cols, const uint16_t* x, int batch, int ldx, const float* y, int ldy) {
+  if (batch < 1 || batch > SE12_MAX_BATCH)
+    return fail(SE12_ERR_INVALID_ARGUMENT, "batch must be in 1..16, got " + std::to_string(batch));
+  if (!x || !y) return fail(SE12_ERR_INVALID_ARGUMENT, "null x or y");
+  if (ldx < (cols + 7) / 8 * 8 || ldy < rows)
+    return fail(SE12_ERR_INVALID_ARGUMENT, "ldx < cols rounded up to 8, or ldy < rows");
+  if (!aligned16(x) || (ldx % 8) != 0)
+    return fail(SE12_ERR_MISALIGNED, "x must be 16-byte aligned with ldx a multiple of 8");
+  return SE12_OK;
+}
+
+int se12_gemv(const se12_matrix* m, const uint16_t* x, int batch, int ldx, float* y, int ldy, void* workspace,
+              size_t workspace_bytes, void* stream) {
+  if (!m) return fail(SE12_ERR_INVALID_ARGUMENT, "null matrix");
+  int st = check_gemv_io(m->view.rows, m->view.cols, x, batch, ldx, y, ldy);
+  if (st != SE12_OK) return st;
+  const LaunchConfig c = choose_config(false, m->view.tiles, batch, m->sm_count);
+  const size_t need = workspace_bytes_for(m->view.tile_rows, c);
+  if (!workspace || workspace_bytes < need)
+    return fail(SE12_ERR_WORKSPACE_TOO_SMALL, "workspace needs " + std::to_string(need) + " bytes");
+  se12::GemvArgs a{};
+  a.m = m->view;
+  a.x = x;
+  a.ldx = ldx;
+  a.batch = batch;
+  a.y = y;
+  a.ldy = ldy;
+  const size_t counters = (static_cast<size_t>(m->view.tile_rows) * 4 + 255) / 256 * 256;
+  a.counters = static_cast<int*>(workspace);
+  a.partials = reinterpret_cast<float*>(static_cast<char*>(workspace) + counters);
+  a.grid = c.grid;
+  a.stages = c.stages;
+  cudaError_t err = se12::launch_gemv(false, m->sm_map, m->ec_map, a, c.nblocks, c.smem,
+                                      static_cast<cudaStream_t>(stream), true);
+  if (err != cudaSuccess) return cuda_fail(err, "se12_gemv launch");
+  return SE12_OK;
+}
+
+int se12_decode(const se12_matrix* m, uint16_t* out, int ldo, void* stream) {
+  if (!m || !out) return fail(SE12_ERR_INVALID_ARGUMENT, "null argument");
+  if (ldo < m->view.cols) return fail(SE12_ERR_INVALID_ARGUMENT, "ldo < cols");
+  cudaError_t err = se12::launch_decode(m->view, out, ldo, static_cast<cudaStream_t>(stream));
+  if (err != cudaSuccess) return cuda_fail(err, "se12_decode launch");
+  return SE12_OK;
+}
+
+int se12_decode_rows(const se12_matrix* m, const int32_t* rows, int nrows, uint16_t* out, int ldo, void* stream) {
+  if (!m || (nrows > 0 && (!rows || !out))) return fail(SE12_ERR_INVALID_ARGUMENT, "null argument");
+  if (nrows < 0 || ldo < m->view.cols) return fail(SE12_ERR_INVALID_ARGUMENT, "nrows < 0 or ldo < cols");
+  cudaError_t err = se12::launch_decode_rows(m->view, rows, nrows, out, ldo, static_cast<cudaStream_t>(stream));
+  if (err != cudaSuccess) return cuda_fail(err, "se12_decode_rows launch");
+  return SE12_OK;
+}
+
+size_t bf16_gemv_workspace_bytes(int rows, int cols, int batch) {
+  if (rows <= 0 || cols <= 0 || batch < 1 || batch > SE12_MAX_BATCH) return 0;
+  int device = 0, sm_count = 148;
+  if (cudaGetDevice(&device) == cudaSuccess) cudaDeviceGetAttribute(&sm_count, cudaDevAttrMultiProcessorCount, device);
+  const LaunchConfig c = choose_config(true, tiles_of(rows, cols), batch, sm_count);
+  return workspace_bytes_for((rows + SE12_TILE_ROWS - 1) / SE12_TILE_ROWS, c);
+}
+
+int bf16_gemv(const uint16_t* w, int rows, int cols, int ldw, const uint16_t* x, int batch, int ldx, float* y,
+              int ldy, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!w) return fail(SE12_ERR_INVALID_ARGUMENT, "null weights");
+  if (rows <= 0 || cols <= 0 || ldw < cols) return fail(SE12_ERR_INVALID_ARGUMENT, "bad weight shape");
+  if (!aligned16(w) || (ldw % 8) != 0) return fail(SE12_ERR_MISALIGNED, "W must be 16-byte aligned, ldw % 8 == 0");
+  int st = check_gemv_io(rows, cols, x, batch, ldx, y, ldy);
+  if (st != SE12_OK) return st;
+  int device = 0, sm_count = 0;
+  st = current_device_info(&device, &sm_count);
+  if (st != SE12_OK) return st;
+  const int tile_rows = (rows + SE12_TILE_ROWS - 1) / SE12_TILE_ROWS;
+  const int tile_cols = (cols + SE12_TILE_COLS - 1) / SE12_TILE_COLS;
+  const LaunchConfig c = choose_config(true, tile_rows * tile_cols, batch, sm_count);
+  const size_t need = workspace_bytes_for(tile_rows, c);
+  if (!workspace || workspace_bytes < need)
+    return fail(SE12_ERR_WORKSPACE_TOO_SMALL, "workspace needs " + std::to_string(need) + " bytes");
+  alignas(64) CUtensorMap wmap;
+  st = encode_2d(&wmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, w, static_cast<uint64_t>(cols), static_cast<uint64_t>(rows),
+                 static_cast<uint64_t>(ldw) * 2, 64, 16);
+  if (st != SE12_OK) return st;
+  se12::GemvArgs a{};
+  a.m.rows = rows;
+  a.m.cols = cols;
+  a.m.tile_rows = tile_rows;
+  a.m.tile_cols = tile_cols;
+  a.m.tiles = tile_rows * tile_cols;
+  a.x = x;
+  a.ldx = ldx;
+  a.batch = batch;
+  a.y = y;
+  a.ldy = ldy;
+  const size_t counters = (static_cast<size_t>(tile_rows) * 4 + 255) / 256 * 256;
+  a.counters = static_cast<int*>(workspace);
+  a.partials = reinterpret_cast<float*>(static_cast<char*>(workspace) + counters);
+  a.grid = c.grid;
+  a.stages = c.stages;
+  cudaError_t err = se12::launch_gemv(true, wmap, wmap, a, c.nblocks, c.smem, static_cast<cudaStream_t>(stream), true);
+  if (err != cudaSuccess) return cuda_fail(err, "bf16_gemv launch");
+  return SE12_OK;
+}
+
+int se12_encode_histogram(const uint16_t* w, int rows, int cols, int ldw, uint32_t* counts, void* stream) {
+  if (!w || !counts || rows < 0 || cols < 0 || ldw < cols) return fail(SE12_ERR_INVALID_ARGUMENT, "bad arguments");
+  cudaError_t err = se12::launch_encode_histogram(w, rows, cols, ldw, counts, static_cast<cudaStream_t>(stream));
+  if (err != cudaSuccess) return cuda_fail(err, "se12_encode_histogram");
+  return SE12_OK;
+}
+
+int se12_codebook_from_counts(const uint32_t* counts, uint8_t* codebook) {
+  if (!counts || !codebook) return fail(SE12_ERR_INVALID_ARGUMENT, "null argument");
+  int order[256];
+  for (int i = 0; i < 256; ++i) order[i] = i;
+  std::sort(order, order + 256, [&](int a, int b) {
+    if (counts[a] != counts[b]) return counts[a] > counts[b];
+    return a > b;  // equal counts: larger exponent first (stable argsort, reversed)
+  });
+  for (int i = 0; i < SE12_CODEBOOK_SIZE; ++i) codebook[i] = static_cast<uint8_t>(order[i]);
+  return SE12_OK;
+}
+
+int se12_encode_tiles(const uint16_t* w, int rows, int cols, int ldw, const uint8_t* codebook, uint8_t* sm,
+                      uint8_t* ec, uint8_t* esc, uint8_t* tile_fallback, void* stream) {
+  if (!w || !codebook || !sm || !ec || !esc || !tile_fallback || rows <= 0 || cols <= 0 || ldw < cols)
+    return fail(SE12_ERR_INVALID_ARGUMENT, "bad arguments");
+  if (!aligned16(sm) || !aligned16(ec)) return fail(SE12_ERR_MISALIGNED, "sm and ec must be 16-byte aligned");
+  cudaError_t err = se12::launch_encode_tiles(w, rows, cols, ldw, codebook, sm, ec, esc, tile_fallback,
+                                              static_cast<cudaStream_t>(stream));
+  if (err != cudaSuccess) return cuda_fail(err, "se12_encode_tiles");
+  return SE12_OK;
+}
+
+int se12_encode_bitmap(const uint8_t* tile_fallback, int tiles, uint8_t* bitmap, int32_t* fallback_index,
+                       int32_t* fallback_count, void* stream) {
+  if (!tile_fallback || !bitmap || !fallback_index || !fallback_count || tiles < 0)
+    return fail(SE12_ERR_INVALID_ARGUMENT, "bad arguments");
+  cudaError_t err = se12::launch_encode_bitmap(tile_fallback, tiles, bitmap, fallback_index, fallback_count,
+                                               static_cast<cudaStream_t>(stream));
+  if (err != cudaSuccess) return cuda_fail(err, "se12_encode_bitmap");
+  return SE12_OK;
+}
+
+int se12_encode_raw(const uint16_t* w, int rows, int cols, int ldw, const int32_t* fallback_index, int16_t* raw,
+                    void* stream) {
+  if (!w || !fallback_index || rows <= 0 || cols <= 0 || ldw < cols)
+    return fail(SE12_ERR_INVALID_ARGUMENT, "bad arguments");
+  cudaError_t err = se12::launch_encode_raw(w, rows, cols, ldw, fallback_index, reinterpret_cast<uint16_t*>(raw),
+                                            static_cast<cudaStream_t>(stream));
+  if (err != cudaSuccess) return cuda_fail(err, "se12_encode_raw");
+  return SE12_OK;
+}
+
+int se12_device_status(unsigned* status, int clear) {
+  if (!status) return fail(SE12_ERR_INVALID_ARGUMENT, "null argument");
+  cudaError_t err = se12::read_device_status(status, clear != 0);
+  if (err != cudaSuccess) return cuda_fail(err, "read device status");
+  return SE12_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,196 @@
+// Device-side building blocks shared by the SE12 kernels (sm_100a only).
+//
+// * SE12 format constants (16x256 tiles, 15-entry codebook, escape code 15,
+//   16 escape slots per tile) -- the on-disk format of lws.pack
+//   (src/lws/domain/se12/tile.py:19-24 in the reference).
+// * Thin inline-PTX wrappers: mbarrier, TMA tensor loads, 1-D bulk copies,
+//   L2 cache policies, bf16 mma.sync, programmatic dependent launch.
+// * Bounded waits: every spin on an mbarrier gives up after a wall-clock
+//   limit, records an error code in the device status word and lets the
+//   caller drain and return, so a logic error can never hang a GPU.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace se12 {
+
+constexpr int kTileRows = 16;
+constexpr int kTileCols = 256;
+constexpr int kTileSize = kTileRows * kTileCols;  // 4096 weights
+constexpr int kEscapeBudget = 16;
+constexpr int kCodebookSize = 15;
+constexpr int kEscapeCode = 15;
+constexpr uint16_t kNoEscape = 0xFFFF;
+
+// Device status word (bit flags), read back by se12_device_status().
+constexpr unsigned kStatusWaitTimeout = 1u;
+constexpr unsigned kStatusBadArgument = 2u;
+
+// A wait that has not completed after this many nanoseconds is a logic
+// error (a correct wait here completes in microseconds).
+constexpr unsigned long long kWaitLimitNs = 2000000000ull;
+
+// Device status word of the library (one translation unit: se12_lib.cu).
+__device__ unsigned int g_status;
+
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void raise_status(unsigned bits) { atomicOr(&g_status, bits); }
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ------------------------------------------------------------------ mbarrier
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_shared() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+// Waits for the phase with the given parity to complete. Returns false (and
+// raises kStatusWaitTimeout) if it did not complete within kWaitLimitNs.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long start = global_ns();
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (global_ns() - start > kWaitLimitNs) {
+      raise_status(kStatusWaitTimeout);
+      return false;
+    }
+  }
+}
+
+// ------------------------------------------------------------------ L2 policy
+
+__device__ __forceinline__ uint64_t policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+__device__ __forceinline__ uint64_t policy_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+// ------------------------------------------------------------------ TMA
+
+// 2-D tiled tensor load (no multicast) into this CTA's shared memory.
+__device__ __forceinline__ void tma_load_2d(void* dst, const void* tmap, int x, int y, uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_addr(dst)),
+      "l"(tmap), "r"(x), "r"(y), "r"(smem_addr(bar)), "l"(policy)
+      : "memory");
+}
+
+// 1-D bulk copy global -> shared (no multicast). dst, src 16-byte aligned,
+// bytes a multiple of 16.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+          smem_addr(dst)),
+      "l"(src), "r"(bytes), "r"(smem_addr(bar)), "l"(policy)
+      : "memory");
+}
+
+__device__ __forceinline__ void prefetch_tmap(const void* tmap) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
+}
+
+// ------------------------------------------------------------------ PDL
+
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// ------------------------------------------------------------------ named barriers
+
+__device__ __forceinline__ void named_barrier(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+// ------------------------------------------------------------------ mma
+
+// D = A(16x16 bf16, row) * B(16x8 bf16, col) + D, fp32 accumulate.
+__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                               uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// ------------------------------------------------------------------ SE12 decode pieces
+
+// BF16 bits from exponent byte and sign|mantissa byte:
+//   bits = ((sm & 0x80) << 8) | (exp << 7) | (sm & 0x7F)
+// (the reference's join_bit_pattern, src/lws/domain/weights.py:109-119).
+__device__ __forceinline__ uint32_t bf16_bits(uint32_t sm, uint32_t exponent) {
+  return ((sm & 0x80u) << 8) | (exponent << 7) | (sm & 0x7Fu);
+}
+
+__device__ __forceinline__ float bf16_bits_to_float(uint32_t bits) { return __uint_as_float(bits << 16); }
+
+// Pair table entry for one ec byte (two 4-bit codes: even weight in the low
+// nibble, odd weight in the high nibble). Entry layout is a BF16x2 word
+// holding only the exponent fields (bits 7..14 and 23..30). For the escape
+// code the entry instead sets every sign and mantissa bit of that half
+// (mask 0x807F); `pair_word` then yields exactly +0.0 for that weight and
+// the kernel adds the escaped weight separately.
+__device__ __forceinline__ uint32_t pair_entry(const uint8_t* codebook, uint32_t byte) {
+  const uint32_t c0 = byte & 0xFu, c1 = byte >> 4;
+  const uint32_t h0 = (c0 == kEscapeCode) ? 0x807Fu : (static_cast<uint32_t>(codebook[c0]) << 7);
+  const uint32_t h1 = (c1 == kEscapeCode) ? 0x807Fu : (static_cast<uint32_t>(codebook[c1]) << 7);
+  return h0 | (h1 << 16);
+}
+
+// Combines two sign|mantissa bytes (already placed as [s0,s0,s1,s1]) with a
+// pair table entry: keep sign+mantissa bits from `dup` where the entry has
+// no kill bits, take the exponent bits from the entry.
+//   result = (dup & M & ~entry) | (entry & ~M),  M = 0x807F807F
+__device__ __forceinline__ uint32_t pair_word(uint32_t dup, uint32_t entry) {
+  uint32_t r;
+  // lop3 truth table for f(a=dup, b=entry, c=M) = (a & c & ~b) | (b & ~c) -> 0x2E... computed:
+  //   a=0xF0 b=0xCC c=0xAA : (0xF0 & 0xAA & 0x33) | (0xCC & 0x55) = 0x20 | 0x44 = 0x64
+  asm("lop3.b32 %0, %1, %2, %3, 0x64;" : "=r"(r) : "r"(dup), "r"(entry), "r"(0x807F807Fu));
+  return r;
+}
+
+}  // namespace se12

@@ -1,0 +1,250 @@
+"""Device-resident SE12 matrices and the calls into libse12_b200.
+
+``DeviceSe12Matrix`` owns the five SE12 streams in GPU memory (torch
+tensors), the two derived tables the kernels use (escape positions,
+fallback ranks) and the native handle with its TMA descriptors. Every
+compute method launches a kernel of libse12_b200.so on the current torch
+stream; nothing here computes on the CPU.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import weakref
+
+import numpy as np
+import torch
+
+from . import _lib
+from .format import CODEBOOK_SIZE, ESCAPE_BUDGET, TILE_COLS, TILE_ROWS, TILE_SIZE, Se12Tensor, as_tensor, make_tensor, tile_grid
+
+MAX_BATCH = 16
+
+
+def stream_handle(device: torch.device | None = None) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+class _WorkspacePool:
+    """One zeroed stream-K workspace per (device, stream), grown on demand.
+
+    Calls on one stream run in order, and every completed GEMV leaves the
+    workspace's arrival counters at zero, so all matrices on a stream can
+    share one workspace.
+    """
+
+    def __init__(self):
+        self._buffers: dict = {}
+
+    def get(self, device: torch.device, stream: int, nbytes: int) -> torch.Tensor:
+        key = (device.index, stream)
+        buf = self._buffers.get(key)
+        if buf is None or buf.numel() < nbytes:
+            size = max(nbytes, 1 << 20)
+            buf = torch.empty(size, dtype=torch.uint8, device=device)
+            _lib.call("se12_workspace_clear", ctypes.c_void_p(buf.data_ptr()), buf.numel(), ctypes.c_void_p(stream))
+            self._buffers[key] = buf
+        return buf
+
+    def clear(self):
+        self._buffers.clear()
+
+
+WORKSPACES = _WorkspacePool()
+
+
+class DeviceSe12Matrix:
+    """An SE12-encoded [rows, cols] BF16 matrix resident on one GPU."""
+
+    def __init__(self, rows: int, cols: int, codebook, sm: torch.Tensor, ec: torch.Tensor, esc: torch.Tensor,
+                 fallback_bitmap: torch.Tensor, fallback_raw: torch.Tensor, fallback_index: torch.Tensor | None = None):
+        lib = _lib.load()
+        self.rows, self.cols = int(rows), int(cols)
+        self.codebook = tuple(int(v) for v in codebook)
+        if len(self.codebook) != CODEBOOK_SIZE:
+            raise ValueError("codebook must have 15 entries")
+        self.device = sm.device
+        tr, tc = tile_grid(self.rows, self.cols)
+        self.tile_rows, self.tile_cols, self.tiles = tr, tc, tr * tc
+        expect = {"sm": self.tiles * TILE_SIZE, "ec": self.tiles * TILE_SIZE // 2, "esc": self.tiles * ESCAPE_BUDGET,
+                  "fallback_bitmap": (self.tiles + 7) // 8}
+        given = {"sm": sm, "ec": ec, "esc": esc, "fallback_bitmap": fallback_bitmap}
+        for name, n in expect.items():
+            if given[name].numel() != n:
+                raise ValueError(f"stream {name} has {given[name].numel()} bytes, expected {n}")
+        self.sm, self.ec = sm.contiguous(), ec.contiguous()
+        self.esc, self.fallback_bitmap = esc.contiguous().reshape(-1), fallback_bitmap.contiguous()
+        raw = fallback_raw.contiguous().reshape(-1)
+        if raw.numel() % TILE_SIZE:
+            raise ValueError("fallback_raw must hold whole 4096-weight tiles")
+        # keep a non-empty allocation so the pointer is valid and aligned
+        self.fallback_raw = raw if raw.numel() else torch.zeros(8, dtype=torch.int16, device=self.device)
+        self.fallback_tiles = raw.numel() // TILE_SIZE
+        self.escape_pos = torch.empty(self.tiles * ESCAPE_BUDGET, dtype=torch.int16, device=self.device)
+        self.fallback_index = torch.empty(self.tiles, dtype=torch.int32, device=self.device)
+
+        s = _lib.Se12StreamsStruct()
+        s.rows, s.cols = self.rows, self.cols
+        s.tile_rows, s.tile_cols, s.escape_budget, s.format_version = TILE_ROWS, TILE_COLS, ESCAPE_BUDGET, 1
+        for i, v in enumerate(self.codebook):
+            s.codebook[i] = v
+        s.sm, s.ec, s.esc = self.sm.data_ptr(), self.ec.data_ptr(), self.esc.data_ptr()
+        s.fallback_bitmap, s.fallback_raw = self.fallback_bitmap.data_ptr(), self.fallback_raw.data_ptr()
+        s.escape_pos, s.fallback_index = self.escape_pos.data_ptr(), self.fallback_index.data_ptr()
+        handle = ctypes.c_void_p()
+        with torch.cuda.device(self.device):
+            _lib.check(lib.se12_matrix_create(ctypes.byref(s), ctypes.byref(handle)), "se12_matrix_create")
+            self._handle = handle
+            self._finalizer = weakref.finalize(self, lib.se12_matrix_destroy, handle)
+            _lib.check(lib.se12_matrix_prepare(handle, ctypes.c_void_p(stream_handle(self.device))), "se12_matrix_prepare")
+
+    # ------------------------------------------------------------------ construction
+    @classmethod
+    def from_tensor(cls, tensor, device="cuda") -> "DeviceSe12Matrix":
+        """Uploads a host Se12Tensor (this package's or the reference's)."""
+        t = as_tensor(tensor)
+        dev = torch.device(device)
+
+        def up(a, dtype):
+            return torch.from_numpy(np.ascontiguousarray(a).reshape(-1).view(dtype)).to(dev, non_blocking=False)
+
+        return cls(t.rows, t.cols, t.codebook, up(t.sm, np.uint8), up(t.ec, np.uint8), up(t.esc, np.uint8),
+                   up(t.fallback_bitmap, np.uint8), up(t.fallback_raw, np.int16))
+
+    def to_tensor(self) -> Se12Tensor:
+        """Host copy of the streams as an Se12Tensor."""
+        raw = self.fallback_raw[: self.fallback_tiles * TILE_SIZE]
+        return make_tensor(self.rows, self.cols, self.codebook, self.sm.cpu().numpy(), self.ec.cpu().numpy(),
+                           self.esc.cpu().numpy(), self.fallback_bitmap.cpu().numpy(), raw.cpu().numpy())
+
+    @property
+    def handle(self) -> ctypes.c_void_p:
+        return self._handle
+
+    @property
+    def byte_size(self) -> int:
+        """Algorithmic SE12 bytes: five streams + 15 codebook bytes."""
+        return (self.sm.numel() + self.ec.numel() + self.esc.numel() + self.fallback_bitmap.numel()
+                + self.fallback_tiles * TILE_SIZE * 2 + CODEBOOK_SIZE)
+
+    # ------------------------------------------------------------------ compute
+    def gemv(self, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        """y[B, N] = x[B, K] . W^T in fp32 (x: BF16 or fp32, [K] or [B, K])."""
+        return gemv_call(self, x, out)
+
+    def decode(self, out: torch.Tensor | None = None) -> torch.Tensor:
+        """The exact BF16 matrix [rows, cols] on the device."""
+        if out is None:
+            out = torch.empty(self.rows, self.cols, dtype=torch.bfloat16, device=self.device)
+        _check_out(out, self.cols)
+        with torch.cuda.device(self.device):
+            _lib.call("se12_decode", self._handle, ctypes.c_void_p(out.data_ptr()), out.stride(0),
+                      ctypes.c_void_p(stream_handle(self.device)))
+        return out
+
+    def decode_rows(self, rows, out: torch.Tensor | None = None) -> torch.Tensor:
+        """Exact BF16 rows [len(rows), cols] in request order."""
+        idx = torch.as_tensor(rows, dtype=torch.int32).reshape(-1).to(self.device)
+        if out is None:
+            out = torch.empty(idx.numel(), self.cols, dtype=torch.bfloat16, device=self.device)
+        _check_out(out, self.cols)
+        with torch.cuda.device(self.device):
+            _lib.call("se12_decode_rows", self._handle, ctypes.c_void_p(idx.data_ptr()), idx.numel(),
+                      ctypes.c_void_p(out.data_ptr()), out.stride(0), ctypes.c_void_p(stream_handle(self.device)))
+        return out
+
+
+def _check_out(out: torch.Tensor, cols: int):
+    if out.dtype != torch.bfloat16 or out.dim() != 2 or out.stride(1) != 1 or out.shape[1] != cols:
+        raise ValueError("out must be a BF16 [n, cols] tensor with unit column stride")
+
+
+def _aligned_bf16(x: torch.Tensor, cols: int) -> torch.Tensor:
+    """x as a [B, ldx] BF16 view with 16-byte aligned rows (ldx % 8 == 0)."""
+    if x.dim() == 1:
+        x = x.unsqueeze(0)
+    if x.stride(-1) == 1 and x.stride(0) % 8 == 0 and x.stride(0) >= (cols + 7) // 8 * 8 and x.data_ptr() % 16 == 0:
+        return x
+    ld = (cols + 7) // 8 * 8
+    buf = torch.zeros(x.shape[0], ld, dtype=torch.bfloat16, device=x.device)
+    buf[:, :cols] = x
+    return buf
+
+
+def _split_fp32(x: torch.Tensor) -> list:
+    """fp32 -> three BF16 parts whose sum is x exactly (8+8+8 significant bits)."""
+    hi = x.to(torch.bfloat16)
+    r1 = x - hi.float()
+    mid = r1.to(torch.bfloat16)
+    lo = (r1 - mid.float()).to(torch.bfloat16)
+    return [hi, mid, lo]
+
+
+def gemv_call(m: DeviceSe12Matrix, x: torch.Tensor, out: torch.Tensor | None = None, raw_weights: torch.Tensor | None = None) -> torch.Tensor:
+    """Shared GEMV driver for the fused SE12 kernel and the dense baseline."""
+    rows, cols = (m.rows, m.cols) if m is not None else raw_weights.shape
+    device = x.device
+    squeeze = x.dim() == 1
+    x2 = x.reshape(1, -1) if squeeze else x
+    if x2.shape[-1] != cols:
+        raise ValueError(f"x has {x2.shape[-1]} columns, matrix has {cols}")
+    if x2.dtype == torch.float32:
+        parts = _split_fp32(x2)
+        ys = [gemv_call(m, p, None, raw_weights) for p in parts]
+        y = (ys[0] + ys[1]) + ys[2]
+        if out is not None:
+            out.copy_(y)
+            y = out
+        return y.reshape(-1) if squeeze else y
+    if x2.dtype != torch.bfloat16:
+        raise TypeError("activations must be bfloat16 or float32")
+    batch = x2.shape[0]
+    if out is None:
+        out = torch.empty(batch, rows, dtype=torch.float32, device=device)
+    if out.dtype != torch.float32 or out.stride(-1) != 1:
+        raise ValueError("out must be fp32 with unit column stride")
+    out2 = out.reshape(1, -1) if out.dim() == 1 else out
+    stream = stream_handle(device)
+    with torch.cuda.device(device):
+        for b0 in range(0, batch, MAX_BATCH):
+            xb = _aligned_bf16(x2[b0 : b0 + MAX_BATCH], cols)
+            yb = out2[b0 : b0 + MAX_BATCH]
+            nb = xb.shape[0]
+            if m is not None:
+                need = _lib.load().se12_gemv_workspace_bytes(m.handle, MAX_BATCH)
+                ws = WORKSPACES.get(device, stream, need)
+                _lib.call("se12_gemv", m.handle, ctypes.c_void_p(xb.data_ptr()), nb, xb.stride(0),
+                          ctypes.c_void_p(yb.data_ptr()), yb.stride(0), ctypes.c_void_p(ws.data_ptr()), ws.numel(),
+                          ctypes.c_void_p(stream))
+            else:
+                w = raw_weights
+                need = _lib.load().bf16_gemv_workspace_bytes(rows, cols, MAX_BATCH)
+                ws = WORKSPACES.get(device, stream, need)
+                _lib.call("bf16_gemv", ctypes.c_void_p(w.data_ptr()), rows, cols, w.stride(0),
+                          ctypes.c_void_p(xb.data_ptr()), nb, xb.stride(0), ctypes.c_void_p(yb.data_ptr()), yb.stride(0),
+                          ctypes.c_void_p(ws.data_ptr()), ws.numel(), ctypes.c_void_p(stream))
+    return out.reshape(-1) if squeeze else out
+
+
+def bf16_gemv(weights: torch.Tensor, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Dense BF16 GEMV baseline with the same pipeline as the fused kernel."""
+    if weights.dtype != torch.bfloat16 or weights.dim() != 2 or weights.stride(1) != 1:
+        raise ValueError("weights must be a BF16 [rows, cols] matrix with unit column stride")
+    w = weights
+    if w.stride(0) % 8 or w.data_ptr() % 16:
+        ld = (w.shape[1] + 7) // 8 * 8
+        buf = torch.zeros(w.shape[0], ld, dtype=torch.bfloat16, device=w.device)
+        buf[:, : w.shape[1]] = w
+        w = buf[:, : weights.shape[1]]
+    return gemv_call(None, x, out, raw_weights=w)
+
+
+def device_status(clear: bool = True) -> int:
+    """Device status word of the library (non-zero after a kernel-side error)."""
+    v = ctypes.c_uint(0)
+    _lib.call("se12_device_status", ctypes.byref(v), 1 if clear else 0)
+    return v.value

@@ -1,0 +1,95 @@
+"""The C ABI without a GPU: the library builds, loads, exports every entry
+point include/se12.h declares, and its host-only functions behave."""
+
+from __future__ import annotations
+
+import ctypes
+import pathlib
+import re
+
+import numpy as np
+import pytest
+
+import se12_oracle as oracle
+
+ROOT = pathlib.Path(__file__).resolve().parent.parent
+HEADER = ROOT / "include" / "se12.h"
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from se12_b200 import _build, _lib
+
+    _build.build()
+    return _lib.load()
+
+
+def declared_functions() -> list:
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?[\w]+\s*\**\s+\**((?:se12|bf16)_\w+)\s*\(", text, flags=re.M)))
+
+
+def test_header_declares_the_expected_surface():
+    names = declared_functions()
+    for required in ("se12_matrix_create", "se12_matrix_prepare", "se12_gemv", "se12_decode", "se12_decode_rows",
+                     "bf16_gemv", "se12_encode_tiles", "se12_status_string", "se12_last_error"):
+        assert required in names
+    assert len(names) >= 20
+
+
+def test_library_exports_every_declared_function(lib):
+    missing = [name for name in declared_functions() if not hasattr(lib, name)]
+    assert not missing, f"declared in include/se12.h but not exported: {missing}"
+
+
+def test_python_binding_covers_every_declared_function():
+    from se12_b200 import _lib
+
+    assert set(declared_functions()) == set(_lib.SIGNATURES)
+
+
+def test_status_strings_and_version(lib):
+    assert lib.se12_abi_version() == 1
+    assert lib.se12_status_string(0) == b"ok"
+    assert b"workspace" in lib.se12_status_string(4)
+    assert lib.se12_status_string(99) == b"unknown status"
+
+
+def test_derived_table_sizes(lib):
+    # 33 x 300 -> 3 x 2 tiles
+    assert lib.se12_escape_pos_bytes(33, 300) == 6 * 16 * 2
+    assert lib.se12_fallback_index_bytes(33, 300) == 6 * 4
+    assert lib.se12_escape_pos_bytes(256000, 2304) == 16000 * 9 * 32
+
+
+@pytest.mark.parametrize("seed", range(6))
+def test_codebook_from_counts_matches_reference_rule(lib, seed):
+    rng = np.random.default_rng(seed)
+    if seed < 4:  # skewed, like real weights: a few dominant binades
+        exps = np.clip(np.round(rng.normal(120, 3 + seed, size=5000)), 0, 255).astype(np.uint8)
+    else:  # many exact ties: the tie rule decides the codebook
+        exps = np.repeat(np.arange(40, dtype=np.uint8), 7)
+    counts = np.bincount(exps, minlength=256).astype(np.uint32)
+    out = (ctypes.c_uint8 * 15)()
+    assert lib.se12_codebook_from_counts(ctypes.c_void_p(counts.ctypes.data), out) == 0
+    assert tuple(out) == oracle.build_codebook(exps)
+
+
+def test_create_rejects_unknown_format_before_touching_a_device(lib):
+    from se12_b200 import _lib
+
+    s = _lib.Se12StreamsStruct()
+    s.rows, s.cols, s.tile_rows, s.tile_cols, s.escape_budget, s.format_version = 16, 256, 16, 256, 16, 99
+    handle = ctypes.c_void_p()
+    status = lib.se12_matrix_create(ctypes.byref(s), ctypes.byref(handle))
+    assert status == 2  # SE12_ERR_UNSUPPORTED_FORMAT
+    assert b"99" in lib.se12_last_error()
+    s.format_version, s.tile_cols = 1, 128
+    assert lib.se12_matrix_create(ctypes.byref(s), ctypes.byref(handle)) == 2
+
+
+def test_null_and_range_arguments_are_rejected(lib):
+    assert lib.se12_gemv(None, None, 1, 256, None, 16, None, 0, None) == 1
+    assert lib.se12_matrix_create(None, None) == 1
+    assert lib.bf16_gemv(None, 16, 256, 256, None, 1, 256, None, 16, None, 0, None) == 1
