@@ -56,7 +56,7 @@ typedef enum se12_status {
  * escape_pos and fallback_index are derived tables (sizes from
  * se12_escape_pos_bytes / se12_fallback_index_bytes) that
  * se12_matrix_prepare fills.
- * All stream pointers must be 16-byte aligned.
+ * All stream and derived-table pointers must be 16-byte aligned.
  */
 typedef struct se12_streams {
   int32_t rows, cols;
@@ -70,7 +70,7 @@ typedef struct se12_streams {
   const uint8_t* fallback_bitmap;
   const int16_t* fallback_raw;
   uint16_t* escape_pos;   /* derived, caller-allocated: [T*16] */
-  int32_t* fallback_index; /* derived, caller-allocated: [T] */
+  int32_t* fallback_index; /* derived, caller-allocated: [T rounded up to a multiple of 4] */
 } se12_streams;
 
 /* Opaque host-side handle: device pointers plus TMA descriptors. Immutable
@@ -93,9 +93,11 @@ int se12_matrix_prepare(const se12_matrix* m, void* stream);
 
 void se12_matrix_destroy(se12_matrix* m);
 
-/* Workspace of se12_gemv for this matrix and batch size. The workspace must
- * be zeroed once (se12_workspace_clear) before first use; every completed
- * call leaves it ready for the next. One workspace per stream. */
+/* Workspace of se12_gemv for this matrix (any batch size). The workspace
+ * must be zeroed once (se12_workspace_clear) before first use; every
+ * completed call leaves it ready for the next. Its layout does not depend on
+ * the matrix, so one workspace (sized for the largest matrix) serves every
+ * call on a stream; calls that may overlap on the GPU need separate ones. */
 size_t se12_gemv_workspace_bytes(const se12_matrix* m, int batch);
 int se12_workspace_clear(void* workspace_dev, size_t bytes, void* stream);
 

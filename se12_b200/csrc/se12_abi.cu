@@ -47,18 +47,48 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   return fn;
 }
 
-int encode_2d(CUtensorMap* map, CUtensorMapDataType type, const void* base, uint64_t inner, uint64_t outer,
-              uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer) {
+int encode_map(CUtensorMap* map, CUtensorMapDataType type, int rank, const void* base, const cuuint64_t* dims,
+               const cuuint64_t* strides, const cuuint32_t* box) {
   auto fn = tensor_map_encoder();
   if (!fn) return fail(SE12_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
-  cuuint64_t dims[2] = {inner, outer};
-  cuuint64_t strides[1] = {row_bytes};
-  cuuint32_t box[2] = {box_inner, box_outer};
-  cuuint32_t estride[2] = {1, 1};
-  CUresult r = fn(map, type, 2, const_cast<void*>(base), dims, strides, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+  cuuint32_t estride[3] = {1, 1, 1};
+  CUresult r = fn(map, type, rank, const_cast<void*>(base), dims, strides, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(SE12_ERR_CUDA, "cuTensorMapEncodeTiled failed with code " + std::to_string(int(r)));
   return SE12_OK;
+}
+
+// sm stream as [16T rows][2 halves][128 B] (one box = a stage's 4 tiles, both
+// halves); ec stream as [16T rows][128 B].
+int encode_se12_maps(se12_matrix* m) {
+  const cuuint64_t rows16 = static_cast<cuuint64_t>(m->view.tiles) * SE12_TILE_ROWS;
+  const cuuint32_t box_rows = se12::kStageTiles * SE12_TILE_ROWS;
+  const cuuint64_t sm_dims[3] = {128, 2, rows16};
+  const cuuint64_t sm_strides[2] = {128, 256};
+  const cuuint32_t sm_box[3] = {128, 2, box_rows};
+  int st = encode_map(&m->sm_map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, m->view.sm, sm_dims, sm_strides, sm_box);
+  if (st != SE12_OK) return st;
+  const cuuint64_t ec_dims[2] = {128, rows16};
+  const cuuint64_t ec_strides[1] = {128};
+  const cuuint32_t ec_box[2] = {128, box_rows};
+  return encode_map(&m->ec_map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, m->view.ec, ec_dims, ec_strides, ec_box);
+}
+
+// Dense W [rows, ldw]: as [rows][cols/64][64] with one box per 16x256 tile
+// when cols % 64 == 0, else [rows][cols] with four 16x64 boxes per tile.
+int encode_raw_map(CUtensorMap* map, const uint16_t* w, int rows, int cols, int ldw, int* raw_3d) {
+  if (cols % 64 == 0) {
+    const cuuint64_t dims[3] = {64, static_cast<cuuint64_t>(cols / 64), static_cast<cuuint64_t>(rows)};
+    const cuuint64_t strides[2] = {128, static_cast<cuuint64_t>(ldw) * 2};
+    const cuuint32_t box[3] = {64, 4, 16};
+    *raw_3d = 1;
+    return encode_map(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, w, dims, strides, box);
+  }
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(ldw) * 2};
+  const cuuint32_t box[2] = {64, 16};
+  *raw_3d = 0;
+  return encode_map(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, w, dims, strides, box);
 }
 
 int current_device_info(int* device, int* sm_count) {
@@ -81,39 +111,51 @@ int tiles_of(int rows, int cols) {
 
 // ------------------------------------------------------------------ launch table
 //
-// The fixed per-shape tile table that replaces the reference's run-time
-// tuner (lws.tune, src/lws/tune.py:34-57). The kernel tile is fixed by the
-// format (16x256); what varies is the pipeline depth (stages) and the
-// number of CTAs per SM. Two CTAs per SM whenever the shared memory allows
-// it; the stream-K grid is then 2 x SM count (one wave), capped at the tile
-// count. Entries were set from ncu measurements on B200 (see the profiles).
+// The fixed launch table that replaces the reference's run-time tuner
+// (lws.tune, src/lws/tune.py:34-57). The tile is fixed by the format (16x256)
+// and a stage by the kernel (4 tiles); what varies is the pipeline depth.
+// One CTA per SM (stream-K over stages). The depth is the largest of 4..2
+// stages that keeps shared memory under kCoResidentSmem, so that the next
+// GEMV in the stream can be resident beside this one and prefetch its
+// weights (programmatic dependent launch); large batches (x slices of 16
+// rows) exceed that and run alone with 2 stages.
 struct LaunchConfig {
   int grid;
   int stages;
   int nblocks;
+  int x_resident;
   size_t smem;
 };
 
-constexpr size_t kSmemPerSm = 228 * 1024;
-constexpr size_t kSmemReservedPerCta = 1024;
-
-LaunchConfig choose_config(bool raw, int tiles, int batch, int sm_count) {
+LaunchConfig choose_config(bool raw, int tiles, int cols, int batch, int sm_count) {
   LaunchConfig c{};
   c.nblocks = batch <= 8 ? 1 : 2;
-  int ctas_per_sm = 2;
-  int stages = 8;
-  const size_t budget = kSmemPerSm / ctas_per_sm - kSmemReservedPerCta;
-  while (stages > 2 && se12::gemv_smem_bytes(raw, stages, c.nblocks, batch) > budget) --stages;
-  c.stages = stages;
-  c.smem = se12::gemv_smem_bytes(raw, stages, c.nblocks, batch);
-  c.grid = std::max(1, std::min(tiles, ctas_per_sm * sm_count));
+  // candidates in order of preference: (x resident?, stages)
+  static const int kCandidates[][2] = {{1, 4}, {1, 3}, {0, 4}, {0, 3}, {1, 2}, {0, 2}};
+  c.x_resident = 0;
+  c.stages = 2;
+  for (const auto& cand : kCandidates) {
+    if (se12::gemv_smem_bytes(raw, cand[0] != 0, cand[1], batch, cols) <= se12::kCoResidentSmem) {
+      c.x_resident = cand[0];
+      c.stages = cand[1];
+      break;
+    }
+  }
+  c.smem = se12::gemv_smem_bytes(raw, c.x_resident != 0, c.stages, batch, cols);
+  const int units = (tiles + se12::kStageTiles - 1) / se12::kStageTiles;
+  c.grid = std::max(1, std::min(units, sm_count));
   return c;
 }
 
-size_t workspace_bytes_for(int tile_rows, const LaunchConfig& c) {
-  size_t counters = (static_cast<size_t>(tile_rows) * 4 + 255) / 256 * 256;
-  size_t partials = static_cast<size_t>(c.grid) * 2 * 16 * 8 * c.nblocks * 4;
-  return counters + partials;
+// Workspace layout, identical for every matrix so that all calls on one
+// stream can share one workspace: [partials][counters]. The partials region
+// has a fixed size (the largest grid and batch: 2 CTAs per SM, 2 slots of
+// 16 rows x 16 batch columns each), the arrival counters (one int per tile
+// row, zero between calls) follow it.
+size_t partials_region_bytes(int sm_count) { return static_cast<size_t>(2 * sm_count) * 2 * 16 * 16 * 4; }
+
+size_t workspace_bytes_for(int tile_rows, int sm_count) {
+  return partials_region_bytes(sm_count) + (static_cast<size_t>(tile_rows) * 4 + 255) / 256 * 256;
 }
 
 }  // namespace
@@ -143,7 +185,7 @@ size_t se12_escape_pos_bytes(int rows, int cols) {
 }
 
 size_t se12_fallback_index_bytes(int rows, int cols) {
-  return static_cast<size_t>(tiles_of(rows, cols)) * sizeof(int32_t);
+  return static_cast<size_t>((tiles_of(rows, cols) + 3) & ~3) * sizeof(int32_t);
 }
 
 int se12_matrix_create(const se12_streams* s, se12_matrix** out) {
@@ -160,7 +202,7 @@ int se12_matrix_create(const se12_streams* s, se12_matrix** out) {
   if (!s->sm || !s->ec || !s->esc || !s->fallback_bitmap || !s->escape_pos || !s->fallback_index)
     return fail(SE12_ERR_INVALID_ARGUMENT, "null stream pointer");
   if (!aligned16(s->sm) || !aligned16(s->ec) || !aligned16(s->esc) || !aligned16(s->escape_pos) ||
-      (s->fallback_raw && !aligned16(s->fallback_raw)))
+      !aligned16(s->fallback_index) || (s->fallback_raw && !aligned16(s->fallback_raw)))
     return fail(SE12_ERR_MISALIGNED, "SE12 streams must be 16-byte aligned");
   int device = 0, sm_count = 0;
   int st = current_device_info(&device, &sm_count);
@@ -184,9 +226,7 @@ int se12_matrix_create(const se12_streams* s, se12_matrix** out) {
   std::memcpy(v.codebook, s->codebook, SE12_CODEBOOK_SIZE);
   m->device = device;
   m->sm_count = sm_count;
-  const uint64_t rows16 = static_cast<uint64_t>(v.tiles) * SE12_TILE_ROWS;
-  st = encode_2d(&m->sm_map, CU_TENSOR_MAP_DATA_TYPE_UINT8, v.sm, 256, rows16, 256, 128, 16);
-  if (st == SE12_OK) st = encode_2d(&m->ec_map, CU_TENSOR_MAP_DATA_TYPE_UINT8, v.ec, 128, rows16, 128, 128, 16);
+  st = encode_se12_maps(m);
   if (st != SE12_OK) {
     delete m;
     return st;
@@ -208,8 +248,7 @@ void se12_matrix_destroy(se12_matrix* m) { delete m; }
 
 size_t se12_gemv_workspace_bytes(const se12_matrix* m, int batch) {
   if (!m || batch < 1 || batch > SE12_MAX_BATCH) return 0;
-  const LaunchConfig c = choose_config(false, m->view.tiles, batch, m->sm_count);
-  return workspace_bytes_for(m->view.tile_rows, c);
+  return workspace_bytes_for(m->view.tile_rows, m->sm_count);
 }
 
 int se12_workspace_clear(void* workspace, size_t bytes, void* stream) {
@@ -235,8 +274,8 @@ int se12_gemv(const se12_matrix* m, const uint16_t* x, int batch, int ldx, float
   if (!m) return fail(SE12_ERR_INVALID_ARGUMENT, "null matrix");
   int st = check_gemv_io(m->view.rows, m->view.cols, x, batch, ldx, y, ldy);
   if (st != SE12_OK) return st;
-  const LaunchConfig c = choose_config(false, m->view.tiles, batch, m->sm_count);
-  const size_t need = workspace_bytes_for(m->view.tile_rows, c);
+  const LaunchConfig c = choose_config(false, m->view.tiles, m->view.cols, batch, m->sm_count);
+  const size_t need = workspace_bytes_for(m->view.tile_rows, m->sm_count);
   if (!workspace || workspace_bytes < need)
     return fail(SE12_ERR_WORKSPACE_TOO_SMALL, "workspace needs " + std::to_string(need) + " bytes");
   se12::GemvArgs a{};
@@ -246,11 +285,11 @@ int se12_gemv(const se12_matrix* m, const uint16_t* x, int batch, int ldx, float
   a.batch = batch;
   a.y = y;
   a.ldy = ldy;
-  const size_t counters = (static_cast<size_t>(m->view.tile_rows) * 4 + 255) / 256 * 256;
-  a.counters = static_cast<int*>(workspace);
-  a.partials = reinterpret_cast<float*>(static_cast<char*>(workspace) + counters);
+  a.partials = static_cast<float*>(workspace);
+  a.counters = reinterpret_cast<int*>(static_cast<char*>(workspace) + partials_region_bytes(m->sm_count));
   a.grid = c.grid;
   a.stages = c.stages;
+  a.x_resident = c.x_resident;
   cudaError_t err = se12::launch_gemv(false, m->sm_map, m->ec_map, a, c.nblocks, c.smem,
                                       static_cast<cudaStream_t>(stream), true);
   if (err != cudaSuccess) return cuda_fail(err, "se12_gemv launch");
@@ -277,8 +316,7 @@ size_t bf16_gemv_workspace_bytes(int rows, int cols, int batch) {
   if (rows <= 0 || cols <= 0 || batch < 1 || batch > SE12_MAX_BATCH) return 0;
   int device = 0, sm_count = 148;
   if (cudaGetDevice(&device) == cudaSuccess) cudaDeviceGetAttribute(&sm_count, cudaDevAttrMultiProcessorCount, device);
-  const LaunchConfig c = choose_config(true, tiles_of(rows, cols), batch, sm_count);
-  return workspace_bytes_for((rows + SE12_TILE_ROWS - 1) / SE12_TILE_ROWS, c);
+  return workspace_bytes_for((rows + SE12_TILE_ROWS - 1) / SE12_TILE_ROWS, sm_count);
 }
 
 int bf16_gemv(const uint16_t* w, int rows, int cols, int ldw, const uint16_t* x, int batch, int ldx, float* y,
@@ -293,15 +331,16 @@ int bf16_gemv(const uint16_t* w, int rows, int cols, int ldw, const uint16_t* x,
   if (st != SE12_OK) return st;
   const int tile_rows = (rows + SE12_TILE_ROWS - 1) / SE12_TILE_ROWS;
   const int tile_cols = (cols + SE12_TILE_COLS - 1) / SE12_TILE_COLS;
-  const LaunchConfig c = choose_config(true, tile_rows * tile_cols, batch, sm_count);
-  const size_t need = workspace_bytes_for(tile_rows, c);
+  const LaunchConfig c = choose_config(true, tile_rows * tile_cols, cols, batch, sm_count);
+  const size_t need = workspace_bytes_for(tile_rows, sm_count);
   if (!workspace || workspace_bytes < need)
     return fail(SE12_ERR_WORKSPACE_TOO_SMALL, "workspace needs " + std::to_string(need) + " bytes");
   alignas(64) CUtensorMap wmap;
-  st = encode_2d(&wmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, w, static_cast<uint64_t>(cols), static_cast<uint64_t>(rows),
-                 static_cast<uint64_t>(ldw) * 2, 64, 16);
+  int raw_3d = 0;
+  st = encode_raw_map(&wmap, w, rows, cols, ldw, &raw_3d);
   if (st != SE12_OK) return st;
   se12::GemvArgs a{};
+  a.raw_3d = raw_3d;
   a.m.rows = rows;
   a.m.cols = cols;
   a.m.tile_rows = tile_rows;
@@ -312,11 +351,11 @@ int bf16_gemv(const uint16_t* w, int rows, int cols, int ldw, const uint16_t* x,
   a.batch = batch;
   a.y = y;
   a.ldy = ldy;
-  const size_t counters = (static_cast<size_t>(tile_rows) * 4 + 255) / 256 * 256;
-  a.counters = static_cast<int*>(workspace);
-  a.partials = reinterpret_cast<float*>(static_cast<char*>(workspace) + counters);
+  a.partials = static_cast<float*>(workspace);
+  a.counters = reinterpret_cast<int*>(static_cast<char*>(workspace) + partials_region_bytes(sm_count));
   a.grid = c.grid;
   a.stages = c.stages;
+  a.x_resident = c.x_resident;
   cudaError_t err = se12::launch_gemv(true, wmap, wmap, a, c.nblocks, c.smem, static_cast<cudaStream_t>(stream), true);
   if (err != cudaSuccess) return cuda_fail(err, "bf16_gemv launch");
   return SE12_OK;

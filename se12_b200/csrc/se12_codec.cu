@@ -80,8 +80,8 @@ __global__ void prepare_escape_positions(const uint8_t* __restrict__ ec, const u
 // Exclusive scan of the fallback bitmap: rank among fallback tiles, -1 for
 // the others (the reference's fallback_offsets, gemv.py:47-53, except that
 // non-fallback tiles get -1 instead of a don't-care value).
-__global__ void scan_fallback(const uint8_t* __restrict__ bitmap, int tiles, int32_t* __restrict__ fallback_index,
-                              int32_t* __restrict__ fallback_count) {
+__global__ void scan_fallback(const uint8_t* __restrict__ bitmap, int tiles, int padded_tiles,
+                              int32_t* __restrict__ fallback_index, int32_t* __restrict__ fallback_count) {
   __shared__ int warp_sums[32];
   __shared__ int carry;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -113,6 +113,7 @@ __global__ void scan_fallback(const uint8_t* __restrict__ bitmap, int tiles, int
     __syncthreads();
   }
   if (tid == 0 && fallback_count) *fallback_count = carry;
+  for (int tile = tiles + tid; tile < padded_tiles; tile += blockDim.x) fallback_index[tile] = -1;
 }
 
 cudaError_t launch_prepare(const MatrixView& m, uint16_t* escape_pos, int32_t* fallback_index, cudaStream_t stream) {
@@ -121,7 +122,8 @@ cudaError_t launch_prepare(const MatrixView& m, uint16_t* escape_pos, int32_t* f
   prepare_escape_positions<<<(m.tiles + warps - 1) / warps, warps * 32, 0, stream>>>(m.ec, m.bitmap, m.tiles, escape_pos);
   cudaError_t err = cudaGetLastError();
   if (err != cudaSuccess) return err;
-  scan_fallback<<<1, 1024, 0, stream>>>(m.bitmap, m.tiles, fallback_index, nullptr);
+  // padded to a multiple of 4 tiles: the GEMV copies whole 16-byte groups
+  scan_fallback<<<1, 1024, 0, stream>>>(m.bitmap, m.tiles, (m.tiles + 3) & ~3, fallback_index, nullptr);
   return cudaGetLastError();
 }
 
@@ -456,7 +458,7 @@ cudaError_t launch_encode_bitmap(const uint8_t* tile_fallback, int tiles, uint8_
   pack_bitmap_kernel<<<(bytes + 255) / 256, 256, 0, stream>>>(tile_fallback, tiles, bitmap);
   cudaError_t err = cudaGetLastError();
   if (err != cudaSuccess) return err;
-  scan_fallback<<<1, 1024, 0, stream>>>(bitmap, tiles, fallback_index, fallback_count);
+  scan_fallback<<<1, 1024, 0, stream>>>(bitmap, tiles, tiles, fallback_index, fallback_count);
   return cudaGetLastError();
 }
 

@@ -31,6 +31,10 @@ constexpr unsigned kStatusBadArgument = 2u;
 // error (a correct wait here completes in microseconds).
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;
 
+// try_wait may suspend the thread up to this long (ns) instead of spinning;
+// it returns as soon as the phase completes.
+constexpr uint32_t kSuspendHintNs = 1000000u;
+
 // Device status word of the library (one translation unit: se12_lib.cu).
 __device__ unsigned int g_status;
 
@@ -73,10 +77,10 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t done;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(done)
-      : "r"(smem_addr(bar)), "r"(parity)
+      : "r"(smem_addr(bar)), "r"(parity), "r"(kSuspendHintNs)
       : "memory");
   return done != 0;
 }
@@ -93,6 +97,33 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
       return false;
     }
   }
+}
+
+// Same, for a warp with nothing else to do: between polls it sleeps with
+// exponential backoff (up to ~256 ns) instead of competing for issue slots
+// with the warps that share its scheduler.
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long start = global_ns();
+  unsigned ns = 32;
+  while (true) {
+    __nanosleep(ns);
+    if (mbar_try_wait(bar, parity)) return true;
+    if (ns < 256) ns <<= 1;
+    if (global_ns() - start > kWaitLimitNs) {
+      raise_status(kStatusWaitTimeout);
+      return false;
+    }
+  }
+}
+
+// Atomic add on a shared-memory counter with acquire-release semantics at
+// CTA scope: orders this thread's earlier shared-memory writes before the
+// add, and the later reads after it.
+__device__ __forceinline__ int atomic_add_acq_rel_cta(int* counter, int v) {
+  int old;
+  asm volatile("atom.acq_rel.cta.shared::cta.add.u32 %0, [%1], %2;" : "=r"(old) : "r"(smem_addr(counter)), "r"(v) : "memory");
+  return old;
 }
 
 // ------------------------------------------------------------------ L2 policy
@@ -128,6 +159,37 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
           smem_addr(dst)),
       "l"(src), "r"(bytes), "r"(smem_addr(bar)), "l"(policy)
       : "memory");
+}
+
+// 3-D tiled tensor load (no multicast).
+__device__ __forceinline__ void tma_load_3d(void* dst, const void* tmap, int x, int y, int z, uint64_t* bar,
+                                            uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(smem_addr(dst)),
+      "l"(tmap), "r"(x), "r"(y), "r"(z), "r"(smem_addr(bar)), "l"(policy)
+      : "memory");
+}
+
+// Per-thread 16-byte asynchronous copy global -> shared through L2 only.
+__device__ __forceinline__ void cp_async_16_cg(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+
+// Same, also caching in L1 (data re-read by this SM).
+__device__ __forceinline__ void cp_async_16_ca(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+
+// The mbarrier's pending count is raised by one now and lowered when every
+// cp.async this thread issued so far has landed in shared memory.
+__device__ __forceinline__ void cp_async_mbar_arrive(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.shared::cta.b64 [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+// Fire-and-forget prefetch of the cache line holding p into L2.
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
 }
 
 __device__ __forceinline__ void prefetch_tmap(const void* tmap) {

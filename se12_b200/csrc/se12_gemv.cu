@@ -5,26 +5,33 @@
 // and re-reads the weights once per batch element. Design here:
 //
 // * Stream-K over the tile sequence. The matrix is the linear sequence of
-//   its T tiles in memory order (tile row major, 16x256 weights each). CTA c
-//   owns the contiguous range [T*c/G, T*(c+1)/G). Rows of tiles entirely
-//   inside a range are written directly; a tile row split between CTAs is
-//   finished by the last contributor, which sums the partials in CTA order
-//   (deterministic, no floating-point atomics).
-// * Warp-specialised pipeline, one tile per stage: a producer warp moves the
-//   tile's sm and ec bytes with 2-D TMA loads (128-byte swizzle), the escape
-//   slots / escape positions / x slice with 1-D bulk copies, all completing
-//   on one mbarrier; four consumer warps each take a 64-column quarter.
-//   Fallback tiles are fetched raw (8 KB) instead of sm+ec.
+//   its T tiles in memory order (tile-row major, 16x256 weights each), cut
+//   into stages of 4 consecutive tiles. CTA c (one per SM) owns a contiguous
+//   run of stages. Tile rows entirely inside a CTA's run are written
+//   directly; a tile row split between CTAs is finished by its last
+//   contributor, which sums the partials in CTA order (deterministic, no
+//   floating-point atomics).
+// * Warp-specialised pipeline. A producer warp moves each stage's sm bytes
+//   with one 3-D TMA load ([64 rows][2 halves][128 B]) and its ec bytes with
+//   one 2-D TMA load ([64 rows][128 B]), both 128-byte swizzled; its lanes
+//   copy the escape slots, escape positions and x slices with cp.async. All
+//   of it completes on one mbarrier per stage. Eight consumer warps: warp w
+//   takes half w % 2 (128 columns) of tile w / 2 of every stage.
 // * Decode in registers straight into mma.sync fragments: per pair of
 //   weights one byte-permute (sign|mantissa), one lookup of the ec byte in a
-//   lane-replicated 256-entry pair table (conflict-free), one lop3. Escaped
-//   weights decode to +0 in the fragment and are added exactly afterwards
-//   (w_escaped * x in fp32) from the per-tile escape position list.
+//   lane-replicated 256-entry pair table, one lop3. Escaped weights decode to
+//   +0 in the fragment and are added exactly afterwards (w * x in fp32) from
+//   the per-tile escape position list. Fallback tiles are read raw.
 // * bf16 m16n8k16 tensor-core MMA with fp32 accumulation; batch padded to
-//   multiples of 8. The MMA's k order is permuted per thread so that each
-//   thread's operands are 16 contiguous weights of one row (the same
-//   permutation is applied to x), and MMA rows are mapped to tile rows by a
-//   3-bit reversal so that every shared-memory read is bank-conflict free.
+//   multiples of 8. A thread's operands are rows g and g + 8 and four groups
+//   of 8 consecutive columns (32k + 8t, k = 0..3, of its half); the MMA k
+//   order is permuted per thread the same way for x. Every shared-memory
+//   read is bank-conflict free except the pair-table lookups (16 table
+//   copies: lanes l and l + 16 share one).
+// * Programmatic dependent launch: the kernel lets the next kernel in the
+//   stream start at once. Shared memory stays under half an SM, so the next
+//   GEMV's CTA is resident alongside, prefetches its first stages of
+//   weights, and waits (griddepcontrol.wait) only before reading x.
 //
 // The dense BF16 baseline (RAW = true) runs the same pipeline over a plain
 // row-major BF16 matrix (the reference's lws_gemv_raw_bf16,
@@ -34,111 +41,159 @@
 
 namespace se12 {
 
-__device__ __forceinline__ int bitrev3(int v) { return ((v & 1) << 2) | (v & 2) | ((v >> 2) & 1); }
-
-__device__ __forceinline__ int range_start(int c, int tiles, int grid) {
-  return static_cast<int>((static_cast<long long>(tiles) * c) / grid);
+__device__ __forceinline__ int unit_start(int c, int units, int grid) {
+  return static_cast<int>((static_cast<long long>(units) * c) / grid);
 }
 
-// CTA whose range contains tile i.
-__device__ __forceinline__ int tile_owner(int i, int tiles, int grid) {
-  return static_cast<int>(((static_cast<long long>(i) + 1) * grid - 1) / tiles);
+// First tile of CTA c's run.
+__device__ __forceinline__ int tile_start(int c, int units, int grid, int tiles) {
+  return min(unit_start(c, units, grid) * kStageTiles, tiles);
 }
 
-// Offset of pair-table row `byte k of w` for this lane: byte * 128 + lane * 4.
+// CTA whose run contains tile i.
+__device__ __forceinline__ int tile_owner(int i, int units, int grid) {
+  const long long u = i / kStageTiles;
+  return static_cast<int>(((u + 1) * grid - 1) / units);
+}
+
+// Offset of the pair-table entry for byte K of w in this lane's column:
+// byte * 64 + (lane % 16) * 4.
 template <int K>
 __device__ __forceinline__ uint32_t lut_offset(uint32_t w, uint32_t lane4) {
-  const uint32_t shifted = (K == 0) ? (w << 7) : (w >> (8 * K - 7));
-  return (shifted & 0x7F80u) | lane4;
+  const uint32_t shifted = (K == 0) ? (w << 6) : (w >> (8 * K - 6));
+  return (shifted & 0x3FC0u) | lane4;
 }
 
 __device__ __forceinline__ uint32_t lds32(const uint8_t* base, uint32_t offset) {
   return *reinterpret_cast<const uint32_t*>(base + offset);
 }
 
-// Decodes the 16 weights (one row, 16 contiguous columns) of this thread:
-// sm bytes in `s`, ec bytes in `e`. Writes fragment halves for MMA j = 0..3:
-// lo[j] = weights (4j, 4j+1), hi[j] = weights (4j+2, 4j+3).
-__device__ __forceinline__ void decode_row16(uint4 s, uint2 e, const uint8_t* lut, uint32_t lane4, uint32_t (&lo)[4],
-                                             uint32_t (&hi)[4]) {
-  const uint32_t sw[4] = {s.x, s.y, s.z, s.w};
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const uint32_t ew = (j < 2) ? e.x : e.y;
-    uint32_t t0, t1;
-    if ((j & 1) == 0) {
-      t0 = lds32(lut, lut_offset<0>(ew, lane4));
-      t1 = lds32(lut, lut_offset<1>(ew, lane4));
-    } else {
-      t0 = lds32(lut, lut_offset<2>(ew, lane4));
-      t1 = lds32(lut, lut_offset<3>(ew, lane4));
-    }
-    lo[j] = pair_word(__byte_perm(sw[j], 0, 0x1100), t0);
-    hi[j] = pair_word(__byte_perm(sw[j], 0, 0x3322), t1);
-  }
+
+// Decodes 8 consecutive weights of one row (sm bytes in s, ec bytes in e)
+// into four BF16x2 words p[0..3] = columns (0,1), (2,3), (4,5), (6,7).
+__device__ __forceinline__ void decode8(uint2 s, uint32_t e, const uint8_t* lut, uint32_t lane4, uint32_t (&p)[4]) {
+  const uint32_t t0 = lds32(lut, lut_offset<0>(e, lane4));
+  const uint32_t t1 = lds32(lut, lut_offset<1>(e, lane4));
+  const uint32_t t2 = lds32(lut, lut_offset<2>(e, lane4));
+  const uint32_t t3 = lds32(lut, lut_offset<3>(e, lane4));
+  p[0] = pair_word(__byte_perm(s.x, 0, 0x1100), t0);
+  p[1] = pair_word(__byte_perm(s.x, 0, 0x3322), t1);
+  p[2] = pair_word(__byte_perm(s.y, 0, 0x1100), t2);
+  p[3] = pair_word(__byte_perm(s.y, 0, 0x3322), t3);
 }
 
-// Zeroes the halves of this thread's weight pairs and x pairs whose column
-// is >= `valid` (last, partial k-tile of a matrix with K % 256 != 0).
+// Zeroes the halves of a BF16x2 word whose column is >= `valid`.
 __device__ __forceinline__ uint32_t keep_pair(uint32_t w, int col, int valid) {
   const uint32_t lo = (col < valid) ? 0x0000FFFFu : 0u;
   const uint32_t hi = (col + 1 < valid) ? 0xFFFF0000u : 0u;
   return w & (lo | hi);
 }
 
-template <int NB, bool RAW>
-__global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const __grid_constant__ CUtensorMap map0,
-                                                            const __grid_constant__ CUtensorMap map1,
-                                                            const __grid_constant__ GemvArgs a) {
-  constexpr int kRedCols = 8 * NB;
-  extern __shared__ uint8_t smem_dynamic[];
-  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_dynamic) + 1023) & ~uintptr_t(1023));
+// Codebook entry c (0..14) from the codebook packed into two 64-bit words.
+__device__ __forceinline__ uint32_t codebook_entry(unsigned long long lo, unsigned long long hi, uint32_t c) {
+  return static_cast<uint32_t>(((c < 8) ? (lo >> (8 * c)) : (hi >> (8 * (c - 8)))) & 0xFFu);
+}
 
+template <typename T>
+__device__ __forceinline__ T lds_at(const uint8_t* smem, uint32_t offset) {
+  return *reinterpret_cast<const T*>(smem + offset);
+}
+
+template <int NB, bool RAW, bool XRES>
+__global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_constant__ CUtensorMap map0,
+                                                               const __grid_constant__ CUtensorMap map1,
+                                                               const GemvArgs a) {
+  constexpr int kWeightBytes = RAW ? kRawStageWeightBytes : kSe12StageWeightBytes;
+  // Pair table in static shared memory: a lookup is one LDS [reg + imm].
+  __shared__ __align__(16) uint32_t s_lut[RAW ? 4 : 256 * kLutCopies];
+  extern __shared__ __align__(1024) uint8_t smem_dynamic[];
+  // All dynamic shared memory is addressed as smem_dynamic + 32-bit offset,
+  // so every access compiles to a shared-memory instruction with 32-bit
+  // address arithmetic. `pad` aligns the weight buffers to 1024 bytes (the
+  // 128-byte TMA swizzle needs it).
+  const uint32_t pad = (1024u - (smem_addr(smem_dynamic) & 1023u)) & 1023u;
+  uint8_t* const sm8 = smem_dynamic;
+
+  // Kernel arguments, read once into registers.
   const int S = a.stages;
-  const int xstage = (a.batch * kXRowStride + 127) / 128 * 128;
-  uint8_t* wbuf = base;
-  uint8_t* p = base + S * kStageWeightBytes;
-  uint8_t* lut = p;
-  if (!RAW) p += kLutBytes;
-  uint8_t* xbuf = p;
-  p += S * xstage;
-  uint8_t* escbuf = p;
-  p += S * 16;
-  uint16_t* posbuf = reinterpret_cast<uint16_t*>(p);
-  p += S * 32;
-  int* meta = reinterpret_cast<int*>(p);
-  p += S * 16;
-  float* red = reinterpret_cast<float*>(p);
-  p += kConsumerWarps * 16 * kRedCols * 4;
-  uint64_t* full = reinterpret_cast<uint64_t*>(p);
-  p += S * 8;
-  uint64_t* empty = reinterpret_cast<uint64_t*>(p);
-  p += S * 8;
-  int* flag = reinterpret_cast<int*>(p);
-
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int B = a.batch;
   const int KT = a.m.tile_cols;
   const int T = a.m.tiles;
   const int K = a.m.cols;
-  const int start = range_start(blockIdx.x, T, a.grid);
-  const int end = range_start(blockIdx.x + 1, T, a.grid);
-  const int n = end - start;
+  const int N = a.m.rows;
+  const int G = a.grid;
+  const int ldx = a.ldx, ldy = a.ldy;
+  const uint16_t* const xg = a.x;
+  float* const yg = a.y;
+  float* const partials = a.partials;
+  int* const counters = a.counters;
+  const uint8_t* const esc_g = a.m.esc;
+  const uint16_t* const pos_g = a.m.escape_pos;
+  const int32_t* const fbindex_g = a.m.fallback_index;
+  const uint16_t* const fbraw_g = a.m.fallback_raw;
+  const int raw_3d = a.raw_3d;
+  const int kpad8 = (K + 7) & ~7;
+
+  // ------------------------------------------------------------ shared memory (offsets into sm8)
+  const uint32_t xrs = static_cast<uint32_t>(x_resident_stride(K));                    // resident x: bytes per batch row
+  const uint32_t xstage = (kStageTiles * B * kXRowStride + 127) / 128 * 128;           // staged x: bytes per stage
+  const uint32_t o_w = pad;                                                            // S x weights
+  const uint32_t o_x = o_w + S * kWeightBytes;                                         // x (resident or staged)
+  const uint32_t o_red = o_x + (XRES ? B * xrs : S * xstage);                          // [2][8][16][B] floats
+  const uint32_t o_rec = o_red + 2 * kConsumerWarps * 16 * B * 4;                      // escape record slots
+  const uint32_t o_bar = o_rec + (RAW ? 0 : kRecSlots * kRecSlotBytes);
+  uint64_t* const full = reinterpret_cast<uint64_t*>(sm8 + o_bar);  // [S] stage loaded
+  uint64_t* const empty = full + S;                                 // [S] stage consumed
+  uint64_t* const xbar = empty + S;                                 // resident x loaded
+  uint64_t* const deposited = xbar + 1;                             // [2] all warps' row partials written
+  uint64_t* const redfree = deposited + 2;                          // [2] row partials summed
+  uint64_t* const rec_full = redfree + 2;                           // [kRecSlots] records loaded
+  uint64_t* const rec_empty = rec_full + kRecSlots;                 // [kRecSlots] records consumed
+  float* const red = reinterpret_cast<float*>(sm8 + o_red);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int units = (T + kStageTiles - 1) / kStageTiles;
+  const int u0 = unit_start(blockIdx.x, units, G);
+  const int nstages = unit_start(blockIdx.x + 1, units, G) - u0;
+  const int tstart = tile_start(blockIdx.x, units, G, T);
+  const int tend = tile_start(blockIdx.x + 1, units, G, T);
+  const int tr_first = tstart / KT;
 
   if (tid == 0) {
     for (int s = 0; s < S; ++s) {
-      mbar_init(&full[s], 1);
+      // resident x: the weights' expect_tx arrival; staged x: + the "x issued" arrival
+      mbar_init(&full[s], XRES ? 1 : 2);
       mbar_init(&empty[s], kConsumerWarps);
+    }
+    mbar_init(xbar, 1);
+    for (int p = 0; p < 2; ++p) {
+      mbar_init(&deposited[p], kConsumerWarps);
+      mbar_init(&redfree[p], 1);
+    }
+    for (int r = 0; r < kRecSlots; ++r) {
+      mbar_init(&rec_full[r], 1);
+      mbar_init(&rec_empty[r], kConsumerWarps);
     }
     fence_barrier_init();
   }
   if (!RAW) {
-    uint32_t* lut32 = reinterpret_cast<uint32_t*>(lut);
-    for (int i = tid; i < 256 * kLutCopies; i += blockDim.x) lut32[i] = pair_entry(a.m.codebook, i >> 5);
+    unsigned long long cb_lo = 0, cb_hi = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) cb_lo |= static_cast<unsigned long long>(a.m.codebook[i]) << (8 * i);
+#pragma unroll
+    for (int i = 8; i < 16; ++i) cb_hi |= static_cast<unsigned long long>(a.m.codebook[i]) << (8 * (i - 8));
+    for (int i = tid; i < 256 * kLutCopies; i += blockDim.x) {
+      const uint32_t byte = static_cast<uint32_t>(i) / kLutCopies;
+      const uint32_t c0 = byte & 0xFu, c1 = byte >> 4;
+      const uint32_t h0 = (c0 == kEscapeCode) ? 0x807Fu : (codebook_entry(cb_lo, cb_hi, c0) << 7);
+      const uint32_t h1 = (c1 == kEscapeCode) ? 0x807Fu : (codebook_entry(cb_lo, cb_hi, c1) << 7);
+      s_lut[i] = h0 | (h1 << 16);
+    }
   }
   __syncthreads();
   grid_launch_dependents();
 
-  if (warp == kConsumerWarps) {
+  if (warp == kProducerWarp) {
     // ------------------------------------------------------------ producer
     const uint64_t pol_w = policy_evict_first();
     const uint64_t pol_x = policy_evict_last();
@@ -146,253 +201,411 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const __grid_constan
       prefetch_tmap(&map0);
       if (!RAW) prefetch_tmap(&map1);
     }
-    auto x_bytes = [&](int kt) -> uint32_t {
-      // the last slice of a row is rounded up to 16 bytes; the caller pads
-      // x rows to a multiple of 8 elements and the columns >= K are masked
-      const int valid = min(kTileCols, K - kt * kTileCols);
-      return (static_cast<uint32_t>(valid) * 2u + 15u) & ~15u;
-    };
-    auto issue_weights = [&](int i) {
-      const int tile = start + i, s = i % S;
-      const int tr = tile / KT, kt = tile - tr * KT;
+    const int prologue = min(nstages, S);
+    // the weights of stage i: 2 TMA loads (SE12) or one per tile (dense)
+    auto issue_weights = [&map0, &map1, sm8, o_w, full, S, T, KT, u0, lane, pol_w, raw_3d](int i) {
       if (lane == 0) {
-        uint8_t* w = wbuf + s * kStageWeightBytes;
-        uint32_t wbytes;
-        int fb = -1;
+        const int s = i % S;
+        const int tile0 = (u0 + i) * kStageTiles;
+        const int ntl = min(kStageTiles, T - tile0);
+        uint8_t* w = sm8 + o_w + s * kWeightBytes;
         if (RAW) {
-          wbytes = kStageWeightBytes;
-        } else {
-          const uint32_t bits = a.m.bitmap[tile >> 3];
-          if ((bits >> (7 - (tile & 7))) & 1u) fb = a.m.fallback_index[tile];
-          wbytes = (fb >= 0) ? kStageWeightBytes : (6144 + 48);
-        }
-        meta[s * 4] = fb;
-        mbar_arrive_expect_tx(&full[s], wbytes + static_cast<uint32_t>(a.batch) * x_bytes(kt));
-        if (RAW) {
+          mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(ntl) * 8192u);
+          int tr = tile0 / KT, kt = tile0 - tr * KT;
+          for (int j = 0; j < ntl; ++j) {
+            if (raw_3d) {
+              tma_load_3d(w + j * 8192, &map0, 0, kt * 4, tr * kTileRows, &full[s], pol_w);
+            } else {
 #pragma unroll
-          for (int c = 0; c < 4; ++c) tma_load_2d(w + c * 2048, &map0, kt * kTileCols + c * 64, tr * kTileRows, &full[s], pol_w);
-        } else if (fb >= 0) {
-          bulk_load(w, a.m.fallback_raw + static_cast<size_t>(fb) * kTileSize, kStageWeightBytes, &full[s], pol_w);
+              for (int c = 0; c < 4; ++c)
+                tma_load_2d(w + j * 8192 + c * 2048, &map0, kt * kTileCols + c * 64, tr * kTileRows, &full[s], pol_w);
+            }
+            if (++kt == KT) {
+              kt = 0;
+              ++tr;
+            }
+          }
         } else {
-          tma_load_2d(w, &map0, 0, tile * kTileRows, &full[s], pol_w);
-          tma_load_2d(w + 2048, &map0, 128, tile * kTileRows, &full[s], pol_w);
-          tma_load_2d(w + 4096, &map1, 0, tile * kTileRows, &full[s], pol_w);
-          bulk_load(escbuf + s * 16, a.m.esc + static_cast<size_t>(tile) * 16, 16, &full[s], pol_w);
-          bulk_load(posbuf + s * 16, a.m.escape_pos + static_cast<size_t>(tile) * 16, 32, &full[s], pol_w);
+          mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(kSe12StageWeightBytes));
+          tma_load_3d(w, &map0, 0, 0, tile0 * kTileRows, &full[s], pol_w);
+          tma_load_2d(w + kStageTiles * 4096, &map1, 0, tile0 * kTileRows, &full[s], pol_w);
         }
       }
       __syncwarp();
     };
-    auto issue_x = [&](int i) {
-      const int tile = start + i, s = i % S;
-      const int kt = tile % KT;
-      if (lane < a.batch) {
-        bulk_load(xbuf + s * xstage + lane * kXRowStride, a.x + static_cast<size_t>(lane) * a.ldx + kt * kTileCols,
-                  x_bytes(kt), &full[s], pol_x);
+    // staged x of stage i: lane l copies 16-byte chunk l of every (tile, batch row) slice
+    auto issue_x = [sm8, o_x, full, xg, ldx, xstage, S, T, KT, B, u0, lane, kpad8](int i) {
+      const int s = i % S;
+      const int tile0 = (u0 + i) * kStageTiles;
+      const int ntl = min(kStageTiles, T - tile0);
+      int kt = tile0 % KT;
+      for (int j = 0; j < ntl; ++j) {
+        const int col = kt * kTileCols + lane * 8;
+        if (col < kpad8) {
+          for (int b = 0; b < B; ++b)
+            cp_async_16_ca(sm8 + o_x + s * xstage + (j * B + b) * kXRowStride + lane * 16, xg + static_cast<size_t>(b) * ldx + col);
+        }
+        if (++kt == KT) kt = 0;
       }
+      cp_async_mbar_arrive(&full[s]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&full[s]);
       __syncwarp();
     };
-    const int prologue = min(n, S);
+    // Escape records of record group r (stages 4 r .. 4 r + 3 of this CTA's
+    // run): three bulk copies into slot r % kRecSlots. The tiles' offsets are
+    // multiples of 4 tiles, so every copy starts 16-byte aligned; the
+    // fallback-index table is padded to a multiple of 4 tiles.
+    auto issue_records = [sm8, o_rec, rec_full, rec_empty, pos_g, esc_g, fbindex_g, T, u0, nstages, lane,
+                          pol_w](int r) -> bool {
+      if (RAW || r * kRecGroupStages >= nstages) return true;
+      bool good = true;
+      if (lane == 0) {
+        const int slot = r % kRecSlots;
+        if (r >= kRecSlots) good = mbar_wait_sleep(&rec_empty[slot], static_cast<uint32_t>(r / kRecSlots - 1) & 1u);
+        if (good) {
+          const int t0 = (u0 + r * kRecGroupStages) * kStageTiles;
+          const int n = min(kRecGroupTiles, T - t0);
+          const int n4 = (n + 3) & ~3;
+          uint8_t* dst = sm8 + o_rec + slot * kRecSlotBytes;
+          mbar_arrive_expect_tx(&rec_full[slot], static_cast<uint32_t>(n * 48 + n4 * 4));
+          bulk_load(dst + kRecPosOffset, pos_g + static_cast<size_t>(t0) * kEscapeBudget, n * 32, &rec_full[slot], pol_w);
+          bulk_load(dst + kRecEscOffset, esc_g + static_cast<size_t>(t0) * kEscapeBudget, n * 16, &rec_full[slot], pol_w);
+          bulk_load(dst + kRecFbOffset, fbindex_g + t0, n4 * 4, &rec_full[slot], pol_w);
+        }
+      }
+      return __shfl_sync(0xFFFFFFFFu, good ? 1 : 0, 0) != 0;
+    };
+    issue_records(0);
+    issue_records(1);
     for (int i = 0; i < prologue; ++i) issue_weights(i);
     grid_dependency_wait();  // x is produced by the previous kernel in the stream
-    for (int i = 0; i < prologue; ++i) issue_x(i);
-    for (int i = prologue; i < n; ++i) {
+    if (XRES) {
+      const uint32_t xbytes = static_cast<uint32_t>(kpad8) * 2u;
+      if (lane == 0) mbar_arrive_expect_tx(xbar, xbytes * static_cast<uint32_t>(B));
+      __syncwarp();
+      if (lane < B) bulk_load(sm8 + o_x + lane * xrs, xg + static_cast<size_t>(lane) * ldx, xbytes, xbar, pol_x);
+      __syncwarp();
+    } else {
+      for (int i = 0; i < prologue; ++i) issue_x(i);
+    }
+    for (int i = prologue; i < nstages; ++i) {
       const int s = i % S;
       const uint32_t ph = static_cast<uint32_t>(i / S) & 1u;
-      if (!mbar_wait(&empty[s], ph ^ 1u)) break;
+      // group r + 1 reuses the slot of group r - 2, which the consumers
+      // finished before stage i - 4 <= i - S
+      if ((i & (kRecGroupStages - 1)) == 0 && !issue_records(i / kRecGroupStages + 1)) break;
+      if (!mbar_wait_sleep(&empty[s], ph ^ 1u)) break;
       issue_weights(i);
-      issue_x(i);
+      if (!XRES) issue_x(i);
+    }
+    return;
+  }
+
+  if (warp == kReducerWarp) {
+    // ------------------------------------------------------------ reducer
+    // Tile rows tr_first .. tr_last end in this CTA, in order. For each: wait
+    // for the eight consumer warps' partials, sum them in warp order, and
+    // write the row of y, or, for a row shared with other CTAs, this CTA's
+    // partial; the row's last contributor then sums all contributors'
+    // partials in CTA order (deterministic, no floating-point atomics).
+    if (tend <= tstart) return;
+    const int tr_last = (tend - 1) / KT;
+    const int outs = 16 * B;
+    grid_dependency_wait();  // y may be read by the previous kernel in the stream
+    for (int tr = tr_first; tr <= tr_last; ++tr) {
+      const int lr = tr - tr_first, pb = lr & 1;
+      if (!mbar_wait(&deposited[pb], static_cast<uint32_t>(lr >> 1) & 1u)) break;
+      const float* buf = red + pb * kConsumerWarps * 16 * B;
+      const bool whole = (tr * KT >= tstart) && ((tr + 1) * KT <= tend);
+      const int slot = (tr == tr_first) ? 0 : 1;
+      float* part = partials + (static_cast<size_t>(blockIdx.x) * 2 + slot) * (16 * 16);
+      for (int idx = lane; idx < outs; idx += 32) {
+        const int row = idx / B, b = idx - row * B;
+        float v = 0.f;
+#pragma unroll
+        for (int ww = 0; ww < kConsumerWarps; ++ww) v += buf[ww * 16 * B + idx];
+        if (whole) {
+          const int grow = tr * kTileRows + row;
+          if (grow < N) yg[static_cast<size_t>(b) * ldy + grow] = v;
+        } else {
+          part[b * 16 + row] = v;
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&redfree[pb]);
+      if (whole) continue;
+      __threadfence();
+      __syncwarp();
+      const int c_lo = tile_owner(tr * KT, units, G);
+      const int c_hi = tile_owner((tr + 1) * KT - 1, units, G);
+      int lastcta = 0;
+      if (lane == 0) lastcta = (atomicAdd(&counters[tr], 1) == c_hi - c_lo);
+      lastcta = __shfl_sync(0xFFFFFFFFu, lastcta, 0);
+      if (!lastcta) continue;
+      __threadfence();
+      for (int idx = lane; idx < outs; idx += 32) {
+        const int row = idx & 15, b = idx >> 4;
+        float v = 0.f;
+        for (int c = c_lo; c <= c_hi; ++c) {
+          const int cslot = (tile_start(c, units, G, T) / KT == tr) ? 0 : 1;
+          v += __ldcg(partials + (static_cast<size_t>(c) * 2 + cslot) * (16 * 16) + b * 16 + row);
+        }
+        const int grow = tr * kTileRows + row;
+        if (grow < N) yg[static_cast<size_t>(b) * ldy + grow] = v;
+      }
+      __syncwarp();
+      if (lane == 0) counters[tr] = 0;
     }
     return;
   }
 
   // -------------------------------------------------------------- consumers
-  grid_dependency_wait();
-  const int q = warp;                // 64-column quarter of every tile
+  const int jw = warp >> 1;          // tile of the stage this warp decodes
+  const int hw = warp & 1;           // its half (128 columns)
   const int g = lane >> 2, t = lane & 3;
-  const int rg = RAW ? g : bitrev3(g);  // tile rows rg and rg + 8 of this thread
-  const int X = rg & 7;                 // 128-byte swizzle phase of those rows
-  const uint32_t lane4 = static_cast<uint32_t>(lane) << 2;
-  const int ctid = tid;              // 0..127 among consumer threads
+  const uint32_t lut_lane = static_cast<uint32_t>(lane & (kLutCopies - 1)) << 2;
+  const uint8_t* const lut8 = reinterpret_cast<const uint8_t*>(s_lut);
 
-  float acc[NB][4];
-#pragma unroll
-  for (int nb = 0; nb < NB; ++nb) acc[nb][0] = acc[nb][1] = acc[nb][2] = acc[nb][3] = 0.f;
+  // Per-thread shared-memory offsets (stage 0, tile jw), fixed for the kernel.
+  // Thread (g, t) owns rows g, g + 8 of its tile and, in its half, the column
+  // groups 32 k + 8 t .. + 7 for k = 0..3. Row g + 8 lies a constant distance
+  // after row g; the group offset is a compile-time value XOR a per-thread
+  // swizzle term, so only four registers hold the layout.
+  uint32_t w_base, w_xor, e_base, e_xor;
+  if (RAW) {
+    // [16 rows][4 x 64-col chunks][128 B] per tile (3-D box; swizzle phase (4 row + chunk) & 7)
+    // or [4 chunks][16 rows][128 B] (2-D boxes; swizzle phase row & 7)
+    w_base = jw * 8192 + (raw_3d ? (4 * g + 2 * hw) * 128 : (2 * hw) * 2048 + g * 128);
+    w_xor = raw_3d ? static_cast<uint32_t>((4 * g + 2 * hw) & 7) : static_cast<uint32_t>(g);
+    e_base = e_xor = 0;
+  } else {
+    // sm: [64 rows][2 halves][128 B], swizzle phase (2 row + half) & 7;
+    // ec: [64 rows][128 B] after the sm box, swizzle phase row & 7.
+    const uint32_t R0 = 16 * jw + g;
+    const uint32_t X = (2 * R0 + hw) & 7;  // same for row R0 + 8
+    w_base = (2 * R0 + hw) * 128 + ((((t >> 1) ^ X) & 1) << 4) + 8 * (t & 1);
+    w_xor = (X & 6) << 4;                   // group k: + ((32 k) ^ w_xor)
+    e_base = kStageTiles * 4096 + R0 * 128 + (((4 * hw) ^ (R0 & 4)) << 4) + 4 * t;
+    e_xor = (R0 & 3) << 4;                  // group k: + ((16 k) ^ e_xor)
+  }
+  // x of batch row g + 8 nb at column 128 hw + 8 t (+ 32 k) of a tile
+  const uint32_t x_thread = XRES ? o_x + static_cast<uint32_t>(g) * xrs + (128 * hw + 8 * t) * 2
+                                 : o_x + (jw * B + g) * kXRowStride + (128 * hw + 8 * t) * 2;
+  const uint32_t x_nb_step = XRES ? 8 * xrs : 8 * kXRowStride;
+
+  grid_dependency_wait();
   bool ok = true;
+  if (XRES) ok = mbar_wait(xbar, 0);
 
-  for (int i = 0; i < n; ++i) {
-    const int tile = start + i, s = i % S;
-    const uint32_t ph = static_cast<uint32_t>(i / S) & 1u;
-    const int tr = tile / KT, kt = tile - tr * KT;
-    if (ok) ok = mbar_wait(&full[s], ph);
-    if (ok) {
-      const uint8_t* w = wbuf + s * kStageWeightBytes;
-      const uint8_t* xs = xbuf + s * xstage;
-      const int fb = RAW ? -1 : meta[s * 4];
-      uint32_t a0[4], a1[4], a2[4], a3[4];  // fragment registers of MMA j: rows rg (a0, a2), rg + 8 (a1, a3)
-      if (RAW) {
-        const uint8_t* c0 = w + q * 2048;
-        const uint4 r0a = *reinterpret_cast<const uint4*>(c0 + rg * 128 + (((2 * t) ^ X) << 4));
-        const uint4 r0b = *reinterpret_cast<const uint4*>(c0 + rg * 128 + (((2 * t + 1) ^ X) << 4));
-        const uint4 r1a = *reinterpret_cast<const uint4*>(c0 + (rg + 8) * 128 + (((2 * t) ^ X) << 4));
-        const uint4 r1b = *reinterpret_cast<const uint4*>(c0 + (rg + 8) * 128 + (((2 * t + 1) ^ X) << 4));
-        a0[0] = r0a.x; a2[0] = r0a.y; a0[1] = r0a.z; a2[1] = r0a.w;
-        a0[2] = r0b.x; a2[2] = r0b.y; a0[3] = r0b.z; a2[3] = r0b.w;
-        a1[0] = r1a.x; a3[0] = r1a.y; a1[1] = r1a.z; a3[1] = r1a.w;
-        a1[2] = r1b.x; a3[2] = r1b.y; a1[3] = r1b.z; a3[3] = r1b.w;
-      } else if (fb >= 0) {
-        const uint8_t* r0 = w + rg * 512 + (64 * q + 16 * t) * 2;
-        const uint8_t* r1 = w + (rg + 8) * 512 + (64 * q + 16 * t) * 2;
-        const uint4 r0a = *reinterpret_cast<const uint4*>(r0), r0b = *reinterpret_cast<const uint4*>(r0 + 16);
-        const uint4 r1a = *reinterpret_cast<const uint4*>(r1), r1b = *reinterpret_cast<const uint4*>(r1 + 16);
-        a0[0] = r0a.x; a2[0] = r0a.y; a0[1] = r0a.z; a2[1] = r0a.w;
-        a0[2] = r0b.x; a2[2] = r0b.y; a0[3] = r0b.z; a2[3] = r0b.w;
-        a1[0] = r1a.x; a3[0] = r1a.y; a1[1] = r1a.z; a3[1] = r1a.w;
-        a1[2] = r1b.x; a3[2] = r1b.y; a1[3] = r1b.z; a3[3] = r1b.w;
-      } else {
-        const uint8_t* half = w + (q >> 1) * 2048;
-        const int smc = ((4 * (q & 1) + t) ^ X) << 4;
-        const uint4 s0 = *reinterpret_cast<const uint4*>(half + rg * 128 + smc);
-        const uint4 s1 = *reinterpret_cast<const uint4*>(half + (rg + 8) * 128 + smc);
-        const uint8_t* ecb = w + 4096;
-        const int ecc = (((2 * q + (t >> 1)) ^ X) << 4) + 8 * (t & 1);
-        const uint2 e0 = *reinterpret_cast<const uint2*>(ecb + rg * 128 + ecc);
-        const uint2 e1 = *reinterpret_cast<const uint2*>(ecb + (rg + 8) * 128 + ecc);
-        decode_row16(s0, e0, lut, lane4, a0, a2);
-        decode_row16(s1, e1, lut, lane4, a1, a3);
+  // two independent accumulator sets (column groups 0, 2 and 1, 3)
+  float acc[2][NB][4];
+#pragma unroll
+  for (int h = 0; h < 2; ++h)
+#pragma unroll
+    for (int nb = 0; nb < NB; ++nb) acc[h][nb][0] = acc[h][nb][1] = acc[h][nb][2] = acc[h][nb][3] = 0.f;
+
+  // Adds this warp's share of tile `tile` (column kt; record `lt` of record
+  // slot `rbase`) of stage s to acc.
+  auto process_tile = [&](int s, int kt, uint32_t rbase, int lt) {
+    const uint32_t wst = o_w + s * kWeightBytes;
+    const uint32_t xt = XRES ? x_thread + kt * (kTileCols * 2) : x_thread + s * xstage;
+    int fbi = -1;
+    uint32_t pos = kNoEscape, ex = 0;
+    if (!RAW) {
+      fbi = lds_at<int>(sm8, rbase + kRecFbOffset + lt * 4);
+      if (lane < kEscapeBudget) {
+        pos = lds_at<uint16_t>(sm8, rbase + kRecPosOffset + lt * 32 + lane * 2);
+        ex = lds_at<uint8_t>(sm8, rbase + kRecEscOffset + lt * 16 + lane);
       }
-
-      const bool partial_k = (kt == KT - 1) && (K & (kTileCols - 1));
+    }
+    const bool fb = !RAW && fbi >= 0;
+    uint32_t frag0[4][4], frag1[4][4];  // [group][pair]: rows g, g + 8
+    if (RAW) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        // chunk m = 2 hw + k / 2, 16-byte column block sc = 4 (k % 2) + t
+        const uint32_t m1 = k >> 1, sc = 4 * (k & 1) + t;
+        uint32_t off0, off1;
+        if (raw_3d) {
+          off0 = w_base + m1 * 128 + ((sc ^ ((w_xor + m1) & 7)) << 4);
+          off1 = off0 + 32 * 128;  // row + 8: same swizzle phase
+        } else {
+          off0 = w_base + m1 * 2048 + ((sc ^ w_xor) << 4);
+          off1 = off0 + 8 * 128;
+        }
+        const uint4 v0 = lds_at<uint4>(sm8, wst + off0);
+        const uint4 v1 = lds_at<uint4>(sm8, wst + off1);
+        frag0[k][0] = v0.x; frag0[k][1] = v0.y; frag0[k][2] = v0.z; frag0[k][3] = v0.w;
+        frag1[k][0] = v1.x; frag1[k][1] = v1.y; frag1[k][2] = v1.z; frag1[k][3] = v1.w;
+      }
+    } else if (fb) {
+      const uint16_t* raw = fbraw_g + static_cast<size_t>(fbi) * kTileSize + 128 * hw + 8 * t;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const uint4 v0 = __ldg(reinterpret_cast<const uint4*>(raw + g * kTileCols + 32 * k));
+        const uint4 v1 = __ldg(reinterpret_cast<const uint4*>(raw + (g + 8) * kTileCols + 32 * k));
+        frag0[k][0] = v0.x; frag0[k][1] = v0.y; frag0[k][2] = v0.z; frag0[k][3] = v0.w;
+        frag1[k][0] = v1.x; frag1[k][1] = v1.y; frag1[k][2] = v1.z; frag1[k][3] = v1.w;
+      }
+    } else {
+      uint2 sv0[4], sv1[4];
+      uint32_t ev0[4], ev1[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const uint32_t wo = wst + w_base + ((32u * k) ^ w_xor);
+        const uint32_t eo = wst + e_base + ((16u * k) ^ e_xor);
+        sv0[k] = lds_at<uint2>(sm8, wo);
+        sv1[k] = lds_at<uint2>(sm8, wo + 16 * 128);   // row + 8: 16 half-rows of 128 B later
+        ev0[k] = lds_at<uint32_t>(sm8, eo);
+        ev1[k] = lds_at<uint32_t>(sm8, eo + 8 * 128);
+      }
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        decode8(sv0[k], ev0[k], lut8, lut_lane, frag0[k]);
+        decode8(sv1[k], ev1[k], lut8, lut_lane, frag1[k]);
+      }
+    }
+    const bool partial_k = (kt == KT - 1) && (K & (kTileCols - 1));
+    if (partial_k) {
       const int valid = K - kt * kTileCols;
-      if (partial_k) {
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int col = 64 * q + 16 * t + 4 * j;
-          a0[j] = keep_pair(a0[j], col, valid);
-          a1[j] = keep_pair(a1[j], col, valid);
-          a2[j] = keep_pair(a2[j], col + 2, valid);
-          a3[j] = keep_pair(a3[j], col + 2, valid);
-        }
-      }
-
+      for (int k = 0; k < 4; ++k)
 #pragma unroll
-      for (int nb = 0; nb < NB; ++nb) {
-        const int row = nb * 8 + g;
-        uint4 xa = make_uint4(0, 0, 0, 0), xb = make_uint4(0, 0, 0, 0);
-        if (row < a.batch) {
-          const uint8_t* xr = xs + row * kXRowStride + (64 * q + 16 * t) * 2;
-          xa = *reinterpret_cast<const uint4*>(xr);
-          xb = *reinterpret_cast<const uint4*>(xr + 16);
+        for (int q = 0; q < 4; ++q) {
+          const int col = 128 * hw + 8 * t + 32 * k + 2 * q;
+          frag0[k][q] = keep_pair(frag0[k][q], col, valid);
+          frag1[k][q] = keep_pair(frag1[k][q], col, valid);
         }
-        uint32_t xw[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+    }
+#pragma unroll
+    for (int nb = 0; nb < NB; ++nb) {
+      const bool have = nb * 8 + g < B;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        uint4 xv = make_uint4(0, 0, 0, 0);
+        if (have) xv = lds_at<uint4>(sm8, xt + nb * x_nb_step + 64 * k);
+        uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
         if (partial_k) {
+          const int valid = K - kt * kTileCols;
 #pragma unroll
-          for (int m = 0; m < 8; ++m) xw[m] = keep_pair(xw[m], 64 * q + 16 * t + 2 * m, valid);
+          for (int q = 0; q < 4; ++q) xw[q] = keep_pair(xw[q], 128 * hw + 8 * t + 32 * k + 2 * q, valid);
         }
-#pragma unroll
-        for (int j = 0; j < 4; ++j) mma_bf16_16816(acc[nb], a0[j], a1[j], a2[j], a3[j], xw[2 * j], xw[2 * j + 1]);
+        mma_bf16_16816(acc[k & 1][nb], frag0[k][0], frag1[k][0], frag0[k][1], frag1[k][1], xw[0], xw[1]);
+        mma_bf16_16816(acc[k & 1][nb], frag0[k][2], frag1[k][2], frag0[k][3], frag1[k][3], xw[2], xw[3]);
       }
-
-      if (!RAW && fb < 0) {
-        // Escaped weights of this quarter: decoded as +0 above, added here.
-        const uint32_t mypos = (lane < kEscapeBudget) ? posbuf[s * 16 + lane] : kNoEscape;
-        const bool mine = (mypos != kNoEscape) && (((mypos & 255u) >> 6) == static_cast<uint32_t>(q));
-        unsigned pending = __ballot_sync(0xFFFFFFFFu, mine);
-        while (pending) {
-          const int e = __ffs(pending) - 1;
-          pending &= pending - 1;
-          const uint32_t pos = __shfl_sync(0xFFFFFFFFu, mypos, e);
-          const int r = static_cast<int>(pos >> 8), c = static_cast<int>(pos & 255u);
-          if ((r & 7) == rg) {
-            const uint32_t smb = w[(c >> 7) * 2048 + r * 128 + ((((c & 127) >> 4) ^ (r & 7)) << 4) + (c & 15)];
-            const float wv = bf16_bits_to_float(bf16_bits(smb, escbuf[s * 16 + e]));
+    }
+    if (!RAW && !fb) {
+      // Escaped weights of this half: decoded as +0 above, added here.
+      const bool mine = (pos != kNoEscape) && (((pos & 255u) >> 7) == static_cast<uint32_t>(hw));
+      unsigned pending = __ballot_sync(0xFFFFFFFFu, mine);
+      while (pending) {
+        const int e = __ffs(pending) - 1;
+        pending &= pending - 1;
+        const uint32_t epos = __shfl_sync(0xFFFFFFFFu, pos, e);
+        const uint32_t eex = __shfl_sync(0xFFFFFFFFu, ex, e);
+        const uint32_t r = epos >> 8, c = epos & 255u;
+        if ((r & 7) == static_cast<uint32_t>(g)) {
+          const uint32_t R = 16 * jw + r, bc = c & 127;
+          const uint32_t smb = sm8[wst + (2 * R + hw) * 128 + ((((bc >> 4) ^ ((2 * R + hw) & 7))) << 4) + (bc & 15)];
+          const float wv = bf16_bits_to_float(bf16_bits(smb, eex));
+          // x of batch rows 2t, 2t + 1 (+ 8 nb) at tile column c
+          const uint32_t xc = XRES ? o_x + kt * (kTileCols * 2) + c * 2 : o_x + s * xstage + jw * B * kXRowStride + c * 2;
+          const uint32_t xstep = XRES ? xrs : kXRowStride;
 #pragma unroll
-            for (int nb = 0; nb < NB; ++nb) {
-              const int b0 = nb * 8 + 2 * t;
-              const float x0 = (b0 < a.batch) ? bf16_bits_to_float(*reinterpret_cast<const uint16_t*>(xs + b0 * kXRowStride + 2 * c)) : 0.f;
-              const float x1 = (b0 + 1 < a.batch) ? bf16_bits_to_float(*reinterpret_cast<const uint16_t*>(xs + (b0 + 1) * kXRowStride + 2 * c)) : 0.f;
-              if (r >= 8) {
-                acc[nb][2] = fmaf(wv, x0, acc[nb][2]);
-                acc[nb][3] = fmaf(wv, x1, acc[nb][3]);
-              } else {
-                acc[nb][0] = fmaf(wv, x0, acc[nb][0]);
-                acc[nb][1] = fmaf(wv, x1, acc[nb][1]);
-              }
+          for (int nb = 0; nb < NB; ++nb) {
+            const int b0 = nb * 8 + 2 * t;
+            const float x0 = (b0 < B) ? bf16_bits_to_float(lds_at<uint16_t>(sm8, xc + b0 * xstep)) : 0.f;
+            const float x1 = (b0 + 1 < B) ? bf16_bits_to_float(lds_at<uint16_t>(sm8, xc + (b0 + 1) * xstep)) : 0.f;
+            if (r >= 8) {
+              acc[0][nb][2] = fmaf(wv, x0, acc[0][nb][2]);
+              acc[0][nb][3] = fmaf(wv, x1, acc[0][nb][3]);
+            } else {
+              acc[0][nb][0] = fmaf(wv, x0, acc[0][nb][0]);
+              acc[0][nb][1] = fmaf(wv, x1, acc[0][nb][1]);
             }
           }
         }
       }
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[s]);
+  };
 
-    if (kt == KT - 1 || i == n - 1) {
-      // ---------------------------------------------------- finish tile row tr
-      const bool whole = (tr * KT >= start) && ((tr + 1) * KT <= end);
-      const int slot = (tr == start / KT) ? 0 : 1;
-      float* rw = red + q * 16 * kRedCols;
+  // Tile row tr ends: deposit this warp's partial in reduction buffer
+  // (local row index & 1) for the reducer warp. A warp waits only to reuse
+  // a buffer whose previous row the reducer has not summed yet.
+  auto finish_row = [&](int tr) {
+    const int lr = tr - tr_first;
+    const int pb = lr & 1;
+    const uint32_t use = static_cast<uint32_t>(lr >> 1) & 1u;
+    if (ok && !mbar_wait(&redfree[pb], use ^ 1u)) ok = false;
+    if (ok) {
+      float* rw = red + (pb * kConsumerWarps + warp) * 16 * B;
 #pragma unroll
       for (int nb = 0; nb < NB; ++nb) {
-        rw[rg * kRedCols + nb * 8 + 2 * t] = acc[nb][0];
-        rw[rg * kRedCols + nb * 8 + 2 * t + 1] = acc[nb][1];
-        rw[(rg + 8) * kRedCols + nb * 8 + 2 * t] = acc[nb][2];
-        rw[(rg + 8) * kRedCols + nb * 8 + 2 * t + 1] = acc[nb][3];
-        acc[nb][0] = acc[nb][1] = acc[nb][2] = acc[nb][3] = 0.f;
-      }
-      named_barrier(1, kConsumerWarps * 32);
-      const int outs = 16 * a.batch;
-      const int stride = 16 * kRedCols;
-      float* part = a.partials + (static_cast<size_t>(blockIdx.x) * 2 + slot) * (16 * kRedCols);
-      for (int idx = ctid; idx < outs && ok; idx += kConsumerWarps * 32) {
-        const int row = idx & 15, b = idx >> 4;
-        const float v = ((red[row * kRedCols + b] + red[stride + row * kRedCols + b]) + red[2 * stride + row * kRedCols + b]) +
-                        red[3 * stride + row * kRedCols + b];
-        if (whole) {
-          const int grow = tr * kTileRows + row;
-          if (grow < a.m.rows) a.y[static_cast<size_t>(b) * a.ldy + grow] = v;
-        } else {
-          part[b * 16 + row] = v;
+        const int b0 = nb * 8 + 2 * t;
+        if (b0 < B) {
+          rw[g * B + b0] = acc[0][nb][0] + acc[1][nb][0];
+          rw[(g + 8) * B + b0] = acc[0][nb][2] + acc[1][nb][2];
+        }
+        if (b0 + 1 < B) {
+          rw[g * B + b0 + 1] = acc[0][nb][1] + acc[1][nb][1];
+          rw[(g + 8) * B + b0 + 1] = acc[0][nb][3] + acc[1][nb][3];
         }
       }
-      if (!whole) {
-        __threadfence();
-        named_barrier(1, kConsumerWarps * 32);
-        const int c_lo = tile_owner(tr * KT, T, a.grid);
-        const int c_hi = tile_owner((tr + 1) * KT - 1, T, a.grid);
-        if (ctid == 0) {
-          int last = 0;
-          if (ok) last = (atomicAdd(&a.counters[tr], 1) == c_hi - c_lo);
-          *flag = last;
-        }
-        named_barrier(1, kConsumerWarps * 32);
-        if (*flag) {
-          __threadfence();
-          for (int idx = ctid; idx < outs; idx += kConsumerWarps * 32) {
-            const int row = idx & 15, b = idx >> 4;
-            float v = 0.f;
-            for (int c = c_lo; c <= c_hi; ++c) {
-              const int cslot = (range_start(c, T, a.grid) / KT == tr) ? 0 : 1;
-              v += __ldcg(a.partials + (static_cast<size_t>(c) * 2 + cslot) * (16 * kRedCols) + b * 16 + row);
-            }
-            const int grow = tr * kTileRows + row;
-            if (grow < a.m.rows) a.y[static_cast<size_t>(b) * a.ldy + grow] = v;
-          }
-          if (ctid == 0) a.counters[tr] = 0;
-        }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&deposited[pb]);
+    }
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+#pragma unroll
+      for (int nb = 0; nb < NB; ++nb) acc[h][nb][0] = acc[h][nb][1] = acc[h][nb][2] = acc[h][nb][3] = 0.f;
+  };
+
+  int tile0 = u0 * kStageTiles;
+  int tr0 = tile0 / KT, kt0 = tile0 - tr0 * KT;  // row and column of the stage's first tile
+  for (int i = 0; i < nstages; ++i) {
+    const int s = i % S;
+    const uint32_t ph = static_cast<uint32_t>(i / S) & 1u;
+    const int rg = i / kRecGroupStages;
+    const int rslot = rg % kRecSlots;
+    const uint32_t rbase = o_rec + rslot * kRecSlotBytes;
+    if (!RAW && (i & (kRecGroupStages - 1)) == 0 && ok)
+      ok = mbar_wait(&rec_full[rslot], static_cast<uint32_t>(rg / kRecSlots) & 1u);
+    if (ok) ok = mbar_wait(&full[s], ph);
+    const int ntl = min(kStageTiles, T - tile0);
+    // Walk the stage's tiles in order: this warp decodes tile jw; every tile
+    // row that ends inside the stage is finished at that point.
+    int kt = kt0, tr = tr0;
+    for (int j = 0; j < ntl; ++j) {
+      if (j == jw && ok) process_tile(s, kt, rbase, (i & (kRecGroupStages - 1)) * kStageTiles + jw);
+      if (kt == KT - 1 || tile0 + j == tend - 1) finish_row(tr);
+      if (++kt == KT) {
+        kt = 0;
+        ++tr;
       }
-      named_barrier(1, kConsumerWarps * 32);
+    }
+    __syncwarp();
+    if (lane == 0) {
+      mbar_arrive(&empty[s]);
+      if (!RAW && ((i & (kRecGroupStages - 1)) == kRecGroupStages - 1 || i == nstages - 1)) mbar_arrive(&rec_empty[rslot]);
+    }
+    tile0 += kStageTiles;
+    kt0 += kStageTiles;
+    while (kt0 >= KT) {
+      kt0 -= KT;
+      ++tr0;
     }
   }
 }
 
 cudaError_t launch_gemv(bool raw, const CUtensorMap& map0, const CUtensorMap& map1, const GemvArgs& a, int nblocks,
                         size_t smem, cudaStream_t stream, bool pdl) {
-  void (*kernel)(const CUtensorMap, const CUtensorMap, const GemvArgs) = nullptr;
-  if (raw) {
-    kernel = (nblocks == 1) ? gemv_kernel<1, true> : gemv_kernel<2, true>;
-  } else {
-    kernel = (nblocks == 1) ? gemv_kernel<1, false> : gemv_kernel<2, false>;
-  }
+  using Kernel = void (*)(const CUtensorMap, const CUtensorMap, const GemvArgs);
+  static const Kernel table[2][2][2] = {
+      {{gemv_kernel<1, false, false>, gemv_kernel<1, false, true>}, {gemv_kernel<1, true, false>, gemv_kernel<1, true, true>}},
+      {{gemv_kernel<2, false, false>, gemv_kernel<2, false, true>}, {gemv_kernel<2, true, false>, gemv_kernel<2, true, true>}}};
+  const Kernel kernel = table[nblocks == 1 ? 0 : 1][raw ? 1 : 0][a.x_resident ? 1 : 0];
+  if (!raw) smem -= kLutBytes;  // the pair table is static shared memory
   cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (err != cudaSuccess) return err;
   cudaLaunchConfig_t cfg = {};

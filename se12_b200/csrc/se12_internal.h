@@ -17,7 +17,7 @@ struct MatrixView {
   const uint8_t* bitmap;           // [ceil(T/8)] fallback bitmap, MSB first
   const uint16_t* fallback_raw;    // [F*4096] raw BF16 bits of fallback tiles
   const uint16_t* escape_pos;      // [T*16] derived: tile-flat index of each escape, 0xFFFF unused
-  const int32_t* fallback_index;   // [T] derived: rank among fallback tiles, -1 otherwise
+  const int32_t* fallback_index;   // [round4(T)] derived: rank among fallback tiles, -1 otherwise
   int rows, cols;                  // N, K (unpadded)
   int tile_rows, tile_cols;        // ceil(N/16), ceil(K/256)
   int tiles;                       // tile_rows * tile_cols
@@ -36,28 +36,56 @@ struct GemvArgs {
   int* counters;       // [tile_rows] arrival counters, zero between calls
   int grid;
   int stages;
+  int raw_3d;          // dense baseline: 1 = one 3-D box per tile, 0 = four 2-D boxes
+  int x_resident;      // 1: all of x in shared memory; 0: x staged per stage
 };
 
-// Shared-memory carve-up of the GEMV kernels (bytes). The weight area of a
-// stage holds either one SE12 tile (sm: 2 x 2048 swizzled halves, ec: 2048
-// swizzled) or one raw 16x256 BF16 tile (8192 bytes).
-constexpr int kStageWeightBytes = 8192;
-constexpr int kXRowStride = 528;        // bytes per batch row of a staged x slice (512 + 16 pad)
-constexpr int kLutCopies = 32;          // one LUT column per lane: conflict-free lookups
+// Pipeline geometry of the GEMV kernels. One stage holds kStageTiles
+// consecutive tiles of the linear tile sequence:
+//   SE12: sm as one 3-D TMA box [64 rows][2 halves][128 B] (16 KB) and ec as
+//         one 2-D box [64 rows][128 B] (8 KB), both with the 128-byte swizzle;
+//   dense baseline: one 3-D box [16 rows][4 x 64 columns] (8 KB) per tile.
+// x is either resident (all of x[B, K] in shared memory, one bulk copy per
+// batch row per CTA) or, when that does not fit, staged per stage by the
+// producer warp's lanes with cp.async.
+constexpr int kStageTiles = 4;
+constexpr int kSe12StageWeightBytes = kStageTiles * 6144;
+constexpr int kRawStageWeightBytes = kStageTiles * 8192;
+constexpr int kXRowStride = 576;        // bytes per (tile, batch row) x slice when staged: 512 + 64 pad
+constexpr int kLutCopies = 16;          // pair-table column per lane % 16
 constexpr int kLutBytes = 256 * kLutCopies * 4;
-constexpr int kConsumerWarps = 4;
-constexpr int kGemvThreads = (kConsumerWarps + 1) * 32;
+constexpr int kConsumerWarps = 8;       // warp w: half w % 2 of tile w / 2 of every stage
+constexpr int kProducerWarp = kConsumerWarps;      // TMA / bulk copies
+constexpr int kReducerWarp = kConsumerWarps + 1;   // sums the consumers' row partials
+constexpr int kGemvThreads = (kConsumerWarps + 2) * 32;
+// Escape records (escape positions, escape slots, fallback indices) of
+// kRecGroupStages consecutive stages are copied into shared memory together,
+// into one of kRecSlots slots: [16 tiles][16] u16 positions, [16][16] u8
+// slots, [16] i32 fallback indices.
+constexpr int kRecGroupStages = 4;
+constexpr int kRecGroupTiles = kRecGroupStages * kStageTiles;
+constexpr int kRecSlots = 3;
+constexpr int kRecPosOffset = 0;
+constexpr int kRecEscOffset = kRecGroupTiles * 32;
+constexpr int kRecFbOffset = kRecEscOffset + kRecGroupTiles * 16;
+constexpr int kRecSlotBytes = kRecFbOffset + kRecGroupTiles * 4;
+constexpr size_t kCoResidentSmem = 112 * 1024;  // two CTAs (current + next kernel) fit on one SM
 
-inline int x_stage_bytes(int batch) { return (batch * kXRowStride + 127) / 128 * 128; }
+// Bytes per batch row of resident x: K rounded up to 8 elements, then to 128
+// bytes, plus 64 so consecutive rows start in different bank groups.
+__host__ __device__ inline int x_resident_stride(int cols) { return ((cols + 7) / 8 * 16 + 127) / 128 * 128 + 64; }
 
-inline size_t gemv_smem_bytes(bool raw, int stages, int nblocks, int batch) {
-  size_t bytes = 1024;                                      // alignment slack
-  bytes += (size_t)stages * kStageWeightBytes;              // weights
-  if (!raw) bytes += kLutBytes;                             // pair LUT
-  bytes += (size_t)stages * x_stage_bytes(batch);           // x slices
-  bytes += (size_t)stages * 64;                             // esc (16) + positions (32) + meta (16)
-  bytes += (size_t)kConsumerWarps * 16 * 8 * nblocks * 4;   // row reduction
-  bytes += (size_t)stages * 16 + 64;                        // barriers + flags
+inline size_t x_stage_bytes(int batch) { return ((size_t)kStageTiles * batch * kXRowStride + 127) / 128 * 128; }
+
+inline size_t gemv_smem_bytes(bool raw, bool x_resident, int stages, int batch, int cols) {
+  size_t per_stage = (raw ? kRawStageWeightBytes : kSe12StageWeightBytes) + (x_resident ? 0 : x_stage_bytes(batch));
+  size_t bytes = 1024;                                                  // alignment slack
+  bytes += (size_t)stages * per_stage;
+  if (!raw) bytes += kLutBytes;
+  if (x_resident) bytes += (size_t)batch * x_resident_stride(cols);
+  bytes += 2 * (size_t)kConsumerWarps * 16 * batch * 4;                // two row-reduction buffers
+  if (!raw) bytes += (size_t)kRecSlots * kRecSlotBytes;                 // escape records
+  bytes += (size_t)stages * 16 + 128;                                   // barriers
   return bytes;
 }
 

@@ -61,7 +61,7 @@ class DeviceSe12Matrix:
     """An SE12-encoded [rows, cols] BF16 matrix resident on one GPU."""
 
     def __init__(self, rows: int, cols: int, codebook, sm: torch.Tensor, ec: torch.Tensor, esc: torch.Tensor,
-                 fallback_bitmap: torch.Tensor, fallback_raw: torch.Tensor, fallback_index: torch.Tensor | None = None):
+                 fallback_bitmap: torch.Tensor, fallback_raw: torch.Tensor):
         lib = _lib.load()
         self.rows, self.cols = int(rows), int(cols)
         self.codebook = tuple(int(v) for v in codebook)
@@ -85,7 +85,8 @@ class DeviceSe12Matrix:
         self.fallback_raw = raw if raw.numel() else torch.zeros(8, dtype=torch.int16, device=self.device)
         self.fallback_tiles = raw.numel() // TILE_SIZE
         self.escape_pos = torch.empty(self.tiles * ESCAPE_BUDGET, dtype=torch.int16, device=self.device)
-        self.fallback_index = torch.empty(self.tiles, dtype=torch.int32, device=self.device)
+        # padded to a multiple of 4 tiles (the GEMV copies it in 16-byte groups)
+        self.fallback_index = torch.empty((self.tiles + 3) // 4 * 4, dtype=torch.int32, device=self.device)
 
         s = _lib.Se12StreamsStruct()
         s.rows, s.cols = self.rows, self.cols

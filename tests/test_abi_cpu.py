@@ -59,7 +59,7 @@ def test_status_strings_and_version(lib):
 def test_derived_table_sizes(lib):
     # 33 x 300 -> 3 x 2 tiles
     assert lib.se12_escape_pos_bytes(33, 300) == 6 * 16 * 2
-    assert lib.se12_fallback_index_bytes(33, 300) == 6 * 4
+    assert lib.se12_fallback_index_bytes(33, 300) == 8 * 4  # padded to a multiple of 4 tiles
     assert lib.se12_escape_pos_bytes(256000, 2304) == 16000 * 9 * 32
 
 
