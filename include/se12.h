@@ -112,6 +112,29 @@ int se12_workspace_clear(void* workspace_dev, size_t bytes, void* stream);
 int se12_gemv(const se12_matrix* m, const uint16_t* x_dev, int batch, int ldx, float* y_dev, int ldy,
               void* workspace_dev, size_t workspace_bytes, void* stream);
 
+/*
+ * se12_gemv without a caller workspace, for callers that cannot allocate
+ * device memory: a host that has reserved all of HBM for its own arena (so
+ * cudaMalloc fails), or a binding that holds no device buffer it could keep
+ * alive and zeroed between calls. It has no counterpart in the reference.
+ * Same arguments, result and errors as se12_gemv, except:
+ *  - The scratch is a fixed 768 KiB array in the library's device image,
+ *    held by every GPU that loads the library until the process exits. It
+ *    limits the matrix to 65536 tile rows (1,048,576 rows) and the launch to
+ *    256 CTAs; larger requests return SE12_ERR_INVALID_ARGUMENT or
+ *    SE12_ERR_UNSUPPORTED_DEVICE with a message, and launch nothing.
+ *  - The current device must be the matrix's device. The first call on a
+ *    device looks up the scratch's address (cudaGetSymbolAddress); make that
+ *    first call before any stream capture.
+ *  - Every call clears the scratch's arrival counters on `stream`
+ *    (cudaMemsetAsync) and then launches the GEMV; it allocates nothing.
+ *  - All calls on a device share the one scratch, which keeps the last
+ *    call's contents: calls that can overlap on the GPU (on different
+ *    streams without ordering between them) race and give wrong results.
+ */
+int se12_gemv_noalloc(const se12_matrix* m, const uint16_t* x_dev, int batch, int ldx, float* y_dev, int ldy,
+                      void* stream);
+
 /* Exact BF16 bits of the whole matrix, row-major [rows, ldo] (ldo >= cols).
  * Replaces CudaSe12WeightDecoder.decode / decode_to_device and the kernel
  * lws_se12_decode (src/lws/adapters/cuda/se12_decoder.py:54-76,

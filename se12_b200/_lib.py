@@ -58,6 +58,7 @@ SIGNATURES = {
     "se12_gemv_workspace_bytes": (c_size_t, [c_void_p, c_int]),
     "se12_workspace_clear": (c_int, [c_void_p, c_size_t, c_void_p]),
     "se12_gemv": (c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p, c_int, c_void_p, c_size_t, c_void_p]),
+    "se12_gemv_noalloc": (c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p, c_int, c_void_p]),
     "se12_decode": (c_int, [c_void_p, c_void_p, c_int, c_void_p]),
     "se12_decode_rows": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p]),
     "bf16_gemv_workspace_bytes": (c_size_t, [c_int, c_int, c_int]),

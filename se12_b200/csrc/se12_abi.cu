@@ -296,6 +296,91 @@ int se12_gemv(const se12_matrix* m, const uint16_t* x, int batch, int ldx, float
   return SE12_OK;
 }
 
+}  // extern "C"
+
+// ------------------------------------------------------------------ no-allocation GEMV
+// Scratch of se12_gemv_noalloc, for callers that cannot allocate device
+// memory: the stream-K partial rows of up to kNoAllocMaxGrid CTAs, then one
+// arrival counter per tile row for up to kNoAllocMaxTileRows tile rows. It
+// is part of the library's device image, so every GPU that loads the
+// library holds these 768 KiB until the process exits.
+namespace {
+constexpr int kNoAllocMaxGrid = 256;
+constexpr int kNoAllocMaxTileRows = 65536;
+constexpr size_t kNoAllocPartialsBytes = static_cast<size_t>(kNoAllocMaxGrid) * 2 * 16 * 16 * sizeof(float);
+constexpr size_t kNoAllocScratchBytes = kNoAllocPartialsBytes + static_cast<size_t>(kNoAllocMaxTileRows) * sizeof(int);
+constexpr int kNoAllocMaxDevices = 64;
+
+std::mutex g_noalloc_mutex;
+void* g_noalloc_scratch_ptr[kNoAllocMaxDevices] = {};
+}  // namespace
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+// Device address of the scratch on `device` (the current device). The first
+// call on a device looks it up with cudaGetSymbolAddress; later calls reuse it.
+static int noalloc_scratch(int device, void** out) {
+  if (device < 0 || device >= kNoAllocMaxDevices)
+    return fail(SE12_ERR_UNSUPPORTED_DEVICE, "se12_gemv_noalloc supports device ordinals below 64");
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (!g_noalloc_scratch_ptr[device]) {
+    void* ptr = nullptr;
+    cudaError_t err = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (err != cudaSuccess) return cuda_fail(err, "cudaGetSymbolAddress of the se12_gemv_noalloc scratch");
+    g_noalloc_scratch_ptr[device] = ptr;
+  }
+  *out = g_noalloc_scratch_ptr[device];
+  return SE12_OK;
+}
+
+extern "C" {
+
+int se12_gemv_noalloc(const se12_matrix* m, const uint16_t* x, int batch, int ldx, float* y, int ldy, void* stream) {
+  if (!m) return fail(SE12_ERR_INVALID_ARGUMENT, "null matrix");
+  int st = check_gemv_io(m->view.rows, m->view.cols, x, batch, ldx, y, ldy);
+  if (st != SE12_OK) return st;
+  int device = -1;
+  cudaError_t err = cudaGetDevice(&device);
+  if (err != cudaSuccess) return cuda_fail(err, "cudaGetDevice");
+  if (device != m->device)
+    return fail(SE12_ERR_INVALID_ARGUMENT, "se12_gemv_noalloc: the current device (" + std::to_string(device) +
+                                               ") is not the matrix's device (" + std::to_string(m->device) + ")");
+  if (m->view.tile_rows > kNoAllocMaxTileRows)
+    return fail(SE12_ERR_INVALID_ARGUMENT,
+                "se12_gemv_noalloc supports at most " + std::to_string(kNoAllocMaxTileRows * SE12_TILE_ROWS) +
+                    " rows (" + std::to_string(kNoAllocMaxTileRows) + " tile rows), got " +
+                    std::to_string(m->view.rows) + "; use se12_gemv with a workspace");
+  const LaunchConfig c = choose_config(false, m->view.tiles, m->view.cols, batch, m->sm_count);
+  if (c.grid > kNoAllocMaxGrid)
+    return fail(SE12_ERR_UNSUPPORTED_DEVICE, "se12_gemv_noalloc supports grids of at most " +
+                                                 std::to_string(kNoAllocMaxGrid) + " CTAs, this device needs " +
+                                                 std::to_string(c.grid));
+  void* scratch = nullptr;
+  st = noalloc_scratch(device, &scratch);
+  if (st != SE12_OK) return st;
+  int* counters = reinterpret_cast<int*>(static_cast<char*>(scratch) + kNoAllocPartialsBytes);
+  // The counters must start at zero; a completed call leaves them at zero,
+  // but clearing them here also recovers from a call that did not complete.
+  err = cudaMemsetAsync(counters, 0, static_cast<size_t>(m->view.tile_rows) * sizeof(int),
+                        static_cast<cudaStream_t>(stream));
+  if (err != cudaSuccess) return cuda_fail(err, "cudaMemsetAsync of the se12_gemv_noalloc counters");
+  se12::GemvArgs a{};
+  a.m = m->view;
+  a.x = x;
+  a.ldx = ldx;
+  a.batch = batch;
+  a.y = y;
+  a.ldy = ldy;
+  a.partials = static_cast<float*>(scratch);
+  a.counters = counters;
+  a.grid = c.grid;
+  a.stages = c.stages;
+  a.x_resident = c.x_resident;
+  err = se12::launch_gemv(false, m->sm_map, m->ec_map, a, c.nblocks, c.smem, static_cast<cudaStream_t>(stream), false);
+  if (err != cudaSuccess) return cuda_fail(err, "se12_gemv_noalloc launch");
+  return SE12_OK;
+}
+
 int se12_decode(const se12_matrix* m, uint16_t* out, int ldo, void* stream) {
   if (!m || !out) return fail(SE12_ERR_INVALID_ARGUMENT, "null argument");
   if (ldo < m->view.cols) return fail(SE12_ERR_INVALID_ARGUMENT, "ldo < cols");
