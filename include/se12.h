@@ -118,10 +118,10 @@ int se12_gemv(const se12_matrix* m, const uint16_t* x_dev, int batch, int ldx, f
  * cudaMalloc fails), or a binding that holds no device buffer it could keep
  * alive and zeroed between calls. It has no counterpart in the reference.
  * Same arguments, result and errors as se12_gemv, except:
- *  - The scratch is a fixed 768 KiB array in the library's device image,
+ *  - The scratch is a fixed 896 KiB array in the library's device image,
  *    held by every GPU that loads the library until the process exits. It
  *    limits the matrix to 65536 tile rows (1,048,576 rows) and the launch to
- *    256 CTAs; larger requests return SE12_ERR_INVALID_ARGUMENT or
+ *    320 CTAs (two per SM on up to 160 SMs); larger requests return SE12_ERR_INVALID_ARGUMENT or
  *    SE12_ERR_UNSUPPORTED_DEVICE with a message, and launch nothing.
  *  - The current device must be the matrix's device. The first call on a
  *    device looks up the scratch's address (cudaGetSymbolAddress); make that

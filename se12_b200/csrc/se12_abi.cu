@@ -114,11 +114,10 @@ int tiles_of(int rows, int cols) {
 // The fixed launch table that replaces the reference's run-time tuner
 // (lws.tune, src/lws/tune.py:34-57). The tile is fixed by the format (16x256)
 // and a stage by the kernel (4 tiles); what varies is the pipeline depth.
-// One CTA per SM (stream-K over stages). The depth is the largest of 4..2
-// stages that keeps shared memory under kCoResidentSmem, so that the next
-// GEMV in the stream can be resident beside this one and prefetch its
-// weights (programmatic dependent launch); large batches (x slices of 16
-// rows) exceed that and run alone with 2 stages.
+// Two CTAs per SM (stream-K over stages). The depth is the largest of 4..2
+// stages that keeps shared memory under kCoResidentSmem, so that two CTAs
+// fit on one SM; large batches (x slices of 16 rows) exceed that and run
+// with 2 stages.
 struct LaunchConfig {
   int grid;
   int stages;
@@ -143,7 +142,9 @@ LaunchConfig choose_config(bool raw, int tiles, int cols, int batch, int sm_coun
   }
   c.smem = se12::gemv_smem_bytes(raw, c.x_resident != 0, c.stages, batch, cols);
   const int units = (tiles + se12::kStageTiles - 1) / se12::kStageTiles;
-  c.grid = std::max(1, std::min(units, sm_count));
+  // two CTAs per SM: shared memory and registers allow it, and the second
+  // CTA's warps hide the first one's decode and barrier latencies
+  c.grid = std::max(1, std::min(units, 2 * sm_count));
   return c;
 }
 
@@ -303,9 +304,9 @@ int se12_gemv(const se12_matrix* m, const uint16_t* x, int batch, int ldx, float
 // memory: the stream-K partial rows of up to kNoAllocMaxGrid CTAs, then one
 // arrival counter per tile row for up to kNoAllocMaxTileRows tile rows. It
 // is part of the library's device image, so every GPU that loads the
-// library holds these 768 KiB until the process exits.
+// library holds these 896 KiB until the process exits.
 namespace {
-constexpr int kNoAllocMaxGrid = 256;
+constexpr int kNoAllocMaxGrid = 320;
 constexpr int kNoAllocMaxTileRows = 65536;
 constexpr size_t kNoAllocPartialsBytes = static_cast<size_t>(kNoAllocMaxGrid) * 2 * 16 * 16 * sizeof(float);
 constexpr size_t kNoAllocScratchBytes = kNoAllocPartialsBytes + static_cast<size_t>(kNoAllocMaxTileRows) * sizeof(int);

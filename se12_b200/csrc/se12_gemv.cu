@@ -6,32 +6,35 @@
 //
 // * Stream-K over the tile sequence. The matrix is the linear sequence of
 //   its T tiles in memory order (tile-row major, 16x256 weights each), cut
-//   into stages of 4 consecutive tiles. CTA c (one per SM) owns a contiguous
+//   into stages of 4 consecutive tiles. CTA c (two per SM) owns a contiguous
 //   run of stages. Tile rows entirely inside a CTA's run are written
 //   directly; a tile row split between CTAs is finished by its last
 //   contributor, which sums the partials in CTA order (deterministic, no
 //   floating-point atomics).
 // * Warp-specialised pipeline. A producer warp moves each stage's sm bytes
 //   with one 3-D TMA load ([64 rows][2 halves][128 B]) and its ec bytes with
-//   one 2-D TMA load ([64 rows][128 B]), both 128-byte swizzled; its lanes
-//   copy the escape slots, escape positions and x slices with cp.async. All
-//   of it completes on one mbarrier per stage. Eight consumer warps: warp w
-//   takes half w % 2 (128 columns) of tile w / 2 of every stage.
-// * Decode in registers straight into mma.sync fragments: per pair of
-//   weights one byte-permute (sign|mantissa), one lookup of the ec byte in a
-//   lane-replicated 256-entry pair table, one lop3. Escaped weights decode to
-//   +0 in the fragment and are added exactly afterwards (w * x in fp32) from
-//   the per-tile escape position list. Fallback tiles are read raw.
+//   one 2-D TMA load ([64 rows][128 B]), both 128-byte swizzled, onto one
+//   mbarrier per stage; the escape records of four stages at a time come
+//   with three bulk copies. Eight consumer warps: warp w takes half w % 2
+//   (128 columns) of tile w / 2 of every stage. A reducer warp sums the
+//   consumers' per-row partials, so consumers never wait for each other.
+// * Decode in registers straight into mma.sync fragments, with no table in
+//   memory: the 16-entry code -> exponent table lives in four registers and
+//   is indexed with byte permutes (prmt), 8 codes at a time. Escaped weights
+//   enter the MMA with exponent 0 (|w| < 2^-126) and their exact w * x is
+//   added in fp32 afterwards from the per-tile escape position list.
+//   Fallback tiles are read raw.
 // * bf16 m16n8k16 tensor-core MMA with fp32 accumulation; batch padded to
 //   multiples of 8. A thread's operands are rows g and g + 8 and four groups
 //   of 8 consecutive columns (32k + 8t, k = 0..3, of its half); the MMA k
 //   order is permuted per thread the same way for x. Every shared-memory
-//   read is bank-conflict free except the pair-table lookups (16 table
-//   copies: lanes l and l + 16 share one).
+//   read is bank-conflict free.
+// * Two CTAs per SM (shared memory under half an SM, 96 registers a
+//   thread): the second CTA's warps hide the first one's latencies.
 // * Programmatic dependent launch: the kernel lets the next kernel in the
-//   stream start at once. Shared memory stays under half an SM, so the next
-//   GEMV's CTA is resident alongside, prefetches its first stages of
-//   weights, and waits (griddepcontrol.wait) only before reading x.
+//   stream launch at once; its CTAs start as SMs free up, prefetch their
+//   first stages of weights, and wait (griddepcontrol.wait) only before
+//   reading x and writing y.
 //
 // The dense BF16 baseline (RAW = true) runs the same pipeline over a plain
 // row-major BF16 matrix (the reference's lws_gemv_raw_bf16,
@@ -56,42 +59,71 @@ __device__ __forceinline__ int tile_owner(int i, int units, int grid) {
   return static_cast<int>(((u + 1) * grid - 1) / units);
 }
 
-// Offset of the pair-table entry for byte K of w in this lane's column:
-// byte * 64 + (lane % 16) * 4.
-template <int K>
-__device__ __forceinline__ uint32_t lut_offset(uint32_t w, uint32_t lane4) {
-  const uint32_t shifted = (K == 0) ? (w << 6) : (w >> (8 * K - 6));
-  return (shifted & 0x3FC0u) | lane4;
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t selector) {
+  uint32_t d;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(selector));
+  return d;
 }
 
-__device__ __forceinline__ uint32_t lds32(const uint8_t* base, uint32_t offset) {
-  return *reinterpret_cast<const uint32_t*>(base + offset);
+// (a & m) | (b & ~m)
+__device__ __forceinline__ uint32_t select_bits(uint32_t a, uint32_t b, uint32_t m) {
+  uint32_t d;
+  asm("lop3.b32 %0, %1, %2, %3, 0xE4;" : "=r"(d) : "r"(a), "r"(b), "r"(m));
+  return d;
 }
 
-
-// Decodes 8 consecutive weights of one row (sm bytes in s, ec bytes in e)
-// into four BF16x2 words p[0..3] = columns (0,1), (2,3), (4,5), (6,7).
-__device__ __forceinline__ void decode8(uint2 s, uint32_t e, const uint8_t* lut, uint32_t lane4, uint32_t (&p)[4]) {
-  const uint32_t t0 = lds32(lut, lut_offset<0>(e, lane4));
-  const uint32_t t1 = lds32(lut, lut_offset<1>(e, lane4));
-  const uint32_t t2 = lds32(lut, lut_offset<2>(e, lane4));
-  const uint32_t t3 = lds32(lut, lut_offset<3>(e, lane4));
-  p[0] = pair_word(__byte_perm(s.x, 0, 0x1100), t0);
-  p[1] = pair_word(__byte_perm(s.x, 0, 0x3322), t1);
-  p[2] = pair_word(__byte_perm(s.y, 0, 0x1100), t2);
-  p[3] = pair_word(__byte_perm(s.y, 0, 0x3322), t3);
+// Exponent byte of code c as the decode table stores it: rotated right by
+// one bit, so that the byte placed twice in a half word ([b, b]) has the
+// exponent in bits 7..14. The escape code maps to exponent 0.
+__host__ __device__ __forceinline__ uint32_t table_byte(const uint8_t* codebook, int c) {
+  const uint32_t e = (c == kEscapeCode) ? 0u : codebook[c];
+  return ((e >> 1) | (e << 7)) & 0xFFu;
 }
 
-// Zeroes the halves of a BF16x2 word whose column is >= `valid`.
-__device__ __forceinline__ uint32_t keep_pair(uint32_t w, int col, int valid) {
-  const uint32_t lo = (col < valid) ? 0x0000FFFFu : 0u;
-  const uint32_t hi = (col + 1 < valid) ? 0xFFFF0000u : 0u;
-  return w & (lo | hi);
+// Decodes 8 consecutive weights of one row (sign|mantissa bytes in s, codes
+// in the nibbles of e, weight i in bits 4i..4i+3) into four BF16x2 words
+// p[0..3] = columns (0,1), (2,3), (4,5), (6,7). tab[0..3] hold table_byte
+// for codes 0..15 (code c in byte c % 4 of tab[c / 4]).
+//  * prmt selects bytes by 3-bit selectors: codes mod 8 look up tab[0..1]
+//    and tab[2..3] in two permutes per 4 codes, and a byte mask built from
+//    each code's bit 3 (a selector nibble with bit 3 set copies a byte's
+//    top bit) picks between them.
+//  * Each BF16 is the sign and mantissa bits (0x807F) of its sm byte placed
+//    twice, [s, s], and the exponent bits (0x7F80) of its table byte placed
+//    twice, [b, b].
+__device__ __forceinline__ void decode8(uint2 s, uint32_t e, const uint32_t (&tab)[4], uint32_t (&p)[4]) {
+  const uint32_t sel03 = e & 0x77777777u;   // selectors for weights 0..3 (low 16 bits)
+  const uint32_t sel47 = sel03 >> 16;        // weights 4..7
+  const uint32_t e4 = e << 4;                // bit 3 of the even codes at a byte's top bit
+  const uint32_t hi03 = prmt(e4, e, 0xD9C8u);  // 0xFF where code >= 8: bytes of e4/e for weights 0,1,2,3
+  const uint32_t hi47 = prmt(e4, e, 0xFBEAu);  // weights 4..7
+  const uint32_t x03 = select_bits(prmt(tab[2], tab[3], sel03), prmt(tab[0], tab[1], sel03), hi03);
+  const uint32_t x47 = select_bits(prmt(tab[2], tab[3], sel47), prmt(tab[0], tab[1], sel47), hi47);
+  p[0] = select_bits(prmt(s.x, 0, 0x1100u), prmt(x03, 0, 0x1100u), 0x807F807Fu);
+  p[1] = select_bits(prmt(s.x, 0, 0x3322u), prmt(x03, 0, 0x3322u), 0x807F807Fu);
+  p[2] = select_bits(prmt(s.y, 0, 0x1100u), prmt(x47, 0, 0x1100u), 0x807F807Fu);
+  p[3] = select_bits(prmt(s.y, 0, 0x3322u), prmt(x47, 0, 0x3322u), 0x807F807Fu);
 }
 
-// Codebook entry c (0..14) from the codebook packed into two 64-bit words.
-__device__ __forceinline__ uint32_t codebook_entry(unsigned long long lo, unsigned long long hi, uint32_t c) {
-  return static_cast<uint32_t>(((c < 8) ? (lo >> (8 * c)) : (hi >> (8 * (c - 8)))) & 0xFFu);
+// Padding weights (columns >= K of the last tile column) are +0.0 in the
+// packed tile with code 0, so they decode to +2^(codebook[0] - 127); against
+// the zeros that x holds there they contribute exactly 0, unless
+// codebook[0] == 255 (an infinite padding weight). For that case this
+// rewrites, in shared memory, the codes of this thread's padding weights to
+// the escape code, which decodes to +0. Each thread patches only the ec
+// words it reads itself.
+__device__ __forceinline__ void force_padding_escapes(uint8_t* sm8, uint32_t e_addr, uint32_t e_xor, int col0, int valid) {
+#pragma unroll
+  for (int r = 0; r < 2; ++r)
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      uint32_t* word = reinterpret_cast<uint32_t*>(sm8 + e_addr + r * 1024 + ((16u * k) ^ e_xor));
+      uint32_t v = *word;
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        if (col0 + 32 * k + i >= valid) v |= 0xFu << (4 * i);
+      *word = v;
+    }
 }
 
 template <typename T>
@@ -104,8 +136,6 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
                                                                const __grid_constant__ CUtensorMap map1,
                                                                const GemvArgs a) {
   constexpr int kWeightBytes = RAW ? kRawStageWeightBytes : kSe12StageWeightBytes;
-  // Pair table in static shared memory: a lookup is one LDS [reg + imm].
-  __shared__ __align__(16) uint32_t s_lut[RAW ? 4 : 256 * kLutCopies];
   extern __shared__ __align__(1024) uint8_t smem_dynamic[];
   // All dynamic shared memory is addressed as smem_dynamic + 32-bit offset,
   // so every access compiles to a shared-memory instruction with 32-bit
@@ -145,7 +175,8 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
   uint64_t* const full = reinterpret_cast<uint64_t*>(sm8 + o_bar);  // [S] stage loaded
   uint64_t* const empty = full + S;                                 // [S] stage consumed
   uint64_t* const xbar = empty + S;                                 // resident x loaded
-  uint64_t* const deposited = xbar + 1;                             // [2] all warps' row partials written
+  uint64_t* const xready = xbar + 1;                                // resident x loaded and its tail zeroed
+  uint64_t* const deposited = xready + 1;                           // [2] all warps' row partials written
   uint64_t* const redfree = deposited + 2;                          // [2] row partials summed
   uint64_t* const rec_full = redfree + 2;                           // [kRecSlots] records loaded
   uint64_t* const rec_empty = rec_full + kRecSlots;                 // [kRecSlots] records consumed
@@ -166,6 +197,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
       mbar_init(&empty[s], kConsumerWarps);
     }
     mbar_init(xbar, 1);
+    mbar_init(xready, 1);
     for (int p = 0; p < 2; ++p) {
       mbar_init(&deposited[p], kConsumerWarps);
       mbar_init(&redfree[p], 1);
@@ -176,18 +208,12 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
     }
     fence_barrier_init();
   }
-  if (!RAW) {
-    unsigned long long cb_lo = 0, cb_hi = 0;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) cb_lo |= static_cast<unsigned long long>(a.m.codebook[i]) << (8 * i);
-#pragma unroll
-    for (int i = 8; i < 16; ++i) cb_hi |= static_cast<unsigned long long>(a.m.codebook[i]) << (8 * (i - 8));
-    for (int i = tid; i < 256 * kLutCopies; i += blockDim.x) {
-      const uint32_t byte = static_cast<uint32_t>(i) / kLutCopies;
-      const uint32_t c0 = byte & 0xFu, c1 = byte >> 4;
-      const uint32_t h0 = (c0 == kEscapeCode) ? 0x807Fu : (codebook_entry(cb_lo, cb_hi, c0) << 7);
-      const uint32_t h1 = (c1 == kEscapeCode) ? 0x807Fu : (codebook_entry(cb_lo, cb_hi, c1) << 7);
-      s_lut[i] = h0 | (h1 << 16);
+  if (XRES) {
+    // columns kpad8 .. 256 KT - 1 of every resident x row are zero
+    const int tail = KT * kTileCols - kpad8;  // a multiple of 8 columns
+    for (int i = tid; i < B * (tail / 8); i += blockDim.x) {
+      const int b = i / (tail / 8), c = kpad8 + 8 * (i - b * (tail / 8));
+      *reinterpret_cast<uint4*>(sm8 + o_x + b * xrs + 2 * c) = make_uint4(0u, 0u, 0u, 0u);
     }
   }
   __syncthreads();
@@ -203,9 +229,8 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
     }
     const int prologue = min(nstages, S);
     // the weights of stage i: 2 TMA loads (SE12) or one per tile (dense)
-    auto issue_weights = [&map0, &map1, sm8, o_w, full, S, T, KT, u0, lane, pol_w, raw_3d](int i) {
+    auto issue_weights = [&map0, &map1, sm8, o_w, full, T, KT, u0, lane, pol_w, raw_3d](int i, int s) {
       if (lane == 0) {
-        const int s = i % S;
         const int tile0 = (u0 + i) * kStageTiles;
         const int ntl = min(kStageTiles, T - tile0);
         uint8_t* w = sm8 + o_w + s * kWeightBytes;
@@ -233,17 +258,33 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
       }
       __syncwarp();
     };
-    // staged x of stage i: lane l copies 16-byte chunk l of every (tile, batch row) slice
-    auto issue_x = [sm8, o_x, full, xg, ldx, xstage, S, T, KT, B, u0, lane, kpad8](int i) {
-      const int s = i % S;
+    // staged x of stage i: lane l copies 16-byte chunk l (columns 8 l .. 8 l
+    // + 7) of every (tile, batch row) slice; columns past K are written as
+    // zeros (the chunk holding column K with a plain load and a mask)
+    auto issue_x = [sm8, o_x, full, xg, ldx, xstage, T, KT, K, B, u0, lane](int i, int s) {
       const int tile0 = (u0 + i) * kStageTiles;
       const int ntl = min(kStageTiles, T - tile0);
       int kt = tile0 % KT;
       for (int j = 0; j < ntl; ++j) {
         const int col = kt * kTileCols + lane * 8;
-        if (col < kpad8) {
-          for (int b = 0; b < B; ++b)
-            cp_async_16_ca(sm8 + o_x + s * xstage + (j * B + b) * kXRowStride + lane * 16, xg + static_cast<size_t>(b) * ldx + col);
+        for (int b = 0; b < B; ++b) {
+          uint8_t* dst = sm8 + o_x + s * xstage + (j * B + b) * kXRowStride + lane * 16;
+          const uint16_t* src = xg + static_cast<size_t>(b) * ldx + col;
+          if (col + 8 <= K) {
+            cp_async_16_ca(dst, src);
+          } else {
+            uint4 v = make_uint4(0u, 0u, 0u, 0u);
+            if (col < K) {
+              v = *reinterpret_cast<const uint4*>(src);
+              uint32_t* w = reinterpret_cast<uint32_t*>(&v);
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                if (col + 2 * q >= K) w[q] = 0u;
+                else if (col + 2 * q + 1 >= K) w[q] &= 0xFFFFu;
+              }
+            }
+            *reinterpret_cast<uint4*>(dst) = v;
+          }
         }
         if (++kt == KT) kt = 0;
       }
@@ -278,7 +319,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
     };
     issue_records(0);
     issue_records(1);
-    for (int i = 0; i < prologue; ++i) issue_weights(i);
+    for (int i = 0; i < prologue; ++i) issue_weights(i, i);
     grid_dependency_wait();  // x is produced by the previous kernel in the stream
     if (XRES) {
       const uint32_t xbytes = static_cast<uint32_t>(kpad8) * 2u;
@@ -286,18 +327,33 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
       __syncwarp();
       if (lane < B) bulk_load(sm8 + o_x + lane * xrs, xg + static_cast<size_t>(lane) * ldx, xbytes, xbar, pol_x);
       __syncwarp();
+      if (K & 7) {
+        // the copy brought columns K .. kpad8 - 1 as the caller left them:
+        // zero them, then release x to the consumers
+        const bool landed = mbar_wait(xbar, 0);
+        if (landed && lane < B)
+          for (int c = K; c < kpad8; ++c) *reinterpret_cast<uint16_t*>(sm8 + o_x + lane * xrs + 2 * c) = 0;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(xready);
+      }
     } else {
-      for (int i = 0; i < prologue; ++i) issue_x(i);
+      for (int i = 0; i < prologue; ++i) issue_x(i, i);
     }
+    // stage i goes to slot s = i % S; its empty barrier completes phase
+    // i / S - 1 when the consumers release the slot's previous stage
+    int s = 0;
+    uint32_t ph = 1u;
     for (int i = prologue; i < nstages; ++i) {
-      const int s = i % S;
-      const uint32_t ph = static_cast<uint32_t>(i / S) & 1u;
       // group r + 1 reuses the slot of group r - 2, which the consumers
       // finished before stage i - 4 <= i - S
       if ((i & (kRecGroupStages - 1)) == 0 && !issue_records(i / kRecGroupStages + 1)) break;
       if (!mbar_wait_sleep(&empty[s], ph ^ 1u)) break;
-      issue_weights(i);
-      if (!XRES) issue_x(i);
+      issue_weights(i, s);
+      if (!XRES) issue_x(i, s);
+      if (++s == S) {
+        s = 0;
+        ph ^= 1u;
+      }
     }
     return;
   }
@@ -364,8 +420,14 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
   const int jw = warp >> 1;          // tile of the stage this warp decodes
   const int hw = warp & 1;           // its half (128 columns)
   const int g = lane >> 2, t = lane & 3;
-  const uint32_t lut_lane = static_cast<uint32_t>(lane & (kLutCopies - 1)) << 2;
-  const uint8_t* const lut8 = reinterpret_cast<const uint8_t*>(s_lut);
+  // an infinite padding weight needs its code rewritten (force_padding_escapes)
+  const bool pad_inf = !RAW && (K & (kTileCols - 1)) && a.m.codebook[0] == 255;
+  // decode table: table_byte of codes 0..15, four per register
+  uint32_t tab[4] = {0u, 0u, 0u, 0u};
+  if (!RAW) {
+#pragma unroll
+    for (int c = 0; c < 16; ++c) tab[c >> 2] |= table_byte(a.m.codebook, c) << (8 * (c & 3));
+  }
 
   // Per-thread shared-memory offsets (stage 0, tile jw), fixed for the kernel.
   // Thread (g, t) owns rows g, g + 8 of its tile and, in its half, the column
@@ -396,7 +458,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
 
   grid_dependency_wait();
   bool ok = true;
-  if (XRES) ok = mbar_wait(xbar, 0);
+  if (XRES) ok = mbar_wait((K & 7) ? xready : xbar, 0);
 
   // two independent accumulator sets (column groups 0, 2 and 1, 3)
   float acc[2][NB][4];
@@ -405,20 +467,12 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
 #pragma unroll
     for (int nb = 0; nb < NB; ++nb) acc[h][nb][0] = acc[h][nb][1] = acc[h][nb][2] = acc[h][nb][3] = 0.f;
 
-  // Adds this warp's share of tile `tile` (column kt; record `lt` of record
-  // slot `rbase`) of stage s to acc.
-  auto process_tile = [&](int s, int kt, uint32_t rbase, int lt) {
+  // Adds this warp's share of its tile of stage s (tile column kt) to acc.
+  // fbi: the tile's fallback index (-1: SE12 tile); lanes 0..15 hold its
+  // escape positions (pos) and exponents (ex).
+  auto process_tile = [&](int s, int kt, int fbi, uint32_t pos, uint32_t ex) {
     const uint32_t wst = o_w + s * kWeightBytes;
     const uint32_t xt = XRES ? x_thread + kt * (kTileCols * 2) : x_thread + s * xstage;
-    int fbi = -1;
-    uint32_t pos = kNoEscape, ex = 0;
-    if (!RAW) {
-      fbi = lds_at<int>(sm8, rbase + kRecFbOffset + lt * 4);
-      if (lane < kEscapeBudget) {
-        pos = lds_at<uint16_t>(sm8, rbase + kRecPosOffset + lt * 32 + lane * 2);
-        ex = lds_at<uint8_t>(sm8, rbase + kRecEscOffset + lt * 16 + lane);
-      }
-    }
     const bool fb = !RAW && fbi >= 0;
     uint32_t frag0[4][4], frag1[4][4];  // [group][pair]: rows g, g + 8
     if (RAW) {
@@ -449,6 +503,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
         frag1[k][0] = v1.x; frag1[k][1] = v1.y; frag1[k][2] = v1.z; frag1[k][3] = v1.w;
       }
     } else {
+      if (pad_inf && kt == KT - 1) force_padding_escapes(sm8, wst + e_base, e_xor, 128 * hw + 8 * t, K - kt * kTileCols);
       uint2 sv0[4], sv1[4];
       uint32_t ev0[4], ev1[4];
 #pragma unroll
@@ -462,21 +517,9 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
       }
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
-        decode8(sv0[k], ev0[k], lut8, lut_lane, frag0[k]);
-        decode8(sv1[k], ev1[k], lut8, lut_lane, frag1[k]);
+        decode8(sv0[k], ev0[k], tab, frag0[k]);
+        decode8(sv1[k], ev1[k], tab, frag1[k]);
       }
-    }
-    const bool partial_k = (kt == KT - 1) && (K & (kTileCols - 1));
-    if (partial_k) {
-      const int valid = K - kt * kTileCols;
-#pragma unroll
-      for (int k = 0; k < 4; ++k)
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int col = 128 * hw + 8 * t + 32 * k + 2 * q;
-          frag0[k][q] = keep_pair(frag0[k][q], col, valid);
-          frag1[k][q] = keep_pair(frag1[k][q], col, valid);
-        }
     }
 #pragma unroll
     for (int nb = 0; nb < NB; ++nb) {
@@ -485,18 +528,13 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
       for (int k = 0; k < 4; ++k) {
         uint4 xv = make_uint4(0, 0, 0, 0);
         if (have) xv = lds_at<uint4>(sm8, xt + nb * x_nb_step + 64 * k);
-        uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
-        if (partial_k) {
-          const int valid = K - kt * kTileCols;
-#pragma unroll
-          for (int q = 0; q < 4; ++q) xw[q] = keep_pair(xw[q], 128 * hw + 8 * t + 32 * k + 2 * q, valid);
-        }
-        mma_bf16_16816(acc[k & 1][nb], frag0[k][0], frag1[k][0], frag0[k][1], frag1[k][1], xw[0], xw[1]);
-        mma_bf16_16816(acc[k & 1][nb], frag0[k][2], frag1[k][2], frag0[k][3], frag1[k][3], xw[2], xw[3]);
+        mma_bf16_16816(acc[k & 1][nb], frag0[k][0], frag1[k][0], frag0[k][1], frag1[k][1], xv.x, xv.y);
+        mma_bf16_16816(acc[k & 1][nb], frag0[k][2], frag1[k][2], frag0[k][3], frag1[k][3], xv.z, xv.w);
       }
     }
     if (!RAW && !fb) {
-      // Escaped weights of this half: decoded as +0 above, added here.
+      // Escaped weights of this half: in the MMA with exponent 0 (below
+      // 2^-126 in magnitude), their exact products are added here.
       const bool mine = (pos != kNoEscape) && (((pos & 255u) >> 7) == static_cast<uint32_t>(hw));
       unsigned pending = __ballot_sync(0xFFFFFFFFu, mine);
       while (pending) {
@@ -561,23 +599,35 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
       for (int nb = 0; nb < NB; ++nb) acc[h][nb][0] = acc[h][nb][1] = acc[h][nb][2] = acc[h][nb][3] = 0.f;
   };
 
+  int s = 0;                 // stage slot of stage i, i % S
+  uint32_t ph = 0u;          // parity of its full-barrier phase, (i / S) & 1
+  int rq = 0, rslot = 0;     // stage within its record group, the group's slot
+  uint32_t rph = 0u;         // parity of the record slot's phase
   int tile0 = u0 * kStageTiles;
   int tr0 = tile0 / KT, kt0 = tile0 - tr0 * KT;  // row and column of the stage's first tile
   for (int i = 0; i < nstages; ++i) {
-    const int s = i % S;
-    const uint32_t ph = static_cast<uint32_t>(i / S) & 1u;
-    const int rg = i / kRecGroupStages;
-    const int rslot = rg % kRecSlots;
-    const uint32_t rbase = o_rec + rslot * kRecSlotBytes;
-    if (!RAW && (i & (kRecGroupStages - 1)) == 0 && ok)
-      ok = mbar_wait(&rec_full[rslot], static_cast<uint32_t>(rg / kRecSlots) & 1u);
-    if (ok) ok = mbar_wait(&full[s], ph);
     const int ntl = min(kStageTiles, T - tile0);
+    // This warp's tile's records, read before its weights arrive.
+    int fbi = -1;
+    uint32_t pos = kNoEscape, ex = 0u;
+    if (!RAW) {
+      if (rq == 0 && ok) ok = mbar_wait(&rec_full[rslot], rph);
+      if (jw < ntl) {
+        const uint32_t rb = o_rec + rslot * kRecSlotBytes;
+        const int lt = rq * kStageTiles + jw;
+        fbi = lds_at<int>(sm8, rb + kRecFbOffset + lt * 4);
+        if (lane < kEscapeBudget) {
+          pos = lds_at<uint16_t>(sm8, rb + kRecPosOffset + lt * 32 + lane * 2);
+          ex = lds_at<uint8_t>(sm8, rb + kRecEscOffset + lt * 16 + lane);
+        }
+      }
+    }
+    if (ok) ok = mbar_wait(&full[s], ph);
     // Walk the stage's tiles in order: this warp decodes tile jw; every tile
     // row that ends inside the stage is finished at that point.
     int kt = kt0, tr = tr0;
     for (int j = 0; j < ntl; ++j) {
-      if (j == jw && ok) process_tile(s, kt, rbase, (i & (kRecGroupStages - 1)) * kStageTiles + jw);
+      if (j == jw && ok) process_tile(s, kt, fbi, pos, ex);
       if (kt == KT - 1 || tile0 + j == tend - 1) finish_row(tr);
       if (++kt == KT) {
         kt = 0;
@@ -587,7 +637,18 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
     __syncwarp();
     if (lane == 0) {
       mbar_arrive(&empty[s]);
-      if (!RAW && ((i & (kRecGroupStages - 1)) == kRecGroupStages - 1 || i == nstages - 1)) mbar_arrive(&rec_empty[rslot]);
+      if (!RAW && (rq == kRecGroupStages - 1 || i == nstages - 1)) mbar_arrive(&rec_empty[rslot]);
+    }
+    if (++s == S) {
+      s = 0;
+      ph ^= 1u;
+    }
+    if (++rq == kRecGroupStages) {
+      rq = 0;
+      if (++rslot == kRecSlots) {
+        rslot = 0;
+        rph ^= 1u;
+      }
     }
     tile0 += kStageTiles;
     kt0 += kStageTiles;
@@ -605,7 +666,6 @@ cudaError_t launch_gemv(bool raw, const CUtensorMap& map0, const CUtensorMap& ma
       {{gemv_kernel<1, false, false>, gemv_kernel<1, false, true>}, {gemv_kernel<1, true, false>, gemv_kernel<1, true, true>}},
       {{gemv_kernel<2, false, false>, gemv_kernel<2, false, true>}, {gemv_kernel<2, true, false>, gemv_kernel<2, true, true>}}};
   const Kernel kernel = table[nblocks == 1 ? 0 : 1][raw ? 1 : 0][a.x_resident ? 1 : 0];
-  if (!raw) smem -= kLutBytes;  // the pair table is static shared memory
   cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (err != cudaSuccess) return err;
   cudaLaunchConfig_t cfg = {};

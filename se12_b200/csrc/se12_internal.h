@@ -52,8 +52,6 @@ constexpr int kStageTiles = 4;
 constexpr int kSe12StageWeightBytes = kStageTiles * 6144;
 constexpr int kRawStageWeightBytes = kStageTiles * 8192;
 constexpr int kXRowStride = 576;        // bytes per (tile, batch row) x slice when staged: 512 + 64 pad
-constexpr int kLutCopies = 16;          // pair-table column per lane % 16
-constexpr int kLutBytes = 256 * kLutCopies * 4;
 constexpr int kConsumerWarps = 8;       // warp w: half w % 2 of tile w / 2 of every stage
 constexpr int kProducerWarp = kConsumerWarps;      // TMA / bulk copies
 constexpr int kReducerWarp = kConsumerWarps + 1;   // sums the consumers' row partials
@@ -69,11 +67,12 @@ constexpr int kRecPosOffset = 0;
 constexpr int kRecEscOffset = kRecGroupTiles * 32;
 constexpr int kRecFbOffset = kRecEscOffset + kRecGroupTiles * 16;
 constexpr int kRecSlotBytes = kRecFbOffset + kRecGroupTiles * 4;
-constexpr size_t kCoResidentSmem = 112 * 1024;  // two CTAs (current + next kernel) fit on one SM
+constexpr size_t kCoResidentSmem = 112 * 1024;  // two CTAs fit on one SM
 
-// Bytes per batch row of resident x: K rounded up to 8 elements, then to 128
-// bytes, plus 64 so consecutive rows start in different bank groups.
-__host__ __device__ inline int x_resident_stride(int cols) { return ((cols + 7) / 8 * 16 + 127) / 128 * 128 + 64; }
+// Bytes per batch row of resident x: K rounded up to whole tiles (256
+// columns; the columns past K hold zeros), plus 64 so consecutive rows start
+// in different bank groups.
+__host__ __device__ inline int x_resident_stride(int cols) { return (cols + 255) / 256 * 512 + 64; }
 
 inline size_t x_stage_bytes(int batch) { return ((size_t)kStageTiles * batch * kXRowStride + 127) / 128 * 128; }
 
@@ -81,7 +80,6 @@ inline size_t gemv_smem_bytes(bool raw, bool x_resident, int stages, int batch, 
   size_t per_stage = (raw ? kRawStageWeightBytes : kSe12StageWeightBytes) + (x_resident ? 0 : x_stage_bytes(batch));
   size_t bytes = 1024;                                                  // alignment slack
   bytes += (size_t)stages * per_stage;
-  if (!raw) bytes += kLutBytes;
   if (x_resident) bytes += (size_t)batch * x_resident_stride(cols);
   bytes += 2 * (size_t)kConsumerWarps * 16 * batch * 4;                // two row-reduction buffers
   if (!raw) bytes += (size_t)kRecSlots * kRecSlotBytes;                 // escape records

@@ -211,6 +211,38 @@ def test_fused_gemv_is_deterministic():
         assert torch.equal(m.gemv(x), first)
 
 
+@pytest.mark.parametrize("cols", [300, 1000, 2311])
+def test_fused_gemv_ignores_x_past_cols(cols):
+    """x[b, cols..ldx) may hold anything (NaN here): the result must not see it."""
+    bits, rows, _ = cases.synthetic_weights(48, cols, seed=cols)
+    m = device_matrix(oracle.encode(bits, rows, cols))
+    xb = activations(3, cols, seed=cols)
+    ldx = (cols + 7) // 8 * 8 + 16
+    x = torch.full((3, ldx), float("nan"), dtype=torch.bfloat16, device="cuda")
+    x[:, :cols] = torch.from_numpy(xb.view(np.int16)).view(torch.bfloat16).cuda()
+    y = m.gemv(x[:, :cols]).cpu().numpy()
+    y64 = oracle.gemv_fp64(bits, rows, cols, oracle.bits_to_float32(xb))
+    assert np.isfinite(y).all()
+    assert oracle.max_relative_error(y, y64) <= TOLERANCE
+
+
+def test_fused_gemv_with_infinite_padding_weight():
+    """codebook[0] == 255: the padding weights (+0.0, code 0) would decode to
+    +inf; rows of finite weights must still match the oracle."""
+    rows, cols = 64, 300
+    w = np.random.default_rng(9).normal(0.0, 0.02, size=(rows, cols)).astype(np.float32)
+    w[:40, :] = np.inf  # 12000 of 19200 weights: the most frequent exponent is 255
+    bits = oracle.bf16_round(w).reshape(-1)
+    streams = oracle.encode(bits, rows, cols)
+    assert streams.codebook[0] == 255
+    m = device_matrix(streams)
+    xb = oracle.bf16_round(np.abs(np.random.default_rng(2).normal(0.0, 1.0, size=(2, cols))) + 0.01)
+    y = m.gemv(torch.from_numpy(xb.view(np.int16)).view(torch.bfloat16).cuda()).cpu().numpy()
+    y64 = oracle.gemv_fp64(bits, rows, cols, oracle.bits_to_float32(xb))
+    assert np.isposinf(y[:, :40]).all()
+    assert oracle.max_relative_error(y[:, 40:], y64[:, 40:]) <= TOLERANCE
+
+
 def test_matvec_adapter_interface():
     from se12_b200.format import make_tensor
     from se12_b200.gemv import RawBf16MatVecKernel, Se12MatVecKernel
