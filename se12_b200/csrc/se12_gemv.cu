@@ -623,16 +623,32 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
       }
     }
     if (ok) ok = mbar_wait(&full[s], ph);
-    // Walk the stage's tiles in order: this warp decodes tile jw; every tile
-    // row that ends inside the stage is finished at that point.
-    int kt = kt0, tr = tr0;
-    for (int j = 0; j < ntl; ++j) {
-      if (j == jw && ok) process_tile(s, kt, fbi, pos, ex);
-      if (kt == KT - 1 || tile0 + j == tend - 1) finish_row(tr);
-      if (++kt == KT) {
-        kt = 0;
+    // Tile rows end at stage positions pe, pe + KT, ... (column KT - 1);
+    // the CTA's last tile (position ntl - 1 of its last stage) ends its
+    // last row. This warp finishes the rows that end before its tile jw,
+    // decodes tile jw, then finishes the rows that end at or after it, in
+    // the order of the tile sequence.
+    {
+      int pe = KT - 1 - kt0;  // first row end in this stage
+      int tr = tr0;
+      while (pe < jw && pe < ntl) {
+        finish_row(tr);
         ++tr;
+        pe += KT;
       }
+      if (jw < ntl && ok) {
+        int kt = kt0 + jw;
+        while (kt >= KT) kt -= KT;
+        process_tile(s, kt, fbi, pos, ex);
+      }
+      while (pe < ntl) {
+        finish_row(tr);
+        ++tr;
+        pe += KT;
+      }
+      // pe is now the first row end past the stage: the stage's last tile
+      // ended a row iff pe - KT == ntl - 1
+      if (i == nstages - 1 && pe - KT != ntl - 1) finish_row(tr);
     }
     __syncwarp();
     if (lane == 0) {
