@@ -474,6 +474,21 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
     const uint32_t wst = o_w + s * kWeightBytes;
     const uint32_t xt = XRES ? x_thread + kt * (kTileCols * 2) : x_thread + s * xstage;
     const bool fb = !RAW && fbi >= 0;
+    // The MMAs of this warp's 16 x 128 half: A fragments f0 (row g), f1
+    // (row g + 8), B from x.
+    auto mma_half = [&](const uint32_t (&f0)[4][4], const uint32_t (&f1)[4][4]) {
+#pragma unroll
+      for (int nb = 0; nb < NB; ++nb) {
+        const bool have = nb * 8 + g < B;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          uint4 xv = make_uint4(0, 0, 0, 0);
+          if (have) xv = lds_at<uint4>(sm8, xt + nb * x_nb_step + 64 * k);
+          mma_bf16_16816(acc[k & 1][nb], f0[k][0], f1[k][0], f0[k][1], f1[k][1], xv.x, xv.y);
+          mma_bf16_16816(acc[k & 1][nb], f0[k][2], f1[k][2], f0[k][3], f1[k][3], xv.z, xv.w);
+        }
+      }
+    };
     uint32_t frag0[4][4], frag1[4][4];  // [group][pair]: rows g, g + 8
     if (RAW) {
 #pragma unroll
@@ -493,7 +508,11 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
         frag0[k][0] = v0.x; frag0[k][1] = v0.y; frag0[k][2] = v0.z; frag0[k][3] = v0.w;
         frag1[k][0] = v1.x; frag1[k][1] = v1.y; frag1[k][2] = v1.z; frag1[k][3] = v1.w;
       }
-    } else if (fb) {
+      mma_half(frag0, frag1);
+      return;
+    }
+    if (__builtin_expect(fb, 0)) {
+      // fallback tile: its raw BF16 bits from global memory
       const uint16_t* raw = fbraw_g + static_cast<size_t>(fbi) * kTileSize + 128 * hw + 8 * t;
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
@@ -502,8 +521,11 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
         frag0[k][0] = v0.x; frag0[k][1] = v0.y; frag0[k][2] = v0.z; frag0[k][3] = v0.w;
         frag1[k][0] = v1.x; frag1[k][1] = v1.y; frag1[k][2] = v1.z; frag1[k][3] = v1.w;
       }
-    } else {
-      if (pad_inf && kt == KT - 1) force_padding_escapes(sm8, wst + e_base, e_xor, 128 * hw + 8 * t, K - kt * kTileCols);
+      mma_half(frag0, frag1);
+      return;
+    }
+    if (pad_inf && kt == KT - 1) force_padding_escapes(sm8, wst + e_base, e_xor, 128 * hw + 8 * t, K - kt * kTileCols);
+    {
       uint2 sv0[4], sv1[4];
       uint32_t ev0[4], ev1[4];
 #pragma unroll
@@ -521,21 +543,12 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
         decode8(sv1[k], ev1[k], tab, frag1[k]);
       }
     }
-#pragma unroll
-    for (int nb = 0; nb < NB; ++nb) {
-      const bool have = nb * 8 + g < B;
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        uint4 xv = make_uint4(0, 0, 0, 0);
-        if (have) xv = lds_at<uint4>(sm8, xt + nb * x_nb_step + 64 * k);
-        mma_bf16_16816(acc[k & 1][nb], frag0[k][0], frag1[k][0], frag0[k][1], frag1[k][1], xv.x, xv.y);
-        mma_bf16_16816(acc[k & 1][nb], frag0[k][2], frag1[k][2], frag0[k][3], frag1[k][3], xv.z, xv.w);
-      }
-    }
-    if (!RAW && !fb) {
+    mma_half(frag0, frag1);
+    {
       // Escaped weights of this half: in the MMA with exponent 0 (below
-      // 2^-126 in magnitude), their exact products are added here.
-      const bool mine = (pos != kNoEscape) && (((pos & 255u) >> 7) == static_cast<uint32_t>(hw));
+      // 2^-126 in magnitude), their exact products are added here. Escapes
+      // whose exponent is 0 (zeros and BF16 subnormals) were exact already.
+      const bool mine = (pos != kNoEscape) && ex != 0u && (((pos & 255u) >> 7) == static_cast<uint32_t>(hw));
       unsigned pending = __ballot_sync(0xFFFFFFFFu, mine);
       while (pending) {
         const int e = __ffs(pending) - 1;
