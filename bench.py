@@ -16,9 +16,13 @@ equivalent GB/s (2 bytes per weight) and decode tok/s (GEMVs only).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Under torchrun (N > 1) every rank runs its own replica of the step (weak
-scaling, no collective in the data path); value is the sum over ranks of the
-bytes processed divided by the slowest rank's time.
+Under torchrun (N > 1) every rank streams its own shard: the same step
+structure over distinct weights (weak scaling, no collective in the data
+path); value is the sum over ranks of the bytes processed divided by the
+slowest rank's time.
+
+--impl reference times the reference's CPU path (numpy SE12 decode + fp32
+matmul, the oracle port) on the host cores instead.
 """
 
 from __future__ import annotations
@@ -38,6 +42,13 @@ ROOT = pathlib.Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 METRIC = "SE12 decode+GEMV HBM GB/s (compressed bytes)"
+# DRAM bytes (read + write) per algorithmic byte of the fused GEMV, from one
+# ncu capture of this script's lm_head GEMV (--layers 0: 256000 x 2304,
+# batch 1): 896.71 MB of DRAM traffic for 888.09 MB of SE12 streams + x + y;
+# the difference is the derived escape-position table, the fallback index
+# and the stream-K partials. The step's GEMVs stream the same kinds of data
+# in proportion, so the step's traffic is scaled from it by algorithmic bytes.
+DRAM_BYTES_PER_ALGORITHMIC_BYTE = 896.71 / 888.09
 NOMINAL_HBM_GBS = 8000.0
 
 
@@ -196,11 +207,31 @@ def cpu_baseline_sample(shapes, batch: int, steps: int, warmup: int, seed: int =
         "unit": "GB/s",
         "cores": threads,
         "kind": "port",
-        "sample": f"1 {shapes.name} decoder layer per step (7 matrices, {total_bytes / 1e6:.1f} MB SE12+x+y), "
-        f"numpy decode + fp32 BLAS matmul, {threads} threads (os.cpu_count()={os.cpu_count()}), {steps} steps",
+        "sample": f"{len(host_streams)} {shapes.name} decoder-layer matrices or row bands per step ("
+        + ", ".join(sorted({f"{s.rows}x{s.cols}" for s, _ in host_streams}))
+        + f"; {total_bytes / 1e6:.1f} MB SE12+x+y), numpy decode + fp32 BLAS matmul, {threads} threads "
+        f"(os.cpu_count()={os.cpu_count()}), {steps} steps",
         "seconds_per_step": mean,
         "bytes_per_step": total_bytes,
     }
+
+
+def reference_band_streams(shapes, rows_per_matrix: int, band_rows: int = 64, seed: int = 0):
+    """The first `rows_per_matrix` rows of each of one decoder layer's seven
+    matrices (same weight distribution as the GPU arm), packed by the CPU
+    encoder in bands of `band_rows` rows (one host thread each): the bounded
+    per-step sample of the reference arm."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    sys.path.insert(0, str(ROOT / "tests" / "golden"))
+    import cases
+    import se12_oracle as oracle
+
+    out = []
+    for i, (_, rows, cols, kind) in enumerate(shapes.layer_matrices()):
+        for j in range(0, min(rows, rows_per_matrix), band_rows):
+            bits, r, c = cases.synthetic_weights(band_rows, cols, seed=seed + 100 * i + j)
+            out.append((oracle.encode(bits, r, c), kind))
+    return out
 
 
 def run_reference(args) -> None:
@@ -210,7 +241,11 @@ def run_reference(args) -> None:
     from se12_b200.shapes import CONFIGS
 
     shapes = CONFIGS[args.config]
-    res = cpu_baseline_sample(shapes, args.batch, max(1, args.steps), max(0, args.warmup))
+    # Each step decodes and multiplies a 256-row band of every matrix of one
+    # decoder layer (about 7.5 M weights, ~0.1-0.3 s on the host), so that
+    # --steps K --warmup W ends within a few minutes for the driver's K.
+    bands = reference_band_streams(shapes, 256)
+    res = cpu_baseline_sample(shapes, args.batch, max(1, args.steps), max(0, args.warmup), host_streams=bands)
     line = {
         "impl": "reference",
         "metric": METRIC,
@@ -225,7 +260,8 @@ def run_reference(args) -> None:
         "vs_baseline": None,
         "dtype": "fp32",
         "data": "synthetic",
-        "config": {"workload": f"{shapes.name} decode-step GEMV set, sampled: one decoder layer per step", "batch": args.batch},
+        "config": {"workload": f"{shapes.name} decode-step GEMV set, sampled: 256-row bands of one decoder layer's "
+                   "7 matrices per step", "batch": args.batch},
         "cpu_baseline": {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")},
         "e2e": {"value": res["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -235,7 +271,7 @@ def run_reference(args) -> None:
 # ---------------------------------------------------------------------- GPU leg
 
 
-def build_stack(torch, shapes, batch, device, layers, lm_head, keep_dense):
+def build_stack(torch, shapes, batch, device, layers, lm_head, keep_dense, seed_offset=0):
     from se12_b200.codec import encode_device
 
     mats, dense = [], []
@@ -247,7 +283,7 @@ def build_stack(torch, shapes, batch, device, layers, lm_head, keep_dense):
         name, rows, cols, kind = shapes.lm_head()
         specs.append((name, rows, cols, kind, 999_999))
     for name, rows, cols, kind, seed in specs:
-        w = synthetic_bf16(torch, rows, cols, seed, device)
+        w = synthetic_bf16(torch, rows, cols, seed + seed_offset, device)
         m = encode_device(w)
         mats.append((name, m, kind))
         dense.append(w if keep_dense else None)
@@ -307,7 +343,10 @@ def run_ours(args) -> None:
     layers = args.layers if args.layers is not None else shapes.layers
     batch = args.batch
     t_setup = time.perf_counter()
-    mats, dense = build_stack(torch, shapes, batch, device, layers, not args.no_lm_head, keep_dense=not args.no_dense)
+    # N > 1: each rank streams its own shard of an N-times larger set of
+    # matrices (distinct seeds per rank): weak scaling, no collective.
+    mats, dense = build_stack(torch, shapes, batch, device, layers, not args.no_lm_head, keep_dense=not args.no_dense,
+                              seed_offset=rank * 10_000_000)
     setup_s = time.perf_counter() - t_setup
 
     gen = torch.Generator(device=device)
@@ -474,7 +513,8 @@ def run_ours(args) -> None:
                 "bytes_per_step": bytes_per_step,
                 "l2": "inputs larger than L2 (every step streams all SE12 bytes once)",
                 "graph": "one CUDA graph per step, programmatic dependent launch between GEMVs",
-                "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                "parallelism": f"sharded x{world}: every rank streams its own full step of distinct weights, "
+                "no collective" if world > 1 else "single GPU",
                 "setup_seconds": setup_s,
             },
             "bf16_equiv_gbs": world * (2 * weights + batch * sum(m.cols * 2 + m.rows * 4 for _, m, _ in mats)) / (ms_per_step * 1e-3) / 1e9,
@@ -487,8 +527,9 @@ def run_ours(args) -> None:
                 "peak": peak,
                 "unit": "GB/s",
                 "frac": achieved / peak,
-                "traffic": None,
-                "kernel": "se12::gemv_kernel<1,false> (all 183 launches of the step)",
+                "traffic": bytes_per_step * DRAM_BYTES_PER_ALGORITHMIC_BYTE,
+                "traffic_unit": "bytes per step (all launches), scaled from the ncu capture of the lm_head GEMV",
+                "kernel": f"se12::gemv_kernel<{1 if batch <= 8 else 2},SE12,x resident> (all {len(mats)} launches of the step)",
                 "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)" if "source" not in peaks else "fallback",
             },
             "cpu_baseline": cpu,
