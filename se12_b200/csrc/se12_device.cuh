@@ -126,6 +126,16 @@ __device__ __forceinline__ int atomic_add_acq_rel_cta(int* counter, int v) {
   return old;
 }
 
+// Atomic add on a global counter with acquire-release semantics at GPU
+// scope: publishes the calling thread's earlier writes (and, through a
+// preceding __syncwarp, its warp's) to whoever acquires a later value, and
+// makes writes published by earlier adders visible to the caller.
+__device__ __forceinline__ int atomic_add_acq_rel_gpu(int* counter, int v) {
+  int old;
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(counter), "r"(v) : "memory");
+  return old;
+}
+
 // ------------------------------------------------------------------ L2 policy
 
 __device__ __forceinline__ uint64_t policy_evict_first() {

@@ -111,8 +111,8 @@ __device__ __forceinline__ void decode8(uint2 s, uint32_t e, const uint32_t (&ta
 // codebook[0] == 255 (an infinite padding weight). For that case this
 // rewrites, in shared memory, the codes of this thread's padding weights to
 // the escape code, which decodes to +0. Each thread patches only the ec
-// words it reads itself.
-__device__ __forceinline__ void force_padding_escapes(uint8_t* sm8, uint32_t e_addr, uint32_t e_xor, int col0, int valid) {
+// words it reads itself. Out of line: only such matrices call it.
+__device__ __noinline__ void force_padding_escapes(uint8_t* sm8, uint32_t e_addr, uint32_t e_xor, int col0, int valid) {
 #pragma unroll
   for (int r = 0; r < 2; ++r)
 #pragma unroll
@@ -391,15 +391,16 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
       __syncwarp();
       if (lane == 0) mbar_arrive(&redfree[pb]);
       if (whole) continue;
-      __threadfence();
-      __syncwarp();
+      // Publish this CTA's partial (the warp's stores, ordered by the
+      // __syncwarp before lane 0's release); the contributor that arrives
+      // last acquires everyone's and sums them.
       const int c_lo = tile_owner(tr * KT, units, G);
       const int c_hi = tile_owner((tr + 1) * KT - 1, units, G);
       int lastcta = 0;
-      if (lane == 0) lastcta = (atomicAdd(&counters[tr], 1) == c_hi - c_lo);
+      if (lane == 0) lastcta = (atomic_add_acq_rel_gpu(&counters[tr], 1) == c_hi - c_lo);
       lastcta = __shfl_sync(0xFFFFFFFFu, lastcta, 0);
       if (!lastcta) continue;
-      __threadfence();
+      __syncwarp();
       for (int idx = lane; idx < outs; idx += 32) {
         const int row = idx & 15, b = idx >> 4;
         float v = 0.f;
@@ -524,7 +525,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
       mma_half(frag0, frag1);
       return;
     }
-    if (pad_inf && kt == KT - 1) force_padding_escapes(sm8, wst + e_base, e_xor, 128 * hw + 8 * t, K - kt * kTileCols);
+    if (__builtin_expect(pad_inf, 0) && kt == KT - 1) force_padding_escapes(sm8, wst + e_base, e_xor, 128 * hw + 8 * t, K - kt * kTileCols);
     {
       uint2 sv0[4], sv1[4];
       uint32_t ev0[4], ev1[4];
