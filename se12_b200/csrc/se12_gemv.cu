@@ -457,9 +457,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
                                  : o_x + (jw * B + g) * kXRowStride + (128 * hw + 8 * t) * 2;
   const uint32_t x_nb_step = XRES ? 8 * xrs : 8 * kXRowStride;
 
-  grid_dependency_wait();
   bool ok = true;
-  if (XRES) ok = mbar_wait((K & 7) ? xready : xbar, 0);
 
   // two independent accumulator sets (column groups 0, 2 and 1, 3)
   float acc[2][NB][4];
@@ -468,29 +466,15 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
 #pragma unroll
     for (int nb = 0; nb < NB; ++nb) acc[h][nb][0] = acc[h][nb][1] = acc[h][nb][2] = acc[h][nb][3] = 0.f;
 
-  // Adds this warp's share of its tile of stage s (tile column kt) to acc.
-  // fbi: the tile's fallback index (-1: SE12 tile); lanes 0..15 hold its
-  // escape positions (pos) and exponents (ex).
-  auto process_tile = [&](int s, int kt, int fbi, uint32_t pos, uint32_t ex) {
+  // This warp's A fragments (rows g and g + 8, its 128 columns) of its
+  // current tile: [group k][pair].
+  uint32_t frag0[4][4], frag1[4][4];
+
+  // Fills frag0 / frag1 with this warp's half of its tile of stage s:
+  // decoded SE12 weights, the raw bits of a fallback tile (fbi >= 0), or
+  // dense BF16 weights. Needs no x, so it may run before the dependency wait.
+  auto load_frags = [&](int s, int kt, int fbi) {
     const uint32_t wst = o_w + s * kWeightBytes;
-    const uint32_t xt = XRES ? x_thread + kt * (kTileCols * 2) : x_thread + s * xstage;
-    const bool fb = !RAW && fbi >= 0;
-    // The MMAs of this warp's 16 x 128 half: A fragments f0 (row g), f1
-    // (row g + 8), B from x.
-    auto mma_half = [&](const uint32_t (&f0)[4][4], const uint32_t (&f1)[4][4]) {
-#pragma unroll
-      for (int nb = 0; nb < NB; ++nb) {
-        const bool have = nb * 8 + g < B;
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          uint4 xv = make_uint4(0, 0, 0, 0);
-          if (have) xv = lds_at<uint4>(sm8, xt + nb * x_nb_step + 64 * k);
-          mma_bf16_16816(acc[k & 1][nb], f0[k][0], f1[k][0], f0[k][1], f1[k][1], xv.x, xv.y);
-          mma_bf16_16816(acc[k & 1][nb], f0[k][2], f1[k][2], f0[k][3], f1[k][3], xv.z, xv.w);
-        }
-      }
-    };
-    uint32_t frag0[4][4], frag1[4][4];  // [group][pair]: rows g, g + 8
     if (RAW) {
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
@@ -509,10 +493,9 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
         frag0[k][0] = v0.x; frag0[k][1] = v0.y; frag0[k][2] = v0.z; frag0[k][3] = v0.w;
         frag1[k][0] = v1.x; frag1[k][1] = v1.y; frag1[k][2] = v1.z; frag1[k][3] = v1.w;
       }
-      mma_half(frag0, frag1);
       return;
     }
-    if (__builtin_expect(fb, 0)) {
+    if (__builtin_expect(fbi >= 0, 0)) {
       // fallback tile: its raw BF16 bits from global memory
       const uint16_t* raw = fbraw_g + static_cast<size_t>(fbi) * kTileSize + 128 * hw + 8 * t;
 #pragma unroll
@@ -522,7 +505,6 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
         frag0[k][0] = v0.x; frag0[k][1] = v0.y; frag0[k][2] = v0.z; frag0[k][3] = v0.w;
         frag1[k][0] = v1.x; frag1[k][1] = v1.y; frag1[k][2] = v1.z; frag1[k][3] = v1.w;
       }
-      mma_half(frag0, frag1);
       return;
     }
     if (__builtin_expect(pad_inf, 0) && kt == KT - 1) force_padding_escapes(sm8, wst + e_base, e_xor, 128 * hw + 8 * t, K - kt * kTileCols);
@@ -544,7 +526,28 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
         decode8(sv1[k], ev1[k], tab, frag1[k]);
       }
     }
-    mma_half(frag0, frag1);
+  };
+
+  // Multiplies the fragments with x (tile column kt of stage s) into acc,
+  // then adds the exact products of this half's escaped weights (records
+  // fbi, pos, ex).
+  auto mma_tile = [&](int s, int kt, int fbi, uint32_t pos, uint32_t ex) {
+    const uint32_t wst = o_w + s * kWeightBytes;
+    const uint32_t xt = XRES ? x_thread + kt * (kTileCols * 2) : x_thread + s * xstage;
+    {
+#pragma unroll
+      for (int nb = 0; nb < NB; ++nb) {
+        const bool have = nb * 8 + g < B;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          uint4 xv = make_uint4(0, 0, 0, 0);
+          if (have) xv = lds_at<uint4>(sm8, xt + nb * x_nb_step + 64 * k);
+          mma_bf16_16816(acc[k & 1][nb], frag0[k][0], frag1[k][0], frag0[k][1], frag1[k][1], xv.x, xv.y);
+          mma_bf16_16816(acc[k & 1][nb], frag0[k][2], frag1[k][2], frag0[k][3], frag1[k][3], xv.z, xv.w);
+        }
+      }
+    }
+    if (RAW || fbi >= 0) return;
     {
       // Escaped weights of this half: in the MMA with exponent 0 (below
       // 2^-126 in magnitude), their exact products are added here. Escapes
@@ -619,11 +622,17 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
   uint32_t rph = 0u;         // parity of the record slot's phase
   int tile0 = u0 * kStageTiles;
   int tr0 = tile0 / KT, kt0 = tile0 - tr0 * KT;  // row and column of the stage's first tile
-  for (int i = 0; i < nstages; ++i) {
-    const int ntl = min(kStageTiles, T - tile0);
-    // This warp's tile's records, read before its weights arrive.
-    int fbi = -1;
-    uint32_t pos = kNoEscape, ex = 0u;
+  // The current stage's tile count, this warp's tile column and records.
+  int ntl = 0, kt_mine = 0, fbi = -1;
+  uint32_t pos = kNoEscape, ex = 0u;
+
+  // Waits for stage i's records and weights and decodes this warp's tile
+  // of it into frag0 / frag1.
+  auto fetch_stage = [&]() {
+    ntl = min(kStageTiles, T - tile0);
+    fbi = -1;
+    pos = kNoEscape;
+    ex = 0u;
     if (!RAW) {
       if (rq == 0 && ok) ok = mbar_wait(&rec_full[rslot], rph);
       if (jw < ntl) {
@@ -637,11 +646,24 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
       }
     }
     if (ok) ok = mbar_wait(&full[s], ph);
+    kt_mine = kt0 + jw;
+    while (kt_mine >= KT) kt_mine -= KT;
+    if (jw < ntl && ok) load_frags(s, kt_mine, fbi);
+  };
+
+  // The weights do not depend on the previous kernel in the stream: decode
+  // this warp's first tile while that kernel finishes, then wait for it
+  // (griddepcontrol.wait) before touching x, y or the workspace.
+  if (nstages > 0) fetch_stage();
+  grid_dependency_wait();
+  if (XRES && !mbar_wait((K & 7) ? xready : xbar, 0)) ok = false;
+
+  for (int i = 0; i < nstages; ++i) {
     // Tile rows end at stage positions pe, pe + KT, ... (column KT - 1);
     // the CTA's last tile (position ntl - 1 of its last stage) ends its
     // last row. This warp finishes the rows that end before its tile jw,
-    // decodes tile jw, then finishes the rows that end at or after it, in
-    // the order of the tile sequence.
+    // multiplies tile jw, then finishes the rows that end at or after it,
+    // in the order of the tile sequence.
     {
       int pe = KT - 1 - kt0;  // first row end in this stage
       int tr = tr0;
@@ -650,11 +672,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
         ++tr;
         pe += KT;
       }
-      if (jw < ntl && ok) {
-        int kt = kt0 + jw;
-        while (kt >= KT) kt -= KT;
-        process_tile(s, kt, fbi, pos, ex);
-      }
+      if (jw < ntl && ok) mma_tile(s, kt_mine, fbi, pos, ex);
       while (pe < ntl) {
         finish_row(tr);
         ++tr;
@@ -686,6 +704,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
       kt0 -= KT;
       ++tr0;
     }
+    if (i + 1 < nstages) fetch_stage();
   }
 }
 
