@@ -129,22 +129,31 @@ struct LaunchConfig {
 LaunchConfig choose_config(bool raw, int tiles, int cols, int batch, int sm_count) {
   LaunchConfig c{};
   c.nblocks = batch <= 8 ? 1 : 2;
-  // candidates in order of preference: (x resident?, stages)
+  // candidates in order of preference: (x resident?, stages); first those
+  // that let two CTAs share an SM, else the best one for one CTA per SM
   static const int kCandidates[][2] = {{1, 4}, {1, 3}, {0, 4}, {0, 3}, {1, 2}, {0, 2}};
-  c.x_resident = 0;
-  c.stages = 2;
-  for (const auto& cand : kCandidates) {
-    if (se12::gemv_smem_bytes(raw, cand[0] != 0, cand[1], batch, cols) <= se12::kCoResidentSmem) {
-      c.x_resident = cand[0];
-      c.stages = cand[1];
-      break;
+  int per_sm = 0;
+  for (const size_t limit : {se12::kCoResidentSmem, se12::kMaxSmemPerCta}) {
+    for (const auto& cand : kCandidates) {
+      if (se12::gemv_smem_bytes(raw, cand[0] != 0, cand[1], batch, cols) <= limit) {
+        c.x_resident = cand[0];
+        c.stages = cand[1];
+        per_sm = (limit == se12::kCoResidentSmem) ? 2 : 1;
+        break;
+      }
     }
+    if (per_sm) break;
+  }
+  if (!per_sm) {  // not reached for batch <= 16: staged x with 2 stages fits one CTA per SM
+    c.x_resident = 0;
+    c.stages = 2;
+    per_sm = 1;
   }
   c.smem = se12::gemv_smem_bytes(raw, c.x_resident != 0, c.stages, batch, cols);
   const int units = (tiles + se12::kStageTiles - 1) / se12::kStageTiles;
-  // two CTAs per SM: shared memory and registers allow it, and the second
-  // CTA's warps hide the first one's decode and barrier latencies
-  c.grid = std::max(1, std::min(units, 2 * sm_count));
+  // two CTAs per SM when they fit: the second CTA's warps hide the first
+  // one's decode and barrier latencies
+  c.grid = std::max(1, std::min(units, per_sm * sm_count));
   return c;
 }
 

@@ -68,6 +68,7 @@ constexpr int kRecEscOffset = kRecGroupTiles * 32;
 constexpr int kRecFbOffset = kRecEscOffset + kRecGroupTiles * 16;
 constexpr int kRecSlotBytes = kRecFbOffset + kRecGroupTiles * 4;
 constexpr size_t kCoResidentSmem = 112 * 1024;  // two CTAs fit on one SM
+constexpr size_t kMaxSmemPerCta = 227 * 1024;   // one CTA per SM (sm_100 opt-in maximum)
 
 // Bytes per batch row of resident x: K rounded up to whole tiles (256
 // columns; the columns past K hold zeros), plus 64 so consecutive rows start
