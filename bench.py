@@ -65,6 +65,8 @@ def parse_args():
     p.add_argument("--no-dense", action="store_true", help="skip the dense BF16 comparisons")
     p.add_argument("--layers", type=int, default=None, help="override the layer count (profiling small cases)")
     p.add_argument("--no-lm-head", action="store_true")
+    p.add_argument("--tp", action="store_true",
+                   help="tensor-parallel decode step over the torchrun ranks (default config gemma2-27b)")
     return p.parse_args()
 
 
@@ -546,10 +548,143 @@ def run_ours(args) -> None:
         torch.distributed.destroy_process_group()
 
 
+def run_tp(args) -> None:
+    """Tensor-parallel decode step (SURVEY configs 2-4): every rank holds
+    its Megatron shards of every matrix -- q/k/v/gate/up by output rows, o
+    and down by input columns followed by an NCCL all-reduce of the fp32
+    partial sums, the LM head by rows followed by an all-gather of the
+    logits -- and replays one CUDA graph of the step's GEMVs and
+    collectives. value = the full model's SE12 bytes (all ranks' shards) per
+    step / the slowest rank's step time: strong scaling at a fixed model."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    world, rank, local = dist_info()
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if world > 1:
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+    from se12_b200 import _build
+    from se12_b200.codec import encode_device
+    from se12_b200.device import device_status, gemv_call
+    from se12_b200.shapes import CONFIGS
+    from se12_b200.sharding import col_range, megatron_plan, row_range
+
+    if rank == 0:
+        _build.build()
+    if world > 1:
+        dist.barrier()
+    shapes = CONFIGS[args.config if args.config != "gemma2-2b" else "gemma2-27b"]
+    layers = args.layers if args.layers is not None else shapes.layers
+    batch = args.batch
+    specs = []
+    for layer in range(layers):
+        for j, (name, rows, cols, kind) in enumerate(shapes.layer_matrices()):
+            specs.append((name, rows, cols, kind, 1000 * layer + j))
+    if not args.no_lm_head:
+        name, rows, cols, kind = shapes.lm_head()
+        specs.append((name, rows, cols, kind, 999_999))
+    t_setup = time.perf_counter()
+    gen = torch.Generator(device=device)
+    gen.manual_seed(1)
+    x_full = torch.randn(batch, shapes.hidden, generator=gen, device=device).to(torch.bfloat16)
+    ops = []  # (matrix, x, y, collective) in step order
+    local_bytes = 0
+    for name, rows, cols, kind, seed in specs:
+        plan = megatron_plan(name)
+        if plan == "rows":
+            r0, r1 = row_range(rows, world, rank)
+            w = synthetic_bf16(torch, r1 - r0, cols, seed * 64 + rank, device)
+            x = x_full
+        else:
+            c0, c1 = col_range(cols, world, rank)
+            w = synthetic_bf16(torch, rows, c1 - c0, seed * 64 + rank, device)
+            x = torch.randn(batch, c1 - c0, generator=gen, device=device).to(torch.bfloat16)
+        m = encode_device(w)
+        del w
+        y = torch.empty(batch, m.rows, dtype=torch.float32, device=device)
+        coll = "all_reduce" if plan == "cols" else ("all_gather" if name == "lm_head" else None)
+        ops.append((m, x, y, coll))
+        local_bytes += m.byte_size + batch * m.cols * 2 + batch * m.rows * 4
+    torch.cuda.synchronize()
+    setup_s = time.perf_counter() - t_setup
+    lm_rows = ops[-1][2].shape[1] if not args.no_lm_head else 0
+    logits = torch.empty(world, batch, lm_rows, dtype=torch.float32, device=device) if lm_rows else None
+
+    def step():
+        for m, x, y, coll in ops:
+            gemv_call(m, x, y)
+            if world > 1 and coll == "all_reduce":
+                dist.all_reduce(y)
+            elif world > 1 and coll == "all_gather":
+                dist.all_gather_into_tensor(logits, y)
+
+    stream = torch.cuda.Stream(device)
+    stream.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(stream):
+        step()
+    stream.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step()
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with sampler:
+        e0.record()  # replay() launches on the current stream
+        for _ in range(args.steps):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+    elapsed = e0.elapsed_time(e1)
+    total_bytes = torch.tensor([float(local_bytes)], device=device, dtype=torch.float64)
+    t = torch.tensor([elapsed], device=device, dtype=torch.float64)
+    if world > 1:
+        dist.barrier()
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.all_reduce(total_bytes)
+    ms = float(t.item()) / args.steps
+    status = device_status()
+    if status:
+        raise RuntimeError(f"device status word is {status}: a kernel reported an error")
+    if rank == 0:
+        value = float(total_bytes.item()) / (ms * 1e-3) / 1e9
+        weights = layers * shapes.weights_per_layer + (0 if args.no_lm_head else shapes.vocab * shapes.hidden)
+        line = {
+            "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic",
+            "config": {"workload": f"{shapes.name} tensor-parallel decode-step GEMV set: {layers} layers x 7 + lm_head, "
+                       f"batch {batch}", "batch": batch, "weights": weights,
+                       "bytes_per_step": float(total_bytes.item()),
+                       "parallelism": f"tp{world}: q/k/v/gate/up by rows, o/down by columns + NCCL all-reduce, "
+                       "lm_head by rows + all-gather; one CUDA graph per step", "setup_seconds": setup_s},
+            "tok_s": batch / (ms * 1e-3),
+            "per_gpu_gbs": value / world,
+            "collectives_per_step": (2 * layers + (0 if args.no_lm_head else 1)) if world > 1 else 0,
+            "clocks": sampler.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    del graph
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     args = parse_args()
     if args.impl == "reference":
         run_reference(args)
+    elif args.tp:
+        run_tp(args)
     else:
         run_ours(args)
 
