@@ -118,16 +118,17 @@ int se12_gemv(const se12_matrix* m, const uint16_t* x_dev, int batch, int ldx, f
  * cudaMalloc fails), or a binding that holds no device buffer it could keep
  * alive and zeroed between calls. It has no counterpart in the reference.
  * Same arguments, result and errors as se12_gemv, except:
- *  - The scratch is a fixed 896 KiB array in the library's device image,
- *    held by every GPU that loads the library until the process exits. It
- *    limits the matrix to 65536 tile rows (1,048,576 rows) and the launch to
- *    320 CTAs (two per SM on up to 160 SMs); larger requests return SE12_ERR_INVALID_ARGUMENT or
- *    SE12_ERR_UNSUPPORTED_DEVICE with a message, and launch nothing.
+ *  - The scratch is a fixed 644 KiB array in the library's device image,
+ *    held by every GPU that loads the library until the process exits: the
+ *    partial rows and flags of up to 320 CTAs (two per SM on up to 160
+ *    SMs). A launch that would need more returns SE12_ERR_UNSUPPORTED_DEVICE,
+ *    and a batch above SE12_MAX_BATCH SE12_ERR_INVALID_ARGUMENT, each with a
+ *    message and without launching anything. Matrix size is not limited.
  *  - The current device must be the matrix's device. The first call on a
  *    device looks up the scratch's address (cudaGetSymbolAddress); make that
  *    first call before any stream capture.
- *  - Every call clears the scratch's arrival counters on `stream`
- *    (cudaMemsetAsync) and then launches the GEMV; it allocates nothing.
+ *  - Every call clears the scratch's flags on `stream` (cudaMemsetAsync)
+ *    and then launches the GEMV; it allocates nothing.
  *  - All calls on a device share the one scratch, which keeps the last
  *    call's contents: calls that can overlap on the GPU (on different
  *    streams without ordering between them) race and give wrong results.

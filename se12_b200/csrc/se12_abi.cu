@@ -158,14 +158,14 @@ LaunchConfig choose_config(bool raw, int tiles, int cols, int batch, int sm_coun
 }
 
 // Workspace layout, identical for every matrix so that all calls on one
-// stream can share one workspace: [partials][counters]. The partials region
+// stream can share one workspace: [partials][flags]. The partials region
 // has a fixed size (the largest grid and batch: 2 CTAs per SM, 2 slots of
-// 16 rows x 16 batch columns each), the arrival counters (one int per tile
-// row, zero between calls) follow it.
+// 16 rows x 16 batch columns each); the flags (one int per CTA, "partial
+// published", zero between calls) follow it.
 size_t partials_region_bytes(int sm_count) { return static_cast<size_t>(2 * sm_count) * 2 * 16 * 16 * 4; }
 
-size_t workspace_bytes_for(int tile_rows, int sm_count) {
-  return partials_region_bytes(sm_count) + (static_cast<size_t>(tile_rows) * 4 + 255) / 256 * 256;
+size_t workspace_bytes_for(int /*tile_rows*/, int sm_count) {
+  return partials_region_bytes(sm_count) + (static_cast<size_t>(2 * sm_count) * 4 + 255) / 256 * 256;
 }
 
 }  // namespace
@@ -311,14 +311,12 @@ int se12_gemv(const se12_matrix* m, const uint16_t* x, int batch, int ldx, float
 // ------------------------------------------------------------------ no-allocation GEMV
 // Scratch of se12_gemv_noalloc, for callers that cannot allocate device
 // memory: the stream-K partial rows of up to kNoAllocMaxGrid CTAs, then one
-// arrival counter per tile row for up to kNoAllocMaxTileRows tile rows. It
-// is part of the library's device image, so every GPU that loads the
-// library holds these 896 KiB until the process exits.
+// flag per CTA. It is part of the library's device image, so every GPU that
+// loads the library holds these 644 KiB until the process exits.
 namespace {
 constexpr int kNoAllocMaxGrid = 320;
-constexpr int kNoAllocMaxTileRows = 65536;
 constexpr size_t kNoAllocPartialsBytes = static_cast<size_t>(kNoAllocMaxGrid) * 2 * 16 * 16 * sizeof(float);
-constexpr size_t kNoAllocScratchBytes = kNoAllocPartialsBytes + static_cast<size_t>(kNoAllocMaxTileRows) * sizeof(int);
+constexpr size_t kNoAllocScratchBytes = kNoAllocPartialsBytes + 4096;  // + kNoAllocMaxGrid flags, padded
 constexpr int kNoAllocMaxDevices = 64;
 
 std::mutex g_noalloc_mutex;
@@ -355,11 +353,6 @@ int se12_gemv_noalloc(const se12_matrix* m, const uint16_t* x, int batch, int ld
   if (device != m->device)
     return fail(SE12_ERR_INVALID_ARGUMENT, "se12_gemv_noalloc: the current device (" + std::to_string(device) +
                                                ") is not the matrix's device (" + std::to_string(m->device) + ")");
-  if (m->view.tile_rows > kNoAllocMaxTileRows)
-    return fail(SE12_ERR_INVALID_ARGUMENT,
-                "se12_gemv_noalloc supports at most " + std::to_string(kNoAllocMaxTileRows * SE12_TILE_ROWS) +
-                    " rows (" + std::to_string(kNoAllocMaxTileRows) + " tile rows), got " +
-                    std::to_string(m->view.rows) + "; use se12_gemv with a workspace");
   const LaunchConfig c = choose_config(false, m->view.tiles, m->view.cols, batch, m->sm_count);
   if (c.grid > kNoAllocMaxGrid)
     return fail(SE12_ERR_UNSUPPORTED_DEVICE, "se12_gemv_noalloc supports grids of at most " +
@@ -369,10 +362,10 @@ int se12_gemv_noalloc(const se12_matrix* m, const uint16_t* x, int batch, int ld
   st = noalloc_scratch(device, &scratch);
   if (st != SE12_OK) return st;
   int* counters = reinterpret_cast<int*>(static_cast<char*>(scratch) + kNoAllocPartialsBytes);
-  // The counters must start at zero; a completed call leaves them at zero,
-  // but clearing them here also recovers from a call that did not complete.
-  err = cudaMemsetAsync(counters, 0, static_cast<size_t>(m->view.tile_rows) * sizeof(int),
-                        static_cast<cudaStream_t>(stream));
+  // The per-CTA flags must start at zero; a completed call leaves them at
+  // zero, but clearing them here also recovers from a call that did not
+  // complete.
+  err = cudaMemsetAsync(counters, 0, static_cast<size_t>(c.grid) * sizeof(int), static_cast<cudaStream_t>(stream));
   if (err != cudaSuccess) return cuda_fail(err, "cudaMemsetAsync of the se12_gemv_noalloc counters");
   se12::GemvArgs a{};
   a.m = m->view;

@@ -136,6 +136,32 @@ __device__ __forceinline__ int atomic_add_acq_rel_gpu(int* counter, int v) {
   return old;
 }
 
+// Release store / acquire load of a flag in global memory at GPU scope.
+__device__ __forceinline__ void st_release_gpu(int* flag, int v) {
+  asm volatile("st.release.gpu.global.s32 [%0], %1;" ::"l"(flag), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ int ld_acquire_gpu(const int* flag) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
+  return v;
+}
+
+// Waits until *flag is non-zero (acquiring what its writer released).
+// Returns false (and raises kStatusWaitTimeout) after kWaitLimitNs.
+__device__ __forceinline__ bool wait_flag_gpu(const int* flag) {
+  if (ld_acquire_gpu(flag)) return true;
+  const unsigned long long start = global_ns();
+  while (!ld_acquire_gpu(flag)) {
+    __nanosleep(64);
+    if (global_ns() - start > kWaitLimitNs) {
+      raise_status(kStatusWaitTimeout);
+      return false;
+    }
+  }
+  return true;
+}
+
 // ------------------------------------------------------------------ L2 policy
 
 __device__ __forceinline__ uint64_t policy_evict_first() {

@@ -361,58 +361,85 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
   if (warp == kReducerWarp) {
     // ------------------------------------------------------------ reducer
     // Tile rows tr_first .. tr_last end in this CTA, in order. For each: wait
-    // for the eight consumer warps' partials, sum them in warp order, and
-    // write the row of y, or, for a row shared with other CTAs, this CTA's
-    // partial; the row's last contributor then sums all contributors'
-    // partials in CTA order (deterministic, no floating-point atomics).
+    // for the eight consumer warps' partials and sum them in warp order.
+    //  * A row entirely in this CTA: write it to y.
+    //  * A row that started in an earlier CTA (only this CTA's first row):
+    //    publish the sum (partials slot 0) with a release flag.
+    //  * A row that started here and continues into later CTAs (only this
+    //    CTA's last row, which it reaches last): acquire the later CTAs'
+    //    flags -- they processed the row first, at the start of their runs
+    //    -- add their partials in CTA order, write y and clear the flags.
+    // Deterministic (CTA order), no atomics. Every CTA of the grid is
+    // resident or done before a dependent grid may launch, so the flag
+    // waits cannot be starved; they are bounded all the same.
     if (tend <= tstart) return;
     const int tr_last = (tend - 1) / KT;
-    const int outs = 16 * B;
-    grid_dependency_wait();  // y may be read by the previous kernel in the stream
+    const int outs = 16 * B;  // <= 256: up to 8 values per lane
+    grid_dependency_wait();   // y and the workspace may be in use by the previous kernel
     for (int tr = tr_first; tr <= tr_last; ++tr) {
       const int lr = tr - tr_first, pb = lr & 1;
       if (!mbar_wait(&deposited[pb], static_cast<uint32_t>(lr >> 1) & 1u)) break;
       const float* buf = red + pb * kConsumerWarps * 16 * B;
-      const bool whole = (tr * KT >= tstart) && ((tr + 1) * KT <= tend);
-      const int slot = (tr == tr_first) ? 0 : 1;
-      float* part = partials + (static_cast<size_t>(blockIdx.x) * 2 + slot) * (16 * 16);
-      for (int idx = lane; idx < outs; idx += 32) {
-        const int row = idx / B, b = idx - row * B;
-        float v = 0.f;
+      float v[8];
 #pragma unroll
-        for (int ww = 0; ww < kConsumerWarps; ++ww) v += buf[ww * 16 * B + idx];
-        if (whole) {
-          const int grow = tr * kTileRows + row;
-          if (grow < N) yg[static_cast<size_t>(b) * ldy + grow] = v;
-        } else {
-          part[b * 16 + row] = v;
+      for (int j = 0; j < 8; ++j) {
+        const int idx = lane + 32 * j;
+        v[j] = 0.f;
+        if (idx < outs) {
+#pragma unroll
+          for (int ww = 0; ww < kConsumerWarps; ++ww) v[j] += buf[ww * 16 * B + idx];
         }
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&redfree[pb]);
-      if (whole) continue;
-      // Publish this CTA's partial (the warp's stores, ordered by the
-      // __syncwarp before lane 0's release); the contributor that arrives
-      // last acquires everyone's and sums them.
-      const int c_lo = tile_owner(tr * KT, units, G);
-      const int c_hi = tile_owner((tr + 1) * KT - 1, units, G);
-      int lastcta = 0;
-      if (lane == 0) lastcta = (atomic_add_acq_rel_gpu(&counters[tr], 1) == c_hi - c_lo);
-      lastcta = __shfl_sync(0xFFFFFFFFu, lastcta, 0);
-      if (!lastcta) continue;
-      __syncwarp();
-      for (int idx = lane; idx < outs; idx += 32) {
-        const int row = idx & 15, b = idx >> 4;
-        float v = 0.f;
-        for (int c = c_lo; c <= c_hi; ++c) {
-          const int cslot = (tile_start(c, units, G, T) / KT == tr) ? 0 : 1;
-          v += __ldcg(partials + (static_cast<size_t>(c) * 2 + cslot) * (16 * 16) + b * 16 + row);
+      const bool starts = tr * KT >= tstart;
+      const bool ends = (tr + 1) * KT <= tend;
+      if (!starts) {
+        // contributor: publish this CTA's partial of the row
+        float* part = partials + static_cast<size_t>(blockIdx.x) * 2 * (16 * 16);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int idx = lane + 32 * j;
+          if (idx < outs) {
+            const int row = idx / B, b = idx - row * B;
+            part[b * 16 + row] = v[j];
+          }
         }
-        const int grow = tr * kTileRows + row;
-        if (grow < N) yg[static_cast<size_t>(b) * ldy + grow] = v;
+        __syncwarp();
+        if (lane == 0) st_release_gpu(&counters[blockIdx.x], 1);
+        continue;
       }
-      __syncwarp();
-      if (lane == 0) counters[tr] = 0;
+      bool good = true;
+      int c_hi = blockIdx.x;
+      if (!ends) {
+        // finisher: add the later contributors' partials, in CTA order
+        c_hi = tile_owner((tr + 1) * KT - 1, units, G);
+        for (int c = blockIdx.x + 1 + lane; c <= c_hi; c += 32) good = wait_flag_gpu(&counters[c]) && good;
+        good = __all_sync(0xFFFFFFFFu, good);
+        __syncwarp();
+        for (int c = blockIdx.x + 1; c <= c_hi; ++c) {
+          const float* part = partials + static_cast<size_t>(c) * 2 * (16 * 16);
+          float p[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const int idx = lane + 32 * j;
+            const int row = idx / B, b = idx - row * B;
+            p[j] = (idx < outs) ? __ldcg(part + b * 16 + row) : 0.f;
+          }
+#pragma unroll
+          for (int j = 0; j < 8; ++j) v[j] += p[j];
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int idx = lane + 32 * j;
+        if (idx < outs) {
+          const int row = idx / B, b = idx - row * B;
+          const int grow = tr * kTileRows + row;
+          if (grow < N && good) yg[static_cast<size_t>(b) * ldy + grow] = v[j];
+        }
+      }
+      for (int c = blockIdx.x + 1 + lane; c <= c_hi; c += 32) counters[c] = 0;
     }
     return;
   }

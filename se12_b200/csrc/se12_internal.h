@@ -32,8 +32,8 @@ struct GemvArgs {
   int batch;
   float* y;            // [B, ldy] fp32
   int ldy;
-  float* partials;     // [grid][2][16 * 8 * nblocks] stream-K partial rows
-  int* counters;       // [tile_rows] arrival counters, zero between calls
+  float* partials;     // [grid][2][16 rows][16 batch] stream-K partial rows (slot 0 used)
+  int* counters;       // [grid] per-CTA "partial published" flags, zero between calls
   int grid;
   int stages;
   int raw_3d;          // dense baseline: 1 = one 3-D box per tile, 0 = four 2-D boxes

@@ -132,6 +132,7 @@ GEMV_SHAPES = [
     ("synthetic", 2048, 2304),     # Gemma-2-2B q_proj
     ("synthetic", 272, 2304),
     ("synthetic", 32, 2560),       # fewer tiles than CTAs: every row shared by 10 CTAs
+    ("synthetic", 16, 65536),      # one row of 256 tiles over 64 CTAs: 63 contributors per split row
     ("synthetic", 33, 300),        # padding in both directions, K % 8 != 0
     ("synthetic", 1, 1),
     ("synthetic", 36, 1),

@@ -70,18 +70,34 @@ def test_noalloc_matches_workspace_entry_point_on_two_calls(rows, cols, batch):
         assert err <= TOLERANCE, f"call {call}: max rel err {err:.3g} against se12_gemv"
 
 
-def test_noalloc_rejects_matrices_beyond_its_scratch():
+def test_noalloc_rejects_a_batch_beyond_its_scratch():
+    from se12_b200 import _lib
+    from se12_b200.codec import encode_device
+
+    m = encode_device(synthetic_bf16(64, 512, seed=3))
+    x = torch.zeros(17, 512, dtype=torch.bfloat16, device="cuda")
+    y = torch.zeros(17, 64, dtype=torch.float32, device="cuda")
+    status = noalloc_gemv(m, x, y)
+    assert status == 1  # SE12_ERR_INVALID_ARGUMENT, nothing launched
+    assert "batch must be in 1..16" in _lib.load().se12_last_error().decode()
+
+
+def test_noalloc_serves_more_than_a_million_rows():
+    """The scratch does not depend on the matrix: 65537 tile rows work."""
     from se12_b200 import _lib
     from se12_b200.device import DeviceSe12Matrix
 
-    rows, cols = 65537 * 16, 256  # one tile row more than the scratch holds
+    rows, cols = 65537 * 16, 256
     tiles = 65537
     dev = torch.device("cuda", 0)
     zeros = lambda n, dtype=torch.uint8: torch.zeros(n, dtype=dtype, device=dev)  # noqa: E731
+    # every weight decodes to +2^(100 - 127): code 0, sign/mantissa 0
     m = DeviceSe12Matrix(rows, cols, tuple(range(100, 115)), zeros(tiles * 4096), zeros(tiles * 2048), zeros(tiles * 16),
                          zeros((tiles + 7) // 8), zeros(0, torch.int16))
-    x = torch.zeros(1, cols, dtype=torch.bfloat16, device=dev)
-    y = torch.zeros(1, rows, dtype=torch.float32, device=dev)
-    status = noalloc_gemv(m, x, y)
-    assert status == 1  # SE12_ERR_INVALID_ARGUMENT
-    assert "1048576 rows" in _lib.load().se12_last_error().decode()
+    x = torch.randn(2, cols, device=dev).to(torch.bfloat16)
+    y_ref = m.gemv(x)
+    for call in range(2):
+        y = torch.full((2, rows), float("nan"), dtype=torch.float32, device=dev)
+        _lib.check(noalloc_gemv(m, x, y), "se12_gemv_noalloc")
+        torch.cuda.synchronize()
+        assert rel_err(y, y_ref) <= TOLERANCE, f"call {call}"
