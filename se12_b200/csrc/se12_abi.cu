@@ -123,6 +123,7 @@ struct LaunchConfig {
   int stages;
   int nblocks;
   int x_resident;
+  int row_mode;
   size_t smem;
 };
 
@@ -150,10 +151,23 @@ LaunchConfig choose_config(bool raw, int tiles, int cols, int batch, int sm_coun
     per_sm = 1;
   }
   c.smem = se12::gemv_smem_bytes(raw, c.x_resident != 0, c.stages, batch, cols);
-  const int units = (tiles + se12::kStageTiles - 1) / se12::kStageTiles;
   // two CTAs per SM when they fit: the second CTA's warps hide the first
   // one's decode and barrier latencies
-  c.grid = std::max(1, std::min(units, per_sm * sm_count));
+  const int slots = per_sm * sm_count;
+  const int tile_cols = (cols + SE12_TILE_COLS - 1) / SE12_TILE_COLS;
+  const int tile_rows = tiles / tile_cols;
+  // Stream-K: stages of 4 tiles spread evenly; a tile row split between
+  // CTAs costs a cross-CTA fixup (about three stages' time on a loaded GPU).
+  // Row mode: whole tile rows per CTA, no fixup. Row mode wins unless its
+  // longest run is more than three stages longer.
+  const int units = (tiles + se12::kStageTiles - 1) / se12::kStageTiles;
+  const int grid_sk = std::max(1, std::min(units, slots));
+  const int grid_rows = std::max(1, std::min(tile_rows, slots));
+  const int stages_sk = (units + grid_sk - 1) / grid_sk;
+  const int rows_per_cta = (tile_rows + grid_rows - 1) / grid_rows;
+  const int stages_rows = (rows_per_cta * tile_cols + se12::kStageTiles - 1) / se12::kStageTiles;
+  c.row_mode = stages_rows <= stages_sk + 3 ? 1 : 0;
+  c.grid = c.row_mode ? grid_rows : grid_sk;
   return c;
 }
 
@@ -300,6 +314,7 @@ int se12_gemv(const se12_matrix* m, const uint16_t* x, int batch, int ldx, float
   a.grid = c.grid;
   a.stages = c.stages;
   a.x_resident = c.x_resident;
+  a.row_mode = c.row_mode;
   cudaError_t err = se12::launch_gemv(false, m->sm_map, m->ec_map, a, c.nblocks, c.smem,
                                       static_cast<cudaStream_t>(stream), true);
   if (err != cudaSuccess) return cuda_fail(err, "se12_gemv launch");
@@ -379,6 +394,7 @@ int se12_gemv_noalloc(const se12_matrix* m, const uint16_t* x, int batch, int ld
   a.grid = c.grid;
   a.stages = c.stages;
   a.x_resident = c.x_resident;
+  a.row_mode = c.row_mode;
   err = se12::launch_gemv(false, m->sm_map, m->ec_map, a, c.nblocks, c.smem, static_cast<cudaStream_t>(stream), false);
   if (err != cudaSuccess) return cuda_fail(err, "se12_gemv_noalloc launch");
   return SE12_OK;
@@ -444,6 +460,7 @@ int bf16_gemv(const uint16_t* w, int rows, int cols, int ldw, const uint16_t* x,
   a.grid = c.grid;
   a.stages = c.stages;
   a.x_resident = c.x_resident;
+  a.row_mode = c.row_mode;
   cudaError_t err = se12::launch_gemv(true, wmap, wmap, a, c.nblocks, c.smem, static_cast<cudaStream_t>(stream), true);
   if (err != cudaSuccess) return cuda_fail(err, "bf16_gemv launch");
   return SE12_OK;

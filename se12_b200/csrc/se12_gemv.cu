@@ -184,10 +184,18 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int units = (T + kStageTiles - 1) / kStageTiles;
-  const int u0 = unit_start(blockIdx.x, units, G);
-  const int nstages = unit_start(blockIdx.x + 1, units, G) - u0;
-  const int tstart = tile_start(blockIdx.x, units, G, T);
-  const int tend = tile_start(blockIdx.x + 1, units, G, T);
+  // This CTA's run of tiles [tstart, tend): whole tile rows (row mode) or
+  // a run of 4-tile stages (stream-K); its stages start at tstart.
+  int tstart, tend;
+  if (a.row_mode) {
+    const long long tile_rows = a.m.tile_rows;
+    tstart = static_cast<int>(tile_rows * blockIdx.x / G) * KT;
+    tend = static_cast<int>(tile_rows * (blockIdx.x + 1) / G) * KT;
+  } else {
+    tstart = tile_start(blockIdx.x, units, G, T);
+    tend = tile_start(blockIdx.x + 1, units, G, T);
+  }
+  const int nstages = (tend - tstart + kStageTiles - 1) / kStageTiles;
   const int tr_first = tstart / KT;
 
   if (tid == 0) {
@@ -229,10 +237,10 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
     }
     const int prologue = min(nstages, S);
     // the weights of stage i: 2 TMA loads (SE12) or one per tile (dense)
-    auto issue_weights = [&map0, &map1, sm8, o_w, full, T, KT, u0, lane, pol_w, raw_3d](int i, int s) {
+    auto issue_weights = [&map0, &map1, sm8, o_w, full, tend, KT, tstart, lane, pol_w, raw_3d](int i, int s) {
       if (lane == 0) {
-        const int tile0 = (u0 + i) * kStageTiles;
-        const int ntl = min(kStageTiles, T - tile0);
+        const int tile0 = tstart + i * kStageTiles;
+        const int ntl = min(kStageTiles, tend - tile0);
         uint8_t* w = sm8 + o_w + s * kWeightBytes;
         if (RAW) {
           mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(ntl) * 8192u);
@@ -261,9 +269,9 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
     // staged x of stage i: lane l copies 16-byte chunk l (columns 8 l .. 8 l
     // + 7) of every (tile, batch row) slice; columns past K are written as
     // zeros (the chunk holding column K with a plain load and a mask)
-    auto issue_x = [sm8, o_x, full, xg, ldx, xstage, T, KT, K, B, u0, lane](int i, int s) {
-      const int tile0 = (u0 + i) * kStageTiles;
-      const int ntl = min(kStageTiles, T - tile0);
+    auto issue_x = [sm8, o_x, full, xg, ldx, xstage, tend, KT, K, B, tstart, lane](int i, int s) {
+      const int tile0 = tstart + i * kStageTiles;
+      const int ntl = min(kStageTiles, tend - tile0);
       int kt = tile0 % KT;
       for (int j = 0; j < ntl; ++j) {
         const int col = kt * kTileCols + lane * 8;
@@ -294,10 +302,11 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
       __syncwarp();
     };
     // Escape records of record group r (stages 4 r .. 4 r + 3 of this CTA's
-    // run): three bulk copies into slot r % kRecSlots. The tiles' offsets are
-    // multiples of 4 tiles, so every copy starts 16-byte aligned; the
-    // fallback-index table is padded to a multiple of 4 tiles.
-    auto issue_records = [sm8, o_rec, rec_full, rec_empty, pos_g, esc_g, fbindex_g, T, u0, nstages, lane,
+    // run): three bulk copies into slot r % kRecSlots. Positions (32 B per
+    // tile) and slots (16 B per tile) start 16-byte aligned at any tile; the
+    // fallback indices (4 B per tile) are copied from the 4-tile-aligned tile
+    // at or before the group (the table is padded to a multiple of 4 tiles).
+    auto issue_records = [sm8, o_rec, rec_full, rec_empty, pos_g, esc_g, fbindex_g, tend, tstart, nstages, lane,
                           pol_w](int r) -> bool {
       if (RAW || r * kRecGroupStages >= nstages) return true;
       bool good = true;
@@ -305,14 +314,15 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
         const int slot = r % kRecSlots;
         if (r >= kRecSlots) good = mbar_wait_sleep(&rec_empty[slot], static_cast<uint32_t>(r / kRecSlots - 1) & 1u);
         if (good) {
-          const int t0 = (u0 + r * kRecGroupStages) * kStageTiles;
-          const int n = min(kRecGroupTiles, T - t0);
-          const int n4 = (n + 3) & ~3;
+          const int t0 = tstart + r * kRecGroupTiles;
+          const int n = min(kRecGroupTiles, tend - t0);
+          const int t0a = t0 & ~3;
+          const int n4 = (t0 - t0a + n + 3) & ~3;
           uint8_t* dst = sm8 + o_rec + slot * kRecSlotBytes;
           mbar_arrive_expect_tx(&rec_full[slot], static_cast<uint32_t>(n * 48 + n4 * 4));
           bulk_load(dst + kRecPosOffset, pos_g + static_cast<size_t>(t0) * kEscapeBudget, n * 32, &rec_full[slot], pol_w);
           bulk_load(dst + kRecEscOffset, esc_g + static_cast<size_t>(t0) * kEscapeBudget, n * 16, &rec_full[slot], pol_w);
-          bulk_load(dst + kRecFbOffset, fbindex_g + t0, n4 * 4, &rec_full[slot], pol_w);
+          bulk_load(dst + kRecFbOffset, fbindex_g + t0a, n4 * 4, &rec_full[slot], pol_w);
         }
       }
       return __shfl_sync(0xFFFFFFFFu, good ? 1 : 0, 0) != 0;
@@ -647,8 +657,9 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
   uint32_t ph = 0u;          // parity of its full-barrier phase, (i / S) & 1
   int rq = 0, rslot = 0;     // stage within its record group, the group's slot
   uint32_t rph = 0u;         // parity of the record slot's phase
-  int tile0 = u0 * kStageTiles;
+  int tile0 = tstart;
   int tr0 = tile0 / KT, kt0 = tile0 - tr0 * KT;  // row and column of the stage's first tile
+  const int fb_shift = tstart & 3;  // the fallback indices of a record slot start at its 4-aligned tile
   // The current stage's tile count, this warp's tile column and records.
   int ntl = 0, kt_mine = 0, fbi = -1;
   uint32_t pos = kNoEscape, ex = 0u;
@@ -656,7 +667,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
   // Waits for stage i's records and weights and decodes this warp's tile
   // of it into frag0 / frag1.
   auto fetch_stage = [&]() {
-    ntl = min(kStageTiles, T - tile0);
+    ntl = min(kStageTiles, tend - tile0);
     fbi = -1;
     pos = kNoEscape;
     ex = 0u;
@@ -665,7 +676,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
       if (jw < ntl) {
         const uint32_t rb = o_rec + rslot * kRecSlotBytes;
         const int lt = rq * kStageTiles + jw;
-        fbi = lds_at<int>(sm8, rb + kRecFbOffset + lt * 4);
+        fbi = lds_at<int>(sm8, rb + kRecFbOffset + (lt + fb_shift) * 4);
         if (lane < kEscapeBudget) {
           pos = lds_at<uint16_t>(sm8, rb + kRecPosOffset + lt * 32 + lane * 2);
           ex = lds_at<uint8_t>(sm8, rb + kRecEscOffset + lt * 16 + lane);

@@ -38,6 +38,7 @@ struct GemvArgs {
   int stages;
   int raw_3d;          // dense baseline: 1 = one 3-D box per tile, 0 = four 2-D boxes
   int x_resident;      // 1: all of x in shared memory; 0: x staged per stage
+  int row_mode;        // 1: each CTA owns whole tile rows; 0: stream-K over stages of 4 tiles
 };
 
 // Pipeline geometry of the GEMV kernels. One stage holds kStageTiles
@@ -66,7 +67,8 @@ constexpr int kRecSlots = 3;
 constexpr int kRecPosOffset = 0;
 constexpr int kRecEscOffset = kRecGroupTiles * 32;
 constexpr int kRecFbOffset = kRecEscOffset + kRecGroupTiles * 16;
-constexpr int kRecSlotBytes = kRecFbOffset + kRecGroupTiles * 4;
+constexpr int kRecFbTiles = kRecGroupTiles + 4;  // copied from the 4-tile-aligned tile at or before the group
+constexpr int kRecSlotBytes = kRecFbOffset + kRecFbTiles * 4;
 constexpr size_t kCoResidentSmem = 112 * 1024;  // two CTAs fit on one SM
 constexpr size_t kMaxSmemPerCta = 227 * 1024;   // one CTA per SM (sm_100 opt-in maximum)
 
