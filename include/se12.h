@@ -101,6 +101,24 @@ void se12_matrix_destroy(se12_matrix* m);
 size_t se12_gemv_workspace_bytes(const se12_matrix* m, int batch);
 int se12_workspace_clear(void* workspace_dev, size_t bytes, void* stream);
 
+/* The launch se12_gemv makes for this matrix and batch: the fixed launch
+ * table that replaces the reference's launch heuristic and tuner
+ * (default_launch_configuration, src/lws/domain/launch/heuristic.py:46-51;
+ * src/lws/tune.py:34-57). Informational: se12_gemv computes the same
+ * configuration itself. */
+typedef struct se12_launch_config {
+  int grid;          /* CTAs */
+  int threads;       /* per CTA */
+  int smem_bytes;    /* dynamic shared memory per CTA */
+  int ctas_per_sm;   /* CTAs the shared memory lets share an SM */
+  int stage_tiles;   /* 16x256 tiles per pipeline stage (4 or 8) */
+  int stages;        /* pipeline depth */
+  int x_resident;    /* 1: all of x in shared memory; 0: staged per stage */
+  int row_mode;      /* 1: whole tile rows per CTA; 0: stream-K with split rows */
+} se12_launch_config;
+
+int se12_gemv_launch_config(const se12_matrix* m, int batch, se12_launch_config* out);
+
 /*
  * Fused decode + GEMV:  y[b, n] = sum_k W[n, k] * x[b, k],  fp32 accumulate,
  * fp32 output. x: device BF16 [batch, ldx], y: device fp32 [batch, ldy].

@@ -48,6 +48,13 @@ class Se12StreamsStruct(ctypes.Structure):
     ]
 
 
+class Se12LaunchConfigStruct(ctypes.Structure):
+    """Mirror of ``se12_launch_config`` in include/se12.h."""
+
+    _fields_ = [(name, ctypes.c_int32) for name in
+                ("grid", "threads", "smem_bytes", "ctas_per_sm", "stage_tiles", "stages", "x_resident", "row_mode")]
+
+
 # name -> (restype, argtypes)
 SIGNATURES = {
     "se12_escape_pos_bytes": (c_size_t, [c_int, c_int]),
@@ -57,6 +64,7 @@ SIGNATURES = {
     "se12_matrix_destroy": (None, [c_void_p]),
     "se12_gemv_workspace_bytes": (c_size_t, [c_void_p, c_int]),
     "se12_workspace_clear": (c_int, [c_void_p, c_size_t, c_void_p]),
+    "se12_gemv_launch_config": (c_int, [c_void_p, c_int, ctypes.POINTER(Se12LaunchConfigStruct)]),
     "se12_gemv": (c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p, c_int, c_void_p, c_size_t, c_void_p]),
     "se12_gemv_noalloc": (c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p, c_int, c_void_p]),
     "se12_decode": (c_int, [c_void_p, c_void_p, c_int, c_void_p]),
@@ -104,6 +112,11 @@ def load() -> ctypes.CDLL:
         fn.argtypes = argtypes
     _LIB = lib
     return lib
+
+
+def is_loaded() -> bool:
+    """Whether this process has loaded the library already."""
+    return _LIB is not None
 
 
 def check(status: int, function: str) -> None:

@@ -58,11 +58,11 @@ int encode_map(CUtensorMap* map, CUtensorMapDataType type, int rank, const void*
   return SE12_OK;
 }
 
-// sm stream as [16T rows][2 halves][128 B] (one box = a stage's 4 tiles, both
-// halves); ec stream as [16T rows][128 B].
+// sm stream as [16T rows][2 halves][128 B] (one box = 4 tiles, both halves);
+// ec stream as [16T rows][128 B] (one box = 4 tiles).
 int encode_se12_maps(se12_matrix* m) {
   const cuuint64_t rows16 = static_cast<cuuint64_t>(m->view.tiles) * SE12_TILE_ROWS;
-  const cuuint32_t box_rows = se12::kStageTiles * SE12_TILE_ROWS;
+  const cuuint32_t box_rows = se12::kSe12BoxTiles * SE12_TILE_ROWS;
   const cuuint64_t sm_dims[3] = {128, 2, rows16};
   const cuuint64_t sm_strides[2] = {128, 256};
   const cuuint32_t sm_box[3] = {128, 2, box_rows};
@@ -112,63 +112,88 @@ int tiles_of(int rows, int cols) {
 // ------------------------------------------------------------------ launch table
 //
 // The fixed launch table that replaces the reference's run-time tuner
-// (lws.tune, src/lws/tune.py:34-57). The tile is fixed by the format (16x256)
-// and a stage by the kernel (4 tiles); what varies is the pipeline depth.
-// Two CTAs per SM (stream-K over stages). The depth is the largest of 4..2
-// stages that keeps shared memory under kCoResidentSmem, so that two CTAs
-// fit on one SM; large batches (x slices of 16 rows) exceed that and run
-// with 2 stages.
+// (lws.tune, src/lws/tune.py:34-57). The tile is fixed by the format
+// (16x256); what varies is the stage (4 or 8 tiles), the pipeline depth,
+// whether x is resident, the grid and how tiles map to CTAs.
+//  * Shared memory: the first candidate (below) that lets two CTAs share an
+//    SM, for each stage size; only if no candidate does, one CTA per SM.
+//    8-tile stages need x resident and as many CTAs per SM as 4-tile ones.
+//  * Work split: row mode (whole tile rows per CTA, no cross-CTA fixup) or
+//    stream-K (equal runs of stages, split rows finished across CTAs).
+//  * Among these, the smallest critical path of the longest CTA, in units of
+//    one warp's time for a half tile: a 4-tile stage costs 1 + r, an 8-tile
+//    stage 2 + r (each warp does a whole tile), with r = 0.65 the per-stage
+//    overhead (barriers, records, row ends), and a stream-K fixup three
+//    4-tile stages (a round trip through L2 on a loaded GPU). Measured on
+//    Gemma-2 shapes, these pick the faster configuration.
 struct LaunchConfig {
   int grid;
   int stages;
   int nblocks;
   int x_resident;
   int row_mode;
+  int full_tiles;
   size_t smem;
 };
 
-LaunchConfig choose_config(bool raw, int tiles, int cols, int batch, int sm_count) {
-  LaunchConfig c{};
-  c.nblocks = batch <= 8 ? 1 : 2;
-  // candidates in order of preference: (x resident?, stages); first those
-  // that let two CTAs share an SM, else the best one for one CTA per SM
-  static const int kCandidates[][2] = {{1, 4}, {1, 3}, {0, 4}, {0, 3}, {1, 2}, {0, 2}};
-  int per_sm = 0;
-  for (const size_t limit : {se12::kCoResidentSmem, se12::kMaxSmemPerCta}) {
-    for (const auto& cand : kCandidates) {
-      if (se12::gemv_smem_bytes(raw, cand[0] != 0, cand[1], batch, cols) <= limit) {
-        c.x_resident = cand[0];
-        c.stages = cand[1];
-        per_sm = (limit == se12::kCoResidentSmem) ? 2 : 1;
-        break;
-      }
+struct MemoryChoice {
+  int x_resident, stages, per_sm;  // per_sm = 0: none fits
+};
+
+// 8-tile stages only with x resident: their staged x (twice that of a
+// 4-tile stage) leaves room for two stages only and measured slower.
+MemoryChoice choose_memory(bool raw, bool full, int batch, int cols) {
+  // (x resident?, stages) in order of preference
+  static const int kOrder[][2] = {{1, 4}, {1, 3}, {0, 4}, {0, 3}, {1, 2}, {0, 2}};
+  for (const size_t limit : {se12::kCoResidentSmem, se12::kMaxSmemPerCta})
+    for (const auto& cand : kOrder) {
+      if (full && !cand[0]) continue;
+      if (se12::gemv_smem_bytes(raw, full, cand[0] != 0, cand[1], batch, cols) <= limit)
+        return {cand[0], cand[1], limit == se12::kCoResidentSmem ? 2 : 1};
     }
-    if (per_sm) break;
-  }
-  if (!per_sm) {  // not reached for batch <= 16: staged x with 2 stages fits one CTA per SM
-    c.x_resident = 0;
-    c.stages = 2;
-    per_sm = 1;
-  }
-  c.smem = se12::gemv_smem_bytes(raw, c.x_resident != 0, c.stages, batch, cols);
-  // two CTAs per SM when they fit: the second CTA's warps hide the first
-  // one's decode and barrier latencies
-  const int slots = per_sm * sm_count;
+  return {0, 0, 0};
+}
+
+LaunchConfig choose_config(bool raw, int tiles, int cols, int batch, int sm_count) {
+  const MemoryChoice mem4 = choose_memory(raw, false, batch, cols);
+  const MemoryChoice mem8 = raw ? MemoryChoice{0, 0, 0} : choose_memory(raw, true, batch, cols);
   const int tile_cols = (cols + SE12_TILE_COLS - 1) / SE12_TILE_COLS;
   const int tile_rows = tiles / tile_cols;
-  // Stream-K: stages of 4 tiles spread evenly; a tile row split between
-  // CTAs costs a cross-CTA fixup (about three stages' time on a loaded GPU).
-  // Row mode: whole tile rows per CTA, no fixup. Row mode wins unless its
-  // longest run is more than three stages longer.
-  const int units = (tiles + se12::kStageTiles - 1) / se12::kStageTiles;
-  const int grid_sk = std::max(1, std::min(units, slots));
-  const int grid_rows = std::max(1, std::min(tile_rows, slots));
-  const int stages_sk = (units + grid_sk - 1) / grid_sk;
-  const int rows_per_cta = (tile_rows + grid_rows - 1) / grid_rows;
-  const int stages_rows = (rows_per_cta * tile_cols + se12::kStageTiles - 1) / se12::kStageTiles;
-  c.row_mode = stages_rows <= stages_sk + 3 ? 1 : 0;
-  c.grid = c.row_mode ? grid_rows : grid_sk;
-  return c;
+  constexpr double kStageOverhead = 0.65;
+  constexpr double kFixup = 3 * (1 + kStageOverhead);
+  LaunchConfig best{};
+  double best_cost = 0;
+  for (const bool full : {false, true}) {
+    const MemoryChoice& mem = full ? mem8 : mem4;
+    // 8-tile stages only where they keep the CTAs per SM of 4-tile stages
+    if (!mem.per_sm || (full && mem.per_sm < mem4.per_sm)) continue;
+    const int stage = se12::stage_tiles(full);
+    const double stage_cost = (full ? 2 : 1) + kStageOverhead;
+    const int slots = mem.per_sm * sm_count;
+    const int units = (tiles + stage - 1) / stage;
+    const int grid_sk = std::max(1, std::min(units, slots));
+    const int grid_rows = std::max(1, std::min(tile_rows, slots));
+    const int stages_sk = (units + grid_sk - 1) / grid_sk;
+    const int rows_per_cta = (tile_rows + grid_rows - 1) / grid_rows;
+    const int stages_rows = (rows_per_cta * tile_cols + stage - 1) / stage;
+    for (const int row_mode : {1, 0}) {
+      const double cost = row_mode ? stages_rows * stage_cost : stages_sk * stage_cost + kFixup;
+      if (best.stages && cost >= best_cost) continue;
+      best_cost = cost;
+      best.full_tiles = full ? 1 : 0;
+      best.x_resident = mem.x_resident;
+      best.stages = mem.stages;
+      best.row_mode = row_mode;
+      best.grid = row_mode ? grid_rows : grid_sk;
+    }
+  }
+  if (!best.stages) {  // not reached for batch <= 16: 4-tile stages with staged x, 2 stages, fit one CTA per SM
+    best.stages = 2;
+    best.grid = std::max(1, std::min((tiles + 3) / 4, sm_count));
+  }
+  best.nblocks = batch <= 8 ? 1 : 2;
+  best.smem = se12::gemv_smem_bytes(raw, best.full_tiles != 0, best.x_resident != 0, best.stages, batch, cols);
+  return best;
 }
 
 // Workspace layout, identical for every matrix so that all calls on one
@@ -293,6 +318,22 @@ static int check_gemv_io(int rows, int cols, const uint16_t* x, int batch, int l
   return SE12_OK;
 }
 
+int se12_gemv_launch_config(const se12_matrix* m, int batch, se12_launch_config* out) {
+  if (!m || !out) return fail(SE12_ERR_INVALID_ARGUMENT, "null argument");
+  if (batch < 1 || batch > SE12_MAX_BATCH)
+    return fail(SE12_ERR_INVALID_ARGUMENT, "batch must be in 1.." + std::to_string(SE12_MAX_BATCH));
+  const LaunchConfig c = choose_config(false, m->view.tiles, m->view.cols, batch, m->sm_count);
+  out->grid = c.grid;
+  out->threads = se12::kGemvThreads;
+  out->smem_bytes = static_cast<int>(c.smem);
+  out->ctas_per_sm = c.smem <= se12::kCoResidentSmem ? 2 : 1;
+  out->stage_tiles = se12::stage_tiles(c.full_tiles != 0);
+  out->stages = c.stages;
+  out->x_resident = c.x_resident;
+  out->row_mode = c.row_mode;
+  return SE12_OK;
+}
+
 int se12_gemv(const se12_matrix* m, const uint16_t* x, int batch, int ldx, float* y, int ldy, void* workspace,
               size_t workspace_bytes, void* stream) {
   if (!m) return fail(SE12_ERR_INVALID_ARGUMENT, "null matrix");
@@ -315,6 +356,7 @@ int se12_gemv(const se12_matrix* m, const uint16_t* x, int batch, int ldx, float
   a.stages = c.stages;
   a.x_resident = c.x_resident;
   a.row_mode = c.row_mode;
+  a.full_tiles = c.full_tiles;
   cudaError_t err = se12::launch_gemv(false, m->sm_map, m->ec_map, a, c.nblocks, c.smem,
                                       static_cast<cudaStream_t>(stream), true);
   if (err != cudaSuccess) return cuda_fail(err, "se12_gemv launch");
@@ -395,6 +437,7 @@ int se12_gemv_noalloc(const se12_matrix* m, const uint16_t* x, int batch, int ld
   a.stages = c.stages;
   a.x_resident = c.x_resident;
   a.row_mode = c.row_mode;
+  a.full_tiles = c.full_tiles;
   err = se12::launch_gemv(false, m->sm_map, m->ec_map, a, c.nblocks, c.smem, static_cast<cudaStream_t>(stream), false);
   if (err != cudaSuccess) return cuda_fail(err, "se12_gemv_noalloc launch");
   return SE12_OK;
@@ -461,6 +504,7 @@ int bf16_gemv(const uint16_t* w, int rows, int cols, int ldw, const uint16_t* x,
   a.stages = c.stages;
   a.x_resident = c.x_resident;
   a.row_mode = c.row_mode;
+  a.full_tiles = c.full_tiles;
   cudaError_t err = se12::launch_gemv(true, wmap, wmap, a, c.nblocks, c.smem, static_cast<cudaStream_t>(stream), true);
   if (err != cudaSuccess) return cuda_fail(err, "bf16_gemv launch");
   return SE12_OK;

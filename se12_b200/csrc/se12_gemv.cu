@@ -6,17 +6,18 @@
 //
 // * Stream-K over the tile sequence. The matrix is the linear sequence of
 //   its T tiles in memory order (tile-row major, 16x256 weights each), cut
-//   into stages of 4 consecutive tiles. CTA c (two per SM) owns a contiguous
-//   run of stages. Tile rows entirely inside a CTA's run are written
-//   directly; a tile row split between CTAs is finished by its last
-//   contributor, which sums the partials in CTA order (deterministic, no
+//   into stages of 8 consecutive tiles. CTA c (two per SM) owns either whole
+//   tile rows (row mode) or a contiguous run of stages (stream-K). Tile rows
+//   entirely inside a CTA's run are written directly; a tile row split
+//   between CTAs is finished by the CTA holding its first tile, which adds
+//   the later CTAs' published partials in CTA order (deterministic, no
 //   floating-point atomics).
 // * Warp-specialised pipeline. A producer warp moves each stage's sm bytes
-//   with one 3-D TMA load ([64 rows][2 halves][128 B]) and its ec bytes with
-//   one 2-D TMA load ([64 rows][128 B]), both 128-byte swizzled, onto one
-//   mbarrier per stage; the escape records of four stages at a time come
-//   with three bulk copies. Eight consumer warps: warp w takes half w % 2
-//   (128 columns) of tile w / 2 of every stage. A reducer warp sums the
+//   with one 3-D TMA load ([128 rows][2 halves][128 B]) and its ec bytes
+//   with one 2-D TMA load ([128 rows][128 B]), both 128-byte swizzled, onto
+//   one mbarrier per stage; the escape records of 16 tiles at a time come
+//   with three bulk copies. Eight consumer warps: warp w takes tile w of
+//   every stage, its two 128-column halves in turn. A reducer warp sums the
 //   consumers' per-row partials, so consumers never wait for each other.
 // * Decode in registers straight into mma.sync fragments, with no table in
 //   memory: the 16-entry code -> exponent table lives in four registers and
@@ -48,14 +49,14 @@ __device__ __forceinline__ int unit_start(int c, int units, int grid) {
   return static_cast<int>((static_cast<long long>(units) * c) / grid);
 }
 
-// First tile of CTA c's run.
-__device__ __forceinline__ int tile_start(int c, int units, int grid, int tiles) {
-  return min(unit_start(c, units, grid) * kStageTiles, tiles);
+// First tile of CTA c's run (stream-K, stages of `stage` tiles).
+__device__ __forceinline__ int tile_start(int c, int units, int grid, int tiles, int stage) {
+  return min(unit_start(c, units, grid) * stage, tiles);
 }
 
 // CTA whose run contains tile i.
-__device__ __forceinline__ int tile_owner(int i, int units, int grid) {
-  const long long u = i / kStageTiles;
+__device__ __forceinline__ int tile_owner(int i, int units, int grid, int stage) {
+  const long long u = i / stage;
   return static_cast<int>(((u + 1) * grid - 1) / units);
 }
 
@@ -131,11 +132,14 @@ __device__ __forceinline__ T lds_at(const uint8_t* smem, uint32_t offset) {
   return *reinterpret_cast<const T*>(smem + offset);
 }
 
-template <int NB, bool RAW, bool XRES>
+template <int NB, bool RAW, bool XRES, bool FULL>
 __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_constant__ CUtensorMap map0,
                                                                const __grid_constant__ CUtensorMap map1,
                                                                const GemvArgs a) {
-  constexpr int kWeightBytes = RAW ? kRawStageWeightBytes : kSe12StageWeightBytes;
+  static_assert(!(RAW && FULL), "the dense baseline runs 4-tile stages");
+  constexpr int kWeightBytes = stage_weight_bytes(RAW, FULL);
+  constexpr int kStage = stage_tiles(FULL);             // tiles per stage
+  constexpr int kRecStages = kRecGroupTiles / kStage;   // stages per escape-record slot
   extern __shared__ __align__(1024) uint8_t smem_dynamic[];
   // All dynamic shared memory is addressed as smem_dynamic + 32-bit offset,
   // so every access compiles to a shared-memory instruction with 32-bit
@@ -166,7 +170,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
 
   // ------------------------------------------------------------ shared memory (offsets into sm8)
   const uint32_t xrs = static_cast<uint32_t>(x_resident_stride(K));                    // resident x: bytes per batch row
-  const uint32_t xstage = (kStageTiles * B * kXRowStride + 127) / 128 * 128;           // staged x: bytes per stage
+  const uint32_t xstage = (kStage * B * kXRowStride + 127) / 128 * 128;           // staged x: bytes per stage
   const uint32_t o_w = pad;                                                            // S x weights
   const uint32_t o_x = o_w + S * kWeightBytes;                                         // x (resident or staged)
   const uint32_t o_red = o_x + (XRES ? B * xrs : S * xstage);                          // [2][8][16][B] floats
@@ -183,19 +187,19 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
   float* const red = reinterpret_cast<float*>(sm8 + o_red);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int units = (T + kStageTiles - 1) / kStageTiles;
+  const int units = (T + kStage - 1) / kStage;
   // This CTA's run of tiles [tstart, tend): whole tile rows (row mode) or
-  // a run of 4-tile stages (stream-K); its stages start at tstart.
+  // a run of stages (stream-K); its stages start at tstart.
   int tstart, tend;
   if (a.row_mode) {
     const long long tile_rows = a.m.tile_rows;
     tstart = static_cast<int>(tile_rows * blockIdx.x / G) * KT;
     tend = static_cast<int>(tile_rows * (blockIdx.x + 1) / G) * KT;
   } else {
-    tstart = tile_start(blockIdx.x, units, G, T);
-    tend = tile_start(blockIdx.x + 1, units, G, T);
+    tstart = tile_start(blockIdx.x, units, G, T, kStage);
+    tend = tile_start(blockIdx.x + 1, units, G, T, kStage);
   }
-  const int nstages = (tend - tstart + kStageTiles - 1) / kStageTiles;
+  const int nstages = (tend - tstart + kStage - 1) / kStage;
   const int tr_first = tstart / KT;
 
   if (tid == 0) {
@@ -239,8 +243,8 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
     // the weights of stage i: 2 TMA loads (SE12) or one per tile (dense)
     auto issue_weights = [&map0, &map1, sm8, o_w, full, tend, KT, tstart, lane, pol_w, raw_3d](int i, int s) {
       if (lane == 0) {
-        const int tile0 = tstart + i * kStageTiles;
-        const int ntl = min(kStageTiles, tend - tile0);
+        const int tile0 = tstart + i * kStage;
+        const int ntl = min(kStage, tend - tile0);
         uint8_t* w = sm8 + o_w + s * kWeightBytes;
         if (RAW) {
           mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(ntl) * 8192u);
@@ -259,9 +263,15 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
             }
           }
         } else {
-          mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(kSe12StageWeightBytes));
-          tma_load_3d(w, &map0, 0, 0, tile0 * kTileRows, &full[s], pol_w);
-          tma_load_2d(w + kStageTiles * 4096, &map1, 0, tile0 * kTileRows, &full[s], pol_w);
+          // one sm and one ec box per 4 tiles; boxes past the matrix's
+          // last tile read zeros and still count their full bytes
+          mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(kWeightBytes));
+#pragma unroll
+          for (int q = 0; q < kStage / kSe12BoxTiles; ++q) {
+            const int row = (tile0 + q * kSe12BoxTiles) * kTileRows;
+            tma_load_3d(w + q * (kSe12BoxTiles * 4096), &map0, 0, 0, row, &full[s], pol_w);
+            tma_load_2d(w + kStage * 4096 + q * (kSe12BoxTiles * 2048), &map1, 0, row, &full[s], pol_w);
+          }
         }
       }
       __syncwarp();
@@ -270,8 +280,8 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
     // + 7) of every (tile, batch row) slice; columns past K are written as
     // zeros (the chunk holding column K with a plain load and a mask)
     auto issue_x = [sm8, o_x, full, xg, ldx, xstage, tend, KT, K, B, tstart, lane](int i, int s) {
-      const int tile0 = tstart + i * kStageTiles;
-      const int ntl = min(kStageTiles, tend - tile0);
+      const int tile0 = tstart + i * kStage;
+      const int ntl = min(kStage, tend - tile0);
       int kt = tile0 % KT;
       for (int j = 0; j < ntl; ++j) {
         const int col = kt * kTileCols + lane * 8;
@@ -301,14 +311,14 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
       if (lane == 0) mbar_arrive(&full[s]);
       __syncwarp();
     };
-    // Escape records of record group r (stages 4 r .. 4 r + 3 of this CTA's
-    // run): three bulk copies into slot r % kRecSlots. Positions (32 B per
+    // Escape records of record group r (tiles 16 r .. 16 r + 15 of this
+    // CTA's run): three bulk copies into slot r % kRecSlots. Positions (32 B per
     // tile) and slots (16 B per tile) start 16-byte aligned at any tile; the
     // fallback indices (4 B per tile) are copied from the 4-tile-aligned tile
     // at or before the group (the table is padded to a multiple of 4 tiles).
     auto issue_records = [sm8, o_rec, rec_full, rec_empty, pos_g, esc_g, fbindex_g, tend, tstart, nstages, lane,
                           pol_w](int r) -> bool {
-      if (RAW || r * kRecGroupStages >= nstages) return true;
+      if (RAW || r * kRecStages >= nstages) return true;
       bool good = true;
       if (lane == 0) {
         const int slot = r % kRecSlots;
@@ -327,9 +337,21 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
       }
       return __shfl_sync(0xFFFFFFFFu, good ? 1 : 0, 0) != 0;
     };
-    issue_records(0);
-    issue_records(1);
-    for (int i = 0; i < prologue; ++i) issue_weights(i, i);
+    // Records run one group ahead of the weights: before stage i is issued,
+    // every group up to i / kRecStages + 1. Group g reuses the slot of group
+    // g - 3, released when the consumers finish its last stage, which lies
+    // before stage i - kRecStages (already issued); the prologue's groups
+    // (at most 0..2) find their slots free.
+    int next_group = 0;
+    auto records_upto = [&issue_records, &next_group](int i) -> bool {
+      for (const int want = i / kRecStages + 1; next_group <= want; ++next_group)
+        if (!issue_records(next_group)) return false;
+      return true;
+    };
+    for (int i = 0; i < prologue; ++i) {
+      records_upto(i);
+      issue_weights(i, i);
+    }
     grid_dependency_wait();  // x is produced by the previous kernel in the stream
     if (XRES) {
       const uint32_t xbytes = static_cast<uint32_t>(kpad8) * 2u;
@@ -354,9 +376,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
     int s = 0;
     uint32_t ph = 1u;
     for (int i = prologue; i < nstages; ++i) {
-      // group r + 1 reuses the slot of group r - 2, which the consumers
-      // finished before stage i - 4 <= i - S
-      if ((i & (kRecGroupStages - 1)) == 0 && !issue_records(i / kRecGroupStages + 1)) break;
+      if (!records_upto(i)) break;
       if (!mbar_wait_sleep(&empty[s], ph ^ 1u)) break;
       issue_weights(i, s);
       if (!XRES) issue_x(i, s);
@@ -423,7 +443,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
       int c_hi = blockIdx.x;
       if (!ends) {
         // finisher: add the later contributors' partials, in CTA order
-        c_hi = tile_owner((tr + 1) * KT - 1, units, G);
+        c_hi = tile_owner((tr + 1) * KT - 1, units, G, kStage);
         for (int c = blockIdx.x + 1 + lane; c <= c_hi; c += 32) good = wait_flag_gpu(&counters[c]) && good;
         good = __all_sync(0xFFFFFFFFu, good);
         __syncwarp();
@@ -455,8 +475,11 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
   }
 
   // -------------------------------------------------------------- consumers
-  const int jw = warp >> 1;          // tile of the stage this warp decodes
-  const int hw = warp & 1;           // its half (128 columns)
+  // 8-tile stages (FULL): warp w decodes tile w of every stage, its two
+  // 128-column halves in turn. 4-tile stages: warp w takes half w % 2 of
+  // tile w / 2.
+  const int jw = FULL ? warp : (warp >> 1);  // tile of the stage this warp multiplies
+  const int hw = FULL ? 0 : (warp & 1);      // its (first) half
   const int g = lane >> 2, t = lane & 3;
   // an infinite padding weight needs its code rewritten (force_padding_escapes)
   const bool pad_inf = !RAW && (K & (kTileCols - 1)) && a.m.codebook[0] == 255;
@@ -467,11 +490,13 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
     for (int c = 0; c < 16; ++c) tab[c >> 2] |= table_byte(a.m.codebook, c) << (8 * (c & 3));
   }
 
-  // Per-thread shared-memory offsets (stage 0, tile jw), fixed for the kernel.
-  // Thread (g, t) owns rows g, g + 8 of its tile and, in its half, the column
-  // groups 32 k + 8 t .. + 7 for k = 0..3. Row g + 8 lies a constant distance
-  // after row g; the group offset is a compile-time value XOR a per-thread
-  // swizzle term, so only four registers hold the layout.
+  // Per-thread shared-memory offsets (stage 0, tile jw, half hw), fixed for
+  // the kernel. Thread (g, t) owns rows g, g + 8 of its tile and, in a half,
+  // the column groups 32 k + 8 t .. + 7 for k = 0..3. Row g + 8 lies a
+  // constant distance after row g; the group offset is a compile-time value
+  // XOR a per-thread swizzle term, so four registers hold the layout (with
+  // FULL, half 1 lies a lane-dependent distance after half 0, recomputed
+  // where it is used).
   uint32_t w_base, w_xor, e_base, e_xor;
   if (RAW) {
     // [16 rows][4 x 64-col chunks][128 B] per tile (3-D box; swizzle phase (4 row + chunk) & 7)
@@ -480,16 +505,19 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
     w_xor = raw_3d ? static_cast<uint32_t>((4 * g + 2 * hw) & 7) : static_cast<uint32_t>(g);
     e_base = e_xor = 0;
   } else {
-    // sm: [64 rows][2 halves][128 B], swizzle phase (2 row + half) & 7;
-    // ec: [64 rows][128 B] after the sm box, swizzle phase row & 7.
+    // sm: [16 kStage rows][2 halves][128 B], swizzle phase (2 row + half)
+    // & 7; 16-byte block 2 k + t / 2 of the half.
+    // ec: [16 kStage rows][128 B] after the sm boxes, swizzle phase row & 7;
+    // 16-byte block 4 half + k.
     const uint32_t R0 = 16 * jw + g;
     const uint32_t X = (2 * R0 + hw) & 7;  // same for row R0 + 8
     w_base = (2 * R0 + hw) * 128 + ((((t >> 1) ^ X) & 1) << 4) + 8 * (t & 1);
     w_xor = (X & 6) << 4;                   // group k: + ((32 k) ^ w_xor)
-    e_base = kStageTiles * 4096 + R0 * 128 + (((4 * hw) ^ (R0 & 4)) << 4) + 4 * t;
+    e_base = kStage * 4096 + R0 * 128 + (((4 * hw) ^ (R0 & 4)) << 4) + 4 * t;
     e_xor = (R0 & 3) << 4;                  // group k: + ((16 k) ^ e_xor)
   }
-  // x of batch row g + 8 nb at column 128 hw + 8 t (+ 32 k) of a tile
+  // x of batch row g + 8 nb at column 128 hw + 8 t (+ 32 k, + 128 for half
+  // 1 with FULL) of a tile
   const uint32_t x_thread = XRES ? o_x + static_cast<uint32_t>(g) * xrs + (128 * hw + 8 * t) * 2
                                  : o_x + (jw * B + g) * kXRowStride + (128 * hw + 8 * t) * 2;
   const uint32_t x_nb_step = XRES ? 8 * xrs : 8 * kXRowStride;
@@ -507,10 +535,11 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
   // current tile: [group k][pair].
   uint32_t frag0[4][4], frag1[4][4];
 
-  // Fills frag0 / frag1 with this warp's half of its tile of stage s:
-  // decoded SE12 weights, the raw bits of a fallback tile (fbi >= 0), or
-  // dense BF16 weights. Needs no x, so it may run before the dependency wait.
-  auto load_frags = [&](int s, int kt, int fbi) {
+  // Fills frag0 / frag1 with half hw + h of this warp's tile of stage s (h =
+  // 1 only with FULL): decoded SE12 weights, the raw bits of a fallback tile
+  // (fbi >= 0), or dense BF16 weights. Needs no x, so it may run before the
+  // dependency wait.
+  auto load_frags = [&](int s, int kt, int fbi, int h) {
     const uint32_t wst = o_w + s * kWeightBytes;
     if (RAW) {
 #pragma unroll
@@ -534,7 +563,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
     }
     if (__builtin_expect(fbi >= 0, 0)) {
       // fallback tile: its raw BF16 bits from global memory
-      const uint16_t* raw = fbraw_g + static_cast<size_t>(fbi) * kTileSize + 128 * hw + 8 * t;
+      const uint16_t* raw = fbraw_g + static_cast<size_t>(fbi) * kTileSize + 128 * (hw + h) + 8 * t;
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
         const uint4 v0 = __ldg(reinterpret_cast<const uint4*>(raw + g * kTileCols + 32 * k));
@@ -544,14 +573,20 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
       }
       return;
     }
-    if (__builtin_expect(pad_inf, 0) && kt == KT - 1) force_padding_escapes(sm8, wst + e_base, e_xor, 128 * hw + 8 * t, K - kt * kTileCols);
+    // half 1 (hw = 0): sm 16-byte block 2 k + t / 2 -> (2 k + t / 2) ^ 1 on
+    // the next 128-byte line (whose swizzle phase is odd); ec block k -> 4 +
+    // k, 64 bytes later or (row bit 2 set in the swizzle) earlier
+    const uint32_t wb = wst + w_base + (h ? 144u - ((static_cast<uint32_t>(lane) & 2u) << 4) : 0u);
+    const uint32_t eb = wst + e_base + (h ? 64u - ((static_cast<uint32_t>(lane) & 16u) << 3) : 0u);
+    if (__builtin_expect(pad_inf, 0) && kt == KT - 1)
+      force_padding_escapes(sm8, eb, e_xor, 128 * (hw + h) + 8 * t, K - kt * kTileCols);
     {
       uint2 sv0[4], sv1[4];
       uint32_t ev0[4], ev1[4];
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
-        const uint32_t wo = wst + w_base + ((32u * k) ^ w_xor);
-        const uint32_t eo = wst + e_base + ((16u * k) ^ e_xor);
+        const uint32_t wo = wb + ((32u * k) ^ w_xor);
+        const uint32_t eo = eb + ((16u * k) ^ e_xor);
         sv0[k] = lds_at<uint2>(sm8, wo);
         sv1[k] = lds_at<uint2>(sm8, wo + 16 * 128);   // row + 8: 16 half-rows of 128 B later
         ev0[k] = lds_at<uint32_t>(sm8, eo);
@@ -565,57 +600,57 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
     }
   };
 
-  // Multiplies the fragments with x (tile column kt of stage s) into acc,
-  // then adds the exact products of this half's escaped weights (records
-  // fbi, pos, ex).
-  auto mma_tile = [&](int s, int kt, int fbi, uint32_t pos, uint32_t ex) {
-    const uint32_t wst = o_w + s * kWeightBytes;
-    const uint32_t xt = XRES ? x_thread + kt * (kTileCols * 2) : x_thread + s * xstage;
-    {
+  // Multiplies the fragments (half hw + h) with x (tile column kt of stage
+  // s) into acc.
+  auto mma_tile = [&](int s, int kt, int h) {
+    const uint32_t xt = (XRES ? x_thread + kt * (kTileCols * 2) : x_thread + s * xstage) + 256 * h;
 #pragma unroll
-      for (int nb = 0; nb < NB; ++nb) {
-        const bool have = nb * 8 + g < B;
+    for (int nb = 0; nb < NB; ++nb) {
+      const bool have = nb * 8 + g < B;
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          uint4 xv = make_uint4(0, 0, 0, 0);
-          if (have) xv = lds_at<uint4>(sm8, xt + nb * x_nb_step + 64 * k);
-          mma_bf16_16816(acc[k & 1][nb], frag0[k][0], frag1[k][0], frag0[k][1], frag1[k][1], xv.x, xv.y);
-          mma_bf16_16816(acc[k & 1][nb], frag0[k][2], frag1[k][2], frag0[k][3], frag1[k][3], xv.z, xv.w);
-        }
+      for (int k = 0; k < 4; ++k) {
+        uint4 xv = make_uint4(0, 0, 0, 0);
+        if (have) xv = lds_at<uint4>(sm8, xt + nb * x_nb_step + 64 * k);
+        mma_bf16_16816(acc[k & 1][nb], frag0[k][0], frag1[k][0], frag0[k][1], frag1[k][1], xv.x, xv.y);
+        mma_bf16_16816(acc[k & 1][nb], frag0[k][2], frag1[k][2], frag0[k][3], frag1[k][3], xv.z, xv.w);
       }
     }
-    if (RAW || fbi >= 0) return;
-    {
-      // Escaped weights of this half: in the MMA with exponent 0 (below
-      // 2^-126 in magnitude), their exact products are added here. Escapes
-      // whose exponent is 0 (zeros and BF16 subnormals) were exact already.
-      const bool mine = (pos != kNoEscape) && ex != 0u && (((pos & 255u) >> 7) == static_cast<uint32_t>(hw));
-      unsigned pending = __ballot_sync(0xFFFFFFFFu, mine);
-      while (pending) {
-        const int e = __ffs(pending) - 1;
-        pending &= pending - 1;
-        const uint32_t epos = __shfl_sync(0xFFFFFFFFu, pos, e);
-        const uint32_t eex = __shfl_sync(0xFFFFFFFFu, ex, e);
-        const uint32_t r = epos >> 8, c = epos & 255u;
-        if ((r & 7) == static_cast<uint32_t>(g)) {
-          const uint32_t R = 16 * jw + r, bc = c & 127;
-          const uint32_t smb = sm8[wst + (2 * R + hw) * 128 + ((((bc >> 4) ^ ((2 * R + hw) & 7))) << 4) + (bc & 15)];
-          const float wv = bf16_bits_to_float(bf16_bits(smb, eex));
-          // x of batch rows 2t, 2t + 1 (+ 8 nb) at tile column c
-          const uint32_t xc = XRES ? o_x + kt * (kTileCols * 2) + c * 2 : o_x + s * xstage + jw * B * kXRowStride + c * 2;
-          const uint32_t xstep = XRES ? xrs : kXRowStride;
+  };
+
+  // Adds the exact products of the warp's escaped weights: in the MMA they
+  // decoded with exponent 0 (below 2^-126 in magnitude). Lane e < 16 holds
+  // escape e as position | exponent << 16, or 0 for an unused slot and for
+  // an escape whose exponent is 0 (zeros and BF16 subnormals: exact
+  // already).
+  auto fix_escapes = [&](int s, int kt, uint32_t rec) {
+    const uint32_t wst = o_w + s * kWeightBytes;
+    // FULL: all of the tile's escapes; else those in this warp's half
+    const bool mine = rec > 0xFFFFu && (FULL || ((rec >> 7) & 1u) == static_cast<uint32_t>(hw));
+    unsigned pending = __ballot_sync(0xFFFFFFFFu, mine);
+    while (pending) {
+      const int e = __ffs(pending) - 1;
+      pending &= pending - 1;
+      const uint32_t erec = __shfl_sync(0xFFFFFFFFu, rec, e);
+      const uint32_t eex = erec >> 16;
+      const uint32_t r = (erec >> 8) & 255u, c = erec & 255u;
+      if ((r & 7) == static_cast<uint32_t>(g)) {
+        const uint32_t L = 2 * (16 * jw + r) + (c >> 7), bc = c & 127;  // 128-byte line of the sm byte
+        const uint32_t smb = sm8[wst + L * 128 + (((bc >> 4) ^ (L & 7)) << 4) + (bc & 15)];
+        const float wv = bf16_bits_to_float(bf16_bits(smb, eex));
+        // x of batch rows 2t, 2t + 1 (+ 8 nb) at tile column c
+        const uint32_t xc = XRES ? o_x + kt * (kTileCols * 2) + c * 2 : o_x + s * xstage + jw * B * kXRowStride + c * 2;
+        const uint32_t xstep = XRES ? xrs : kXRowStride;
 #pragma unroll
-          for (int nb = 0; nb < NB; ++nb) {
-            const int b0 = nb * 8 + 2 * t;
-            const float x0 = (b0 < B) ? bf16_bits_to_float(lds_at<uint16_t>(sm8, xc + b0 * xstep)) : 0.f;
-            const float x1 = (b0 + 1 < B) ? bf16_bits_to_float(lds_at<uint16_t>(sm8, xc + (b0 + 1) * xstep)) : 0.f;
-            if (r >= 8) {
-              acc[0][nb][2] = fmaf(wv, x0, acc[0][nb][2]);
-              acc[0][nb][3] = fmaf(wv, x1, acc[0][nb][3]);
-            } else {
-              acc[0][nb][0] = fmaf(wv, x0, acc[0][nb][0]);
-              acc[0][nb][1] = fmaf(wv, x1, acc[0][nb][1]);
-            }
+        for (int nb = 0; nb < NB; ++nb) {
+          const int b0 = nb * 8 + 2 * t;
+          const float x0 = (b0 < B) ? bf16_bits_to_float(lds_at<uint16_t>(sm8, xc + b0 * xstep)) : 0.f;
+          const float x1 = (b0 + 1 < B) ? bf16_bits_to_float(lds_at<uint16_t>(sm8, xc + (b0 + 1) * xstep)) : 0.f;
+          if (r >= 8) {
+            acc[0][nb][2] = fmaf(wv, x0, acc[0][nb][2]);
+            acc[0][nb][3] = fmaf(wv, x1, acc[0][nb][3]);
+          } else {
+            acc[0][nb][0] = fmaf(wv, x0, acc[0][nb][0]);
+            acc[0][nb][1] = fmaf(wv, x1, acc[0][nb][1]);
           }
         }
       }
@@ -662,31 +697,31 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
   const int fb_shift = tstart & 3;  // the fallback indices of a record slot start at its 4-aligned tile
   // The current stage's tile count, this warp's tile column and records.
   int ntl = 0, kt_mine = 0, fbi = -1;
-  uint32_t pos = kNoEscape, ex = 0u;
+  uint32_t esc_rec = 0u;  // this lane's escape record (fix_escapes)
 
   // Waits for stage i's records and weights and decodes this warp's tile
-  // of it into frag0 / frag1.
+  // of it (SE12: its first half) into frag0 / frag1.
   auto fetch_stage = [&]() {
-    ntl = min(kStageTiles, tend - tile0);
+    ntl = min(kStage, tend - tile0);
     fbi = -1;
-    pos = kNoEscape;
-    ex = 0u;
+    esc_rec = 0u;
     if (!RAW) {
       if (rq == 0 && ok) ok = mbar_wait(&rec_full[rslot], rph);
       if (jw < ntl) {
         const uint32_t rb = o_rec + rslot * kRecSlotBytes;
-        const int lt = rq * kStageTiles + jw;
+        const int lt = rq * kStage + jw;
         fbi = lds_at<int>(sm8, rb + kRecFbOffset + (lt + fb_shift) * 4);
         if (lane < kEscapeBudget) {
-          pos = lds_at<uint16_t>(sm8, rb + kRecPosOffset + lt * 32 + lane * 2);
-          ex = lds_at<uint8_t>(sm8, rb + kRecEscOffset + lt * 16 + lane);
+          const uint32_t pos = lds_at<uint16_t>(sm8, rb + kRecPosOffset + lt * 32 + lane * 2);
+          const uint32_t ex = lds_at<uint8_t>(sm8, rb + kRecEscOffset + lt * 16 + lane);
+          if (pos != kNoEscape) esc_rec = pos | (ex << 16);
         }
       }
     }
     if (ok) ok = mbar_wait(&full[s], ph);
     kt_mine = kt0 + jw;
     while (kt_mine >= KT) kt_mine -= KT;
-    if (jw < ntl && ok) load_frags(s, kt_mine, fbi);
+    if (jw < ntl && ok) load_frags(s, kt_mine, fbi, 0);
   };
 
   // The weights do not depend on the previous kernel in the stream: decode
@@ -710,7 +745,16 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
         ++tr;
         pe += KT;
       }
-      if (jw < ntl && ok) mma_tile(s, kt_mine, fbi, pos, ex);
+      if (jw < ntl && ok) {
+        mma_tile(s, kt_mine, 0);
+        // the escape products before half 1, so that their record is dead
+        // during its decode
+        if (!RAW && fbi < 0) fix_escapes(s, kt_mine, esc_rec);
+        if (FULL) {
+          load_frags(s, kt_mine, fbi, 1);
+          mma_tile(s, kt_mine, 1);
+        }
+      }
       while (pe < ntl) {
         finish_row(tr);
         ++tr;
@@ -723,21 +767,21 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
     __syncwarp();
     if (lane == 0) {
       mbar_arrive(&empty[s]);
-      if (!RAW && (rq == kRecGroupStages - 1 || i == nstages - 1)) mbar_arrive(&rec_empty[rslot]);
+      if (!RAW && (rq == kRecStages - 1 || i == nstages - 1)) mbar_arrive(&rec_empty[rslot]);
     }
     if (++s == S) {
       s = 0;
       ph ^= 1u;
     }
-    if (++rq == kRecGroupStages) {
+    if (++rq == kRecStages) {
       rq = 0;
       if (++rslot == kRecSlots) {
         rslot = 0;
         rph ^= 1u;
       }
     }
-    tile0 += kStageTiles;
-    kt0 += kStageTiles;
+    tile0 += kStage;
+    kt0 += kStage;
     while (kt0 >= KT) {
       kt0 -= KT;
       ++tr0;
@@ -749,10 +793,18 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
 cudaError_t launch_gemv(bool raw, const CUtensorMap& map0, const CUtensorMap& map1, const GemvArgs& a, int nblocks,
                         size_t smem, cudaStream_t stream, bool pdl) {
   using Kernel = void (*)(const CUtensorMap, const CUtensorMap, const GemvArgs);
-  static const Kernel table[2][2][2] = {
-      {{gemv_kernel<1, false, false>, gemv_kernel<1, false, true>}, {gemv_kernel<1, true, false>, gemv_kernel<1, true, true>}},
-      {{gemv_kernel<2, false, false>, gemv_kernel<2, false, true>}, {gemv_kernel<2, true, false>, gemv_kernel<2, true, true>}}};
-  const Kernel kernel = table[nblocks == 1 ? 0 : 1][raw ? 1 : 0][a.x_resident ? 1 : 0];
+  // [batch blocks][kind: SE12 4-tile, SE12 8-tile, dense][x resident];
+  // 8-tile stages always hold x resident
+  static const Kernel table[2][3][2] = {
+      {{gemv_kernel<1, false, false, false>, gemv_kernel<1, false, true, false>},
+       {nullptr, gemv_kernel<1, false, true, true>},
+       {gemv_kernel<1, true, false, false>, gemv_kernel<1, true, true, false>}},
+      {{gemv_kernel<2, false, false, false>, gemv_kernel<2, false, true, false>},
+       {nullptr, gemv_kernel<2, false, true, true>},
+       {gemv_kernel<2, true, false, false>, gemv_kernel<2, true, true, false>}}};
+  const int kind = raw ? 2 : (a.full_tiles ? 1 : 0);
+  const Kernel kernel = table[nblocks == 1 ? 0 : 1][kind][a.x_resident ? 1 : 0];
+  if (!kernel) return cudaErrorInvalidValue;
   cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (err != cudaSuccess) return err;
   cudaLaunchConfig_t cfg = {};

@@ -38,31 +38,37 @@ struct GemvArgs {
   int stages;
   int raw_3d;          // dense baseline: 1 = one 3-D box per tile, 0 = four 2-D boxes
   int x_resident;      // 1: all of x in shared memory; 0: x staged per stage
-  int row_mode;        // 1: each CTA owns whole tile rows; 0: stream-K over stages of 4 tiles
+  int row_mode;        // 1: each CTA owns whole tile rows; 0: stream-K over stages
+  int full_tiles;      // SE12: 1 = 8-tile stages, a warp per tile; 0 = 4-tile stages, a warp per half tile
 };
 
-// Pipeline geometry of the GEMV kernels. One stage holds kStageTiles
-// consecutive tiles of the linear tile sequence:
-//   SE12: sm as one 3-D TMA box [64 rows][2 halves][128 B] (16 KB) and ec as
-//         one 2-D box [64 rows][128 B] (8 KB), both with the 128-byte swizzle;
-//   dense baseline: one 3-D box [16 rows][4 x 64 columns] (8 KB) per tile.
-// x is either resident (all of x[B, K] in shared memory, one bulk copy per
-// batch row per CTA) or, when that does not fit, staged per stage by the
+// Pipeline geometry of the GEMV kernels. One stage holds consecutive tiles
+// of the linear tile sequence, either
+//   4 tiles, consumer warp w taking half w % 2 (128 columns) of tile w / 2, or
+//   8 tiles, consumer warp w taking tile w, its two halves in turn (SE12
+//   only: half the per-stage overhead per weight, twice the staged x).
+// SE12 weights arrive as 3-D TMA boxes [64 rows][2 halves][128 B] of sm
+// (16 KB) and 2-D boxes [64 rows][128 B] of ec (8 KB), both with the 128-byte
+// swizzle: one of each per 4 tiles, the ec boxes after the stage's sm boxes.
+// The dense baseline takes one 3-D box [16 rows][4 x 64 columns] (8 KB) per
+// tile. x is either resident (all of x[B, K] in shared memory, one bulk copy
+// per batch row per CTA) or, when that does not fit, staged per stage by the
 // producer warp's lanes with cp.async.
-constexpr int kStageTiles = 4;
-constexpr int kSe12StageWeightBytes = kStageTiles * 6144;
-constexpr int kRawStageWeightBytes = kStageTiles * 8192;
+constexpr int kSe12BoxTiles = 4;
+__host__ __device__ constexpr int stage_tiles(bool full_tiles) { return full_tiles ? 8 : 4; }
+__host__ __device__ constexpr int stage_weight_bytes(bool raw, bool full_tiles) {
+  return stage_tiles(full_tiles) * (raw ? 8192 : 6144);
+}
 constexpr int kXRowStride = 576;        // bytes per (tile, batch row) x slice when staged: 512 + 64 pad
-constexpr int kConsumerWarps = 8;       // warp w: half w % 2 of tile w / 2 of every stage
+constexpr int kConsumerWarps = 8;
 constexpr int kProducerWarp = kConsumerWarps;      // TMA / bulk copies
 constexpr int kReducerWarp = kConsumerWarps + 1;   // sums the consumers' row partials
 constexpr int kGemvThreads = (kConsumerWarps + 2) * 32;
 // Escape records (escape positions, escape slots, fallback indices) of
-// kRecGroupStages consecutive stages are copied into shared memory together,
-// into one of kRecSlots slots: [16 tiles][16] u16 positions, [16][16] u8
-// slots, [16] i32 fallback indices.
-constexpr int kRecGroupStages = 4;
-constexpr int kRecGroupTiles = kRecGroupStages * kStageTiles;
+// kRecGroupTiles consecutive tiles (two SE12 stages) are copied into shared
+// memory together, into one of kRecSlots slots: [16 tiles][16] u16
+// positions, [16][16] u8 slots, [16 + 4] i32 fallback indices.
+constexpr int kRecGroupTiles = 16;
 constexpr int kRecSlots = 3;
 constexpr int kRecPosOffset = 0;
 constexpr int kRecEscOffset = kRecGroupTiles * 32;
@@ -77,10 +83,12 @@ constexpr size_t kMaxSmemPerCta = 227 * 1024;   // one CTA per SM (sm_100 opt-in
 // in different bank groups.
 __host__ __device__ inline int x_resident_stride(int cols) { return (cols + 255) / 256 * 512 + 64; }
 
-inline size_t x_stage_bytes(int batch) { return ((size_t)kStageTiles * batch * kXRowStride + 127) / 128 * 128; }
+inline size_t x_stage_bytes(bool full_tiles, int batch) {
+  return ((size_t)stage_tiles(full_tiles) * batch * kXRowStride + 127) / 128 * 128;
+}
 
-inline size_t gemv_smem_bytes(bool raw, bool x_resident, int stages, int batch, int cols) {
-  size_t per_stage = (raw ? kRawStageWeightBytes : kSe12StageWeightBytes) + (x_resident ? 0 : x_stage_bytes(batch));
+inline size_t gemv_smem_bytes(bool raw, bool full_tiles, bool x_resident, int stages, int batch, int cols) {
+  size_t per_stage = stage_weight_bytes(raw, full_tiles) + (x_resident ? 0 : x_stage_bytes(full_tiles, batch));
   size_t bytes = 1024;                                                  // alignment slack
   bytes += (size_t)stages * per_stage;
   if (x_resident) bytes += (size_t)batch * x_resident_stride(cols);

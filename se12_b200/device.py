@@ -137,6 +137,12 @@ class DeviceSe12Matrix:
         """y[B, N] = x[B, K] . W^T in fp32 (x: BF16 or fp32, [K] or [B, K])."""
         return gemv_call(self, x, out)
 
+    def launch_config(self, batch: int = 1) -> dict:
+        """The launch se12_gemv makes for this matrix at this batch size."""
+        cfg = _lib.Se12LaunchConfigStruct()
+        _lib.call("se12_gemv_launch_config", self._handle, int(batch), ctypes.byref(cfg))
+        return {name: getattr(cfg, name) for name, _ in cfg._fields_}
+
     def decode(self, out: torch.Tensor | None = None) -> torch.Tensor:
         """The exact BF16 matrix [rows, cols] on the device."""
         if out is None:

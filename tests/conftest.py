@@ -48,3 +48,25 @@ def golden_cases():
     import cases
 
     return cases.all_cases()
+
+
+@pytest.fixture(autouse=True)
+def no_kernel_side_error(request):
+    """Every GPU test ends with the library's device status word at zero:
+    a bounded wait that gave up (which leaves its outputs unwritten) fails
+    the test even where the output buffer happened to hold the right values."""
+    yield
+    if "gpu" not in request.keywords:
+        return
+    import torch
+
+    if not torch.cuda.is_available():
+        return
+    from se12_b200 import _lib
+
+    if _lib.LIBRARY_PATH.exists() and _lib.is_loaded():
+        from se12_b200.device import device_status
+
+        torch.cuda.synchronize()
+        status = device_status()
+        assert status == 0, f"kernel-side error status {status:#x}"

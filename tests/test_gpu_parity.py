@@ -141,6 +141,12 @@ GEMV_SHAPES = [
     ("outliers", 160, 2560),
     ("concentrated", 160, 2560),
     ("forced_fallback", 16, 256),
+    # shapes that reach the remaining launch configurations (checked by
+    # test_launch_table_reaches_every_configuration on a 148-SM B200)
+    ("synthetic", 16, 4608),       # 4-tile stages, stream-K, x resident (batch 1) / staged (batch 4)
+    ("synthetic", 16, 3584),       # 4-tile stages, row mode, staged x (batch 8)
+    ("synthetic", 1024, 5120),     # 8-tile stages, stream-K (batch 1)
+    ("synthetic", 4096, 1792),     # 8-tile stages, 3-deep pipeline, one CTA per SM (batch 16)
 ]
 
 
@@ -185,6 +191,27 @@ def test_fused_gemv_matches_fp64_oracle(kind, rows, cols, batch):
     # the reference CPU path (numpy decode + fp32 matmul) is held to the same bar
     y_cpu = oracle.gemv_reference_cpu(streams, oracle.bits_to_float32(xb))
     assert oracle.max_relative_error(y_cpu, y64) <= TOLERANCE
+
+
+def test_launch_table_reaches_every_configuration():
+    """The parity shapes above run every kernel configuration: 4-tile stages
+    with x resident or staged, 8-tile stages (x always resident), each in row
+    mode and stream-K, and 8-tile stages with a pipeline deeper than 2."""
+    seen, deep = set(), False
+    for kind, rows, cols in GEMV_SHAPES:
+        m = gemv_fixture(kind, rows, cols)[2]
+        for batch in (1, 2, 4, 8, 16):
+            c = m.launch_config(batch)
+            assert c["threads"] == 320 and 1 <= c["grid"] <= 2 * torch.cuda.get_device_properties(0).multi_processor_count
+            seen.add((c["stage_tiles"], c["x_resident"], c["row_mode"]))
+            deep = deep or (c["stage_tiles"] == 8 and c["stages"] > 2)
+    if torch.cuda.get_device_properties(0).multi_processor_count != 148:
+        pytest.skip("the shapes are chosen for 148 SMs")
+    assert all(x == 1 for t, x, _ in seen if t == 8), "8-tile stages with staged x"
+    missing = {(4, x, r) for x in (0, 1) for r in (0, 1)} | {(8, 1, r) for r in (0, 1)}
+    missing -= seen
+    assert not missing, f"configurations no parity shape reaches: {sorted(missing)}"
+    assert deep
 
 
 @pytest.mark.parametrize("batch", [3, 9, 20])
