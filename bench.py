@@ -65,6 +65,8 @@ def parse_args():
     p.add_argument("--no-dense", action="store_true", help="skip the dense BF16 comparisons")
     p.add_argument("--layers", type=int, default=None, help="override the layer count (profiling small cases)")
     p.add_argument("--no-lm-head", action="store_true")
+    p.add_argument("--no-group", action="store_true",
+                   help="one GEMV per projection instead of q/k/v and gate/up as one segmented matrix each")
     p.add_argument("--tp", action="store_true",
                    help="tensor-parallel decode step over the torchrun ranks (default config gemma2-27b)")
     return p.parse_args()
@@ -273,22 +275,49 @@ def run_reference(args) -> None:
 # ---------------------------------------------------------------------- GPU leg
 
 
-def build_stack(torch, shapes, batch, device, layers, lm_head, keep_dense, seed_offset=0):
+def build_stack(torch, shapes, batch, device, layers, lm_head, keep_dense, seed_offset=0, group=True):
+    """Encodes every matrix of the step (each its own SE12 tensor, as lws.pack
+    writes them). With ``group``, the projections of a layer that multiply
+    the same input (q/k/v, gate/up) become one segmented matrix each: one
+    GEMV over the same bytes, each segment with its own codebook."""
     from se12_b200.codec import encode_device
+    from se12_b200.device import DeviceSe12Matrix
 
     mats, dense = [], []
-    specs = []
+
+    def add(entries):
+        if group and len(entries) > 1:
+            name = entries[0][0]
+            mats.append((name, DeviceSe12Matrix.concatenate([e[1] for e in entries]), entries[0][2]))
+            dense.append(torch.cat([e[3] for e in entries]) if keep_dense else None)
+        else:
+            for name, m, kind, w in entries:
+                mats.append((name, m, kind))
+                dense.append(w)
+
     for layer in range(layers):
+        encoded = {}
         for j, (name, rows, cols, kind) in enumerate(shapes.layer_matrices()):
-            specs.append((f"layers.{layer}.{name}", rows, cols, kind, 1000 * layer + j))
+            w = synthetic_bf16(torch, rows, cols, 1000 * layer + j + seed_offset, device)
+            encoded[name] = (f"layers.{layer}.{name}", encode_device(w), kind, w if keep_dense else None)
+            del w
+        members = {m: g for g, ms in shapes.GROUPS for m in ms}
+        done = set()
+        for name, _, _, _ in shapes.layer_matrices():
+            if name in done:
+                continue
+            gname = members.get(name)
+            names = dict(shapes.GROUPS)[gname] if gname else (name,)
+            entries = [encoded[n] for n in names]
+            if gname and group:
+                entries[0] = (f"layers.{layer}.{gname}",) + entries[0][1:]
+            add(entries)
+            done.update(names)
+        del encoded
     if lm_head:
         name, rows, cols, kind = shapes.lm_head()
-        specs.append((name, rows, cols, kind, 999_999))
-    for name, rows, cols, kind, seed in specs:
-        w = synthetic_bf16(torch, rows, cols, seed + seed_offset, device)
-        m = encode_device(w)
-        mats.append((name, m, kind))
-        dense.append(w if keep_dense else None)
+        w = synthetic_bf16(torch, rows, cols, 999_999 + seed_offset, device)
+        add([(name, encode_device(w), kind, w if keep_dense else None)])
         del w
     torch.cuda.synchronize()
     return mats, dense
@@ -348,7 +377,7 @@ def run_ours(args) -> None:
     # N > 1: each rank streams its own shard of an N-times larger set of
     # matrices (distinct seeds per rank): weak scaling, no collective.
     mats, dense = build_stack(torch, shapes, batch, device, layers, not args.no_lm_head, keep_dense=not args.no_dense,
-                              seed_offset=rank * 10_000_000)
+                              seed_offset=rank * 10_000_000, group=not args.no_group)
     setup_s = time.perf_counter() - t_setup
 
     gen = torch.Generator(device=device)
@@ -509,6 +538,9 @@ def run_ours(args) -> None:
                 + ("" if args.no_lm_head else " + lm_head") + f", batch {batch}",
                 "batch": batch,
                 "matrices": len(mats),
+                "grouping": "none: one GEMV per projection" if args.no_group else
+                "q/k/v and gate/up of each layer as one segmented matrix (their own SE12 tensors concatenated, "
+                "one codebook per segment): one GEMV each, 4 GEMVs per layer",
                 "weights": weights,
                 "se12_bytes": se12_bytes,
                 "bits_per_weight": 8 * se12_bytes / weights,

@@ -35,6 +35,7 @@ extern "C" {
 #define SE12_CODEBOOK_SIZE 15
 #define SE12_FORMAT_VERSION 1
 #define SE12_MAX_BATCH 16
+#define SE12_MAX_SEGMENTS 4
 
 typedef enum se12_status {
   SE12_OK = 0,
@@ -85,6 +86,22 @@ size_t se12_fallback_index_bytes(int rows, int cols);
  * Replaces the upload / host precompute of Se12MatVecKernel.__init__ and
  * _upload_se12_streams (src/lws/adapters/cuda/gemv.py:183-194, 229-264). */
 int se12_matrix_create(const se12_streams* streams, se12_matrix** out);
+
+/* A segmented matrix: `streams` hold the tile-major concatenation of
+ * `segments` (1..SE12_MAX_SEGMENTS) SE12 matrices with the same cols -- for
+ * example the q, k and v projections of an attention block, or gate and up
+ * of an MLP, which multiply the same x -- so that one se12_gemv computes all
+ * of them into one y of sum(segment_rows) rows. Each segment keeps its own
+ * codebook (codebooks: [segments][15]). streams->rows must equal
+ * sum(segment_rows) and every segment but the last needs a multiple of 16
+ * rows, so that the segments' tiles follow each other:
+ *   sm, ec, esc, fallback_raw: the segments' streams one after the other;
+ *   fallback_bitmap: the segments' tile bits one after the other, MSB first.
+ * streams->codebook is ignored. Every entry point accepts the result like a
+ * plain matrix. No reference counterpart (the reference launches one GEMV
+ * per tensor). */
+int se12_matrix_create_segmented(const se12_streams* streams, int segments, const int32_t* segment_rows,
+                                 const uint8_t* codebooks, se12_matrix** out);
 
 /* Fills escape_pos and fallback_index on the device (once per matrix).
  * Replaces the host prefix sums fallback_offsets / row_escape_offset

@@ -60,6 +60,8 @@ SIGNATURES = {
     "se12_escape_pos_bytes": (c_size_t, [c_int, c_int]),
     "se12_fallback_index_bytes": (c_size_t, [c_int, c_int]),
     "se12_matrix_create": (c_int, [ctypes.POINTER(Se12StreamsStruct), ctypes.POINTER(c_void_p)]),
+    "se12_matrix_create_segmented": (c_int, [ctypes.POINTER(Se12StreamsStruct), c_int, ctypes.POINTER(ctypes.c_int32),
+                                             ctypes.POINTER(ctypes.c_uint8), ctypes.POINTER(c_void_p)]),
     "se12_matrix_prepare": (c_int, [c_void_p, c_void_p]),
     "se12_matrix_destroy": (None, [c_void_p]),
     "se12_gemv_workspace_bytes": (c_size_t, [c_void_p, c_int]),

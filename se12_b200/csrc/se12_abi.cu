@@ -238,8 +238,26 @@ size_t se12_fallback_index_bytes(int rows, int cols) {
 }
 
 int se12_matrix_create(const se12_streams* s, se12_matrix** out) {
-  if (!s || !out) return fail(SE12_ERR_INVALID_ARGUMENT, "null argument");
+  if (!s) return fail(SE12_ERR_INVALID_ARGUMENT, "null argument");
+  return se12_matrix_create_segmented(s, 1, &s->rows, s->codebook, out);
+}
+
+int se12_matrix_create_segmented(const se12_streams* s, int segments, const int32_t* segment_rows,
+                                 const uint8_t* codebooks, se12_matrix** out) {
+  if (!s || !out || !segment_rows || !codebooks) return fail(SE12_ERR_INVALID_ARGUMENT, "null argument");
   *out = nullptr;
+  if (segments < 1 || segments > SE12_MAX_SEGMENTS)
+    return fail(SE12_ERR_INVALID_ARGUMENT, "segments must be in 1.." + std::to_string(SE12_MAX_SEGMENTS));
+  long long total_rows = 0;
+  for (int i = 0; i < segments; ++i) {
+    if (segment_rows[i] <= 0) return fail(SE12_ERR_INVALID_ARGUMENT, "segment rows must be positive");
+    if (i + 1 < segments && segment_rows[i] % SE12_TILE_ROWS != 0)
+      return fail(SE12_ERR_INVALID_ARGUMENT, "every segment but the last needs a multiple of 16 rows");
+    total_rows += segment_rows[i];
+  }
+  if (total_rows != s->rows)
+    return fail(SE12_ERR_INVALID_ARGUMENT, "segment rows sum to " + std::to_string(total_rows) + ", streams have " +
+                                               std::to_string(s->rows) + " rows");
   if (s->tile_rows != SE12_TILE_ROWS || s->tile_cols != SE12_TILE_COLS || s->escape_budget != SE12_ESCAPE_BUDGET)
     return fail(SE12_ERR_UNSUPPORTED_FORMAT, "tile shape must be 16x256 with an escape budget of 16, got " +
                                                  std::to_string(s->tile_rows) + "x" + std::to_string(s->tile_cols) +
@@ -271,8 +289,16 @@ int se12_matrix_create(const se12_streams* s, se12_matrix** out) {
   v.tile_rows = (s->rows + SE12_TILE_ROWS - 1) / SE12_TILE_ROWS;
   v.tile_cols = (s->cols + SE12_TILE_COLS - 1) / SE12_TILE_COLS;
   v.tiles = v.tile_rows * v.tile_cols;
-  std::memset(v.codebook, 0, sizeof(v.codebook));
-  std::memcpy(v.codebook, s->codebook, SE12_CODEBOOK_SIZE);
+  std::memset(v.codebooks, 0, sizeof(v.codebooks));
+  v.segments = segments;
+  int end = 0;
+  for (int i = 0; i < se12::kMaxSegments; ++i) {
+    if (i < segments) {
+      end += (segment_rows[i] + SE12_TILE_ROWS - 1) / SE12_TILE_ROWS;
+      std::memcpy(v.codebooks[i], codebooks + i * SE12_CODEBOOK_SIZE, SE12_CODEBOOK_SIZE);
+    }
+    v.seg_end[i] = (i < segments - 1) ? end : INT32_MAX;
+  }
   m->device = device;
   m->sm_count = sm_count;
   st = encode_se12_maps(m);
@@ -493,6 +519,8 @@ int bf16_gemv(const uint16_t* w, int rows, int cols, int ldw, const uint16_t* x,
   a.m.tile_rows = tile_rows;
   a.m.tile_cols = tile_cols;
   a.m.tiles = tile_rows * tile_cols;
+  a.m.segments = 1;
+  for (int i = 0; i < se12::kMaxSegments; ++i) a.m.seg_end[i] = INT32_MAX;
   a.x = x;
   a.ldx = ldx;
   a.batch = batch;

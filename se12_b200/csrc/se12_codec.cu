@@ -153,8 +153,8 @@ struct DecodeCodebook {
 // One 256-thread block per pair of tiles; thread -> (tile, local row, 32 columns).
 __global__ void __launch_bounds__(256) decode_kernel(const __grid_constant__ MatrixView m, uint16_t* __restrict__ out,
                                                      int ldo) {
-  __shared__ uint32_t lut[256];
-  for (int i = threadIdx.x; i < 256; i += blockDim.x) lut[i] = pair_entry(m.codebook, i);
+  __shared__ uint32_t lut[kMaxSegments][256];  // per segment
+  for (int i = threadIdx.x; i < 256 * m.segments; i += blockDim.x) lut[i >> 8][i & 255] = pair_entry(m.codebooks[i >> 8], i & 255);
   __syncthreads();
   const int tile = blockIdx.x * 2 + (threadIdx.x >> 7);
   if (tile >= m.tiles) return;
@@ -180,7 +180,7 @@ __global__ void __launch_bounds__(256) decode_kernel(const __grid_constant__ Mat
   } else {
     const uint4* smp = reinterpret_cast<const uint4*>(m.sm + static_cast<size_t>(tile) * kTileSize + r * kTileCols + c0);
     const uint4* ecp = reinterpret_cast<const uint4*>(m.ec + static_cast<size_t>(tile) * (kTileSize / 2) + r * 128 + c0 / 2);
-    decode32(__ldg(smp), __ldg(smp + 1), __ldg(ecp), lut, words);
+    decode32(__ldg(smp), __ldg(smp + 1), __ldg(ecp), lut[segment_of(m, tr)], words);
   }
   uint16_t* dst = out + static_cast<size_t>(grow) * ldo + gcol;
   const int valid = min(32, m.cols - gcol);
@@ -223,8 +223,8 @@ cudaError_t launch_decode(const MatrixView& m, uint16_t* out, int ldo, cudaStrea
 __global__ void __launch_bounds__(64) decode_rows_kernel(const __grid_constant__ MatrixView m,
                                                          const int32_t* __restrict__ rows, int nrows,
                                                          uint16_t* __restrict__ out, int ldo) {
-  __shared__ uint32_t lut[256];
-  for (int i = threadIdx.x; i < 256; i += blockDim.x) lut[i] = pair_entry(m.codebook, i);
+  __shared__ uint32_t lut[kMaxSegments][256];  // per segment
+  for (int i = threadIdx.x; i < 256 * m.segments; i += blockDim.x) lut[i >> 8][i & 255] = pair_entry(m.codebooks[i >> 8], i & 255);
   __syncthreads();
   const int req = blockIdx.x * 8 + (threadIdx.x >> 3);
   const int kt = blockIdx.y;
@@ -254,7 +254,7 @@ __global__ void __launch_bounds__(64) decode_rows_kernel(const __grid_constant__
   } else {
     const uint4* smp = reinterpret_cast<const uint4*>(m.sm + static_cast<size_t>(tile) * kTileSize + r * kTileCols + c0);
     const uint4* ecp = reinterpret_cast<const uint4*>(m.ec + static_cast<size_t>(tile) * (kTileSize / 2) + r * 128 + c0 / 2);
-    decode32(__ldg(smp), __ldg(smp + 1), __ldg(ecp), lut, words);
+    decode32(__ldg(smp), __ldg(smp + 1), __ldg(ecp), lut[segment_of(m, tr)], words);
   }
   uint16_t* dst = out + static_cast<size_t>(req) * ldo + gcol;
   const int valid = min(32, m.cols - gcol);

@@ -220,6 +220,14 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
     }
     fence_barrier_init();
   }
+  // decode table of each segment: table_byte of codes 0..15, four per word
+  __shared__ uint4 seg_tab[kMaxSegments];
+  if (!RAW && tid < a.m.segments) {
+    uint32_t w[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+    for (int c = 0; c < 16; ++c) w[c >> 2] |= table_byte(a.m.codebooks[tid], c) << (8 * (c & 3));
+    seg_tab[tid] = make_uint4(w[0], w[1], w[2], w[3]);
+  }
   if (XRES) {
     // columns kpad8 .. 256 KT - 1 of every resident x row are zero
     const int tail = KT * kTileCols - kpad8;  // a multiple of 8 columns
@@ -481,14 +489,13 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
   const int jw = FULL ? warp : (warp >> 1);  // tile of the stage this warp multiplies
   const int hw = FULL ? 0 : (warp & 1);      // its (first) half
   const int g = lane >> 2, t = lane & 3;
-  // an infinite padding weight needs its code rewritten (force_padding_escapes)
-  const bool pad_inf = !RAW && (K & (kTileCols - 1)) && a.m.codebook[0] == 255;
-  // decode table: table_byte of codes 0..15, four per register
+  // decode table of the current tile's segment (seg_tab[cur_seg]), loaded
+  // when a tile of another segment comes up
   uint32_t tab[4] = {0u, 0u, 0u, 0u};
-  if (!RAW) {
-#pragma unroll
-    for (int c = 0; c < 16; ++c) tab[c >> 2] |= table_byte(a.m.codebook, c) << (8 * (c & 3));
-  }
+  int cur_seg = -1;
+  // an infinite padding weight needs its code rewritten (force_padding_escapes):
+  // codebook[0] of the segment is 255, whose table byte is 0xFF
+  bool pad_inf = false;
 
   // Per-thread shared-memory offsets (stage 0, tile jw, half hw), fixed for
   // the kernel. Thread (g, t) owns rows g, g + 8 of its tile and, in a half,
@@ -720,7 +727,23 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
     }
     if (ok) ok = mbar_wait(&full[s], ph);
     kt_mine = kt0 + jw;
-    while (kt_mine >= KT) kt_mine -= KT;
+    int tr_mine = tr0;
+    while (kt_mine >= KT) {
+      kt_mine -= KT;
+      ++tr_mine;
+    }
+    if (!RAW) {
+      const int seg = segment_of(a.m, tr_mine);
+      if (seg != cur_seg) {
+        const uint4 v = seg_tab[seg];
+        tab[0] = v.x;
+        tab[1] = v.y;
+        tab[2] = v.z;
+        tab[3] = v.w;
+        pad_inf = (K & (kTileCols - 1)) && (v.x & 0xFFu) == 0xFFu;
+        cur_seg = seg;
+      }
+    }
     if (jw < ntl && ok) load_frags(s, kt_mine, fbi, 0);
   };
 

@@ -10,6 +10,14 @@
 namespace se12 {
 
 // One SE12 matrix on the device, as the kernels see it.
+// A matrix may be segmented: the tile-major concatenation of up to
+// kMaxSegments matrices with the same columns (for example the q, k and v
+// projections of one attention block, which share their input), each with
+// its own codebook. Segment s covers tile rows [seg_end[s - 1], seg_end[s]);
+// every segment but the last has a multiple of 16 rows. An unsegmented
+// matrix is one segment.
+constexpr int kMaxSegments = 4;
+
 struct MatrixView {
   const uint8_t* sm;               // [T*4096] tile-major sign|mantissa bytes
   const uint8_t* ec;               // [T*2048] packed 4-bit codes
@@ -21,8 +29,16 @@ struct MatrixView {
   int rows, cols;                  // N, K (unpadded)
   int tile_rows, tile_cols;        // ceil(N/16), ceil(K/256)
   int tiles;                       // tile_rows * tile_cols
-  uint8_t codebook[16];            // 15 entries + 1 pad
+  int segments;                    // 1..kMaxSegments
+  int seg_end[kMaxSegments];       // exclusive end tile row of each segment (INT32_MAX past the last)
+  uint8_t codebooks[kMaxSegments][16];  // per segment: 15 entries + 1 pad
 };
+
+// Segment of tile row tr.
+static_assert(kMaxSegments == 4, "segment_of compares against three segment ends");
+__host__ __device__ __forceinline__ int segment_of(const MatrixView& m, int tr) {
+  return (tr >= m.seg_end[0]) + (tr >= m.seg_end[1]) + (tr >= m.seg_end[2]);
+}
 
 // Arguments of one fused (or dense baseline) GEMV launch: y = x . W^T.
 struct GemvArgs {

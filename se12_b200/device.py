@@ -57,16 +57,30 @@ class _WorkspacePool:
 WORKSPACES = _WorkspacePool()
 
 
+MAX_SEGMENTS = 4
+
+
 class DeviceSe12Matrix:
-    """An SE12-encoded [rows, cols] BF16 matrix resident on one GPU."""
+    """An SE12-encoded [rows, cols] BF16 matrix resident on one GPU.
+
+    ``segments`` (optional) makes it a segmented matrix: the streams are the
+    tile-major concatenation of several SE12 matrices with the same columns,
+    given as ``[(rows_i, codebook_i), ...]``; ``codebook`` is then ignored.
+    ``concatenate`` builds one from separate matrices.
+    """
 
     def __init__(self, rows: int, cols: int, codebook, sm: torch.Tensor, ec: torch.Tensor, esc: torch.Tensor,
-                 fallback_bitmap: torch.Tensor, fallback_raw: torch.Tensor):
+                 fallback_bitmap: torch.Tensor, fallback_raw: torch.Tensor, segments=None):
         lib = _lib.load()
         self.rows, self.cols = int(rows), int(cols)
-        self.codebook = tuple(int(v) for v in codebook)
-        if len(self.codebook) != CODEBOOK_SIZE:
+        if segments is None:
+            segments = [(self.rows, codebook)]
+        self.segments = tuple((int(r), tuple(int(v) for v in book)) for r, book in segments)
+        if not 1 <= len(self.segments) <= MAX_SEGMENTS:
+            raise ValueError(f"1..{MAX_SEGMENTS} segments, got {len(self.segments)}")
+        if any(len(book) != CODEBOOK_SIZE for _, book in self.segments):
             raise ValueError("codebook must have 15 entries")
+        self.codebook = self.segments[0][1]
         self.device = sm.device
         tr, tc = tile_grid(self.rows, self.cols)
         self.tile_rows, self.tile_cols, self.tiles = tr, tc, tr * tc
@@ -96,9 +110,13 @@ class DeviceSe12Matrix:
         s.sm, s.ec, s.esc = self.sm.data_ptr(), self.ec.data_ptr(), self.esc.data_ptr()
         s.fallback_bitmap, s.fallback_raw = self.fallback_bitmap.data_ptr(), self.fallback_raw.data_ptr()
         s.escape_pos, s.fallback_index = self.escape_pos.data_ptr(), self.fallback_index.data_ptr()
+        nseg = len(self.segments)
+        seg_rows = (ctypes.c_int32 * nseg)(*[r for r, _ in self.segments])
+        books = (ctypes.c_uint8 * (nseg * CODEBOOK_SIZE))(*[v for _, book in self.segments for v in book])
         handle = ctypes.c_void_p()
         with torch.cuda.device(self.device):
-            _lib.check(lib.se12_matrix_create(ctypes.byref(s), ctypes.byref(handle)), "se12_matrix_create")
+            _lib.check(lib.se12_matrix_create_segmented(ctypes.byref(s), nseg, seg_rows, books, ctypes.byref(handle)),
+                       "se12_matrix_create_segmented")
             self._handle = handle
             self._finalizer = weakref.finalize(self, lib.se12_matrix_destroy, handle)
             _lib.check(lib.se12_matrix_prepare(handle, ctypes.c_void_p(stream_handle(self.device))), "se12_matrix_prepare")
@@ -116,8 +134,38 @@ class DeviceSe12Matrix:
         return cls(t.rows, t.cols, t.codebook, up(t.sm, np.uint8), up(t.ec, np.uint8), up(t.esc, np.uint8),
                    up(t.fallback_bitmap, np.uint8), up(t.fallback_raw, np.int16))
 
+    @classmethod
+    def concatenate(cls, matrices) -> "DeviceSe12Matrix":
+        """One segmented matrix holding ``matrices`` (same columns, same GPU;
+        every one but the last with a multiple of 16 rows) one after the
+        other, so that one GEMV computes all of them: y = [y_0 | y_1 | ...].
+        The streams are copied; each segment keeps its codebook and its
+        bytes are the matrix's own."""
+        mats = list(matrices)
+        if not mats:
+            raise ValueError("nothing to concatenate")
+        cols, device = mats[0].cols, mats[0].device
+        for i, m in enumerate(mats):
+            if m.cols != cols or m.device != device:
+                raise ValueError("segments need the same columns and device")
+            if i + 1 < len(mats) and m.rows % TILE_ROWS:
+                raise ValueError("every segment but the last needs a multiple of 16 rows")
+        segments = [seg for m in mats for seg in m.segments]
+        if len(segments) > MAX_SEGMENTS:
+            raise ValueError(f"at most {MAX_SEGMENTS} segments")
+        shifts = torch.arange(7, -1, -1, device=device, dtype=torch.uint8)
+        bits = torch.cat([((m.fallback_bitmap.unsqueeze(1) >> shifts) & 1).reshape(-1)[: m.tiles] for m in mats])
+        tiles = bits.numel()
+        bits = torch.nn.functional.pad(bits, (0, (-tiles) % 8)).reshape(-1, 8)
+        bitmap = (bits << shifts).sum(dim=1, dtype=torch.int32).to(torch.uint8)
+        raw = torch.cat([m.fallback_raw[: m.fallback_tiles * TILE_SIZE] for m in mats])
+        return cls(sum(m.rows for m in mats), cols, segments[0][1], torch.cat([m.sm for m in mats]),
+                   torch.cat([m.ec for m in mats]), torch.cat([m.esc for m in mats]), bitmap, raw, segments=segments)
+
     def to_tensor(self) -> Se12Tensor:
         """Host copy of the streams as an Se12Tensor."""
+        if len(self.segments) > 1:
+            raise ValueError("a segmented matrix has one codebook per segment: no single Se12Tensor holds it")
         raw = self.fallback_raw[: self.fallback_tiles * TILE_SIZE]
         return make_tensor(self.rows, self.cols, self.codebook, self.sm.cpu().numpy(), self.ec.cpu().numpy(),
                            self.esc.cpu().numpy(), self.fallback_bitmap.cpu().numpy(), raw.cpu().numpy())
@@ -129,8 +177,11 @@ class DeviceSe12Matrix:
     @property
     def byte_size(self) -> int:
         """Algorithmic SE12 bytes: five streams + 15 codebook bytes."""
-        return (self.sm.numel() + self.ec.numel() + self.esc.numel() + self.fallback_bitmap.numel()
-                + self.fallback_tiles * TILE_SIZE * 2 + CODEBOOK_SIZE)
+        # a segmented matrix counts each segment's own bitmap and codebook,
+        # the bytes its separate tensor has
+        bitmaps = sum((tile_grid(rows, self.cols)[0] * self.tile_cols + 7) // 8 for rows, _ in self.segments)
+        return (self.sm.numel() + self.ec.numel() + self.esc.numel() + bitmaps
+                + self.fallback_tiles * TILE_SIZE * 2 + CODEBOOK_SIZE * len(self.segments))
 
     # ------------------------------------------------------------------ compute
     def gemv(self, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:

@@ -19,6 +19,10 @@ built).
 * ``compress_model(model)`` swaps every eligible layer of a live model;
   ``load_packed(packed_dir, model)`` fills a model skeleton from a packed
   directory written by ``lws.pack`` or ``se12_b200.packed.pack_model``.
+  With ``group=True`` (the default) the projections of one block that read
+  the same input (q/k/v, gate/up) share one segmented matrix: the first of
+  them to run computes all of their outputs in one fused GEMV and the
+  others take their rows of it.
 
 No CPU path: every compressed layer needs the CUDA library.
 """
@@ -42,14 +46,55 @@ def _check_mode(mode: str) -> str:
     return mode
 
 
-class CompressedLinear(torch.nn.Module):
-    """``nn.Linear`` whose weight lives on the GPU as SE12 streams only."""
+class ProjectionGroup:
+    """Projections that multiply the same input, held as one segmented
+    matrix (``DeviceSe12Matrix.concatenate`` of their own matrices).
 
-    def __init__(self, matrix: DeviceSe12Matrix, bias: torch.Tensor | None = None, mode: str = "auto"):
+    ``output(member, x)`` returns the whole group's fused GEMV of x. The
+    result of a call is kept for the other members: each of them takes it
+    once, for an input with the same storage, version, shape and stream;
+    any other call computes afresh. So a block that runs q_proj, k_proj and
+    v_proj on one hidden state (also while a CUDA graph captures it) runs one
+    GEMV."""
+
+    def __init__(self, matrix: DeviceSe12Matrix, members: tuple):
+        self.matrix = matrix
+        self.members = tuple(members)
+        self._key = None
+        self._y = None
+        self._pending: set = set()
+
+    @staticmethod
+    def _key_of(x: torch.Tensor):
+        return (x.data_ptr(), x._version, tuple(x.shape), x.dtype, torch.cuda.current_stream(x.device).cuda_stream)
+
+    def output(self, member: str, x: torch.Tensor) -> torch.Tensor:
+        key = self._key_of(x)
+        if member in self._pending and key == self._key:
+            self._pending.discard(member)
+            return self._y
+        self._y = self.matrix.gemv(x)
+        self._key = key
+        self._pending = set(self.members) - {member}
+        return self._y
+
+
+class CompressedLinear(torch.nn.Module):
+    """``nn.Linear`` whose weight lives on the GPU as SE12 streams only.
+
+    With ``group`` the weight is rows ``rows`` of the group's segmented
+    matrix (its own segment): the fused path takes its slice of the group's
+    GEMV, the exact path decodes just those rows."""
+
+    def __init__(self, matrix: DeviceSe12Matrix, bias: torch.Tensor | None = None, mode: str = "auto",
+                 group: ProjectionGroup | None = None, member: str | None = None, rows: tuple | None = None):
         super().__init__()
         self.matrix = matrix
-        self.in_features, self.out_features = matrix.cols, matrix.rows
+        self.group, self.member = group, member
+        self.row_range = tuple(rows) if rows is not None else (0, matrix.rows)
+        self.in_features, self.out_features = matrix.cols, self.row_range[1] - self.row_range[0]
         self.mode = _check_mode(mode)
+        self._row_ids = None
         if bias is not None:
             self.register_buffer("bias", bias.detach().to(matrix.device))
         else:
@@ -70,15 +115,23 @@ class CompressedLinear(torch.nn.Module):
 
     def weight_bf16(self) -> torch.Tensor:
         """The exact BF16 weight, decoded on the GPU (transient)."""
-        return self.matrix.decode()
+        if self.group is None:
+            return self.matrix.decode()
+        if self._row_ids is None:
+            self._row_ids = torch.arange(*self.row_range, dtype=torch.int32, device=self.matrix.device)
+        return self.matrix.decode_rows(self._row_ids)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         rows = x.numel() // self.in_features if self.in_features else 0
         if self.mode == "exact" or (self.mode == "auto" and rows > FUSED_MAX_ROWS):
-            w = self.matrix.decode()
+            w = self.weight_bf16()
             return F.linear(x, w if x.dtype == torch.bfloat16 else w.to(x.dtype), self.bias)
         lead = x.shape[:-1]
-        y = self.matrix.gemv(x.reshape(-1, self.in_features))
+        x2 = x.reshape(-1, self.in_features)
+        if self.group is None:
+            y = self.matrix.gemv(x2)
+        else:
+            y = self.group.output(self.member, x2)[:, self.row_range[0]:self.row_range[1]]
         if self.bias is not None:
             y = y + self.bias.float()
         return y.to(x.dtype).reshape(*lead, self.out_features)
@@ -134,10 +187,44 @@ def _set_module(model: torch.nn.Module, name: str, module: torch.nn.Module) -> N
     setattr(parent, child, module)
 
 
-def compress_model(model: torch.nn.Module, mode: str = "auto", device="cuda", embeddings: bool = True) -> torch.nn.Module:
+# Sibling projections that read the same input: (member names), grouped
+# when a module has all of them as BF16 linears with one in_features.
+GROUPABLE = (("q_proj", "k_proj", "v_proj"), ("gate_proj", "up_proj"))
+
+
+def group_projections(model: torch.nn.Module) -> int:
+    """Replaces each set of sibling ``CompressedLinear`` projections that
+    read the same input (``GROUPABLE``) by members of one
+    ``ProjectionGroup``; their separate matrices are released. Returns the
+    number of groups made."""
+    made = 0
+    for parent_name, parent in list(model.named_modules()):
+        for names in GROUPABLE:
+            mods = [getattr(parent, n, None) for n in names]
+            if not all(isinstance(m, CompressedLinear) and m.group is None for m in mods):
+                continue
+            mats = [m.matrix for m in mods]
+            if len({id(m) for m in mats}) != len(mats) or len({m.cols for m in mats}) != 1:
+                continue
+            if any(m.rows % 16 for m in mats[:-1]) or sum(len(m.segments) for m in mats) > 4:
+                continue
+            group = ProjectionGroup(DeviceSe12Matrix.concatenate(mats), names)
+            r0 = 0
+            for n, m in zip(names, mods):
+                r1 = r0 + m.out_features
+                setattr(parent, n, CompressedLinear(group.matrix, m.bias, m.mode, group=group, member=n, rows=(r0, r1)))
+                r0 = r1
+            made += 1
+    return made
+
+
+def compress_model(model: torch.nn.Module, mode: str = "auto", device="cuda", embeddings: bool = True,
+                   group: bool = True) -> torch.nn.Module:
     """Replaces every BF16 ``nn.Linear`` (and, with ``embeddings``, every BF16
     ``nn.Embedding``) of ``model`` in place. Layers that share one weight
-    tensor (a tied embedding and LM head) share one set of streams."""
+    tensor (a tied embedding and LM head) share one set of streams. With
+    ``group``, sibling projections that read the same input share one
+    segmented matrix (``group_projections``)."""
     _check_mode(mode)
     shared: dict = {}
     targets = [(n, m) for n, m in model.named_modules() if isinstance(m, (torch.nn.Linear, torch.nn.Embedding))]
@@ -157,10 +244,14 @@ def compress_model(model: torch.nn.Module, mode: str = "auto", device="cuda", em
             _set_module(model, name, CompressedLinear(matrix, mod.bias, mode))
         else:
             _set_module(model, name, CompressedEmbedding(matrix, mod.padding_idx, _embed_scale(mod)))
-    return model.to(device)
+    model = model.to(device)
+    if group:
+        group_projections(model)
+    return model
 
 
-def load_packed(packed_dir: str | pathlib.Path, model: torch.nn.Module, mode: str = "auto", device="cuda") -> torch.nn.Module:
+def load_packed(packed_dir: str | pathlib.Path, model: torch.nn.Module, mode: str = "auto", device="cuda",
+                group: bool = True) -> torch.nn.Module:
     """Fills ``model`` from a packed directory: each ``nn.Linear`` /
     ``nn.Embedding`` whose ``<name>.weight`` is an SE12 entry becomes a
     compressed layer over those streams (no BF16 copy of the weight stays on
@@ -169,7 +260,7 @@ def load_packed(packed_dir: str | pathlib.Path, model: torch.nn.Module, mode: st
     from the file, as transformers saves tied weights once) shares that
     embedding's streams. ``model`` must be materialised (CPU or GPU, any
     initial values): its own buffers computed at construction, such as
-    rotary tables, are kept."""
+    rotary tables, are kept. ``group`` as for ``compress_model``."""
     from .format import Se12Tensor
     from .packed import read_packed
 
@@ -209,7 +300,10 @@ def load_packed(packed_dir: str | pathlib.Path, model: torch.nn.Module, mode: st
         for k, v in state.items():
             if k in own and own[k].shape == v.shape:
                 own[k].copy_(v.to(device))
+    if group:
+        group_projections(model)
     return model
 
 
-__all__ = ["CompressedEmbedding", "CompressedLinear", "FUSED_MAX_ROWS", "compress_model", "load_packed"]
+__all__ = ["CompressedEmbedding", "CompressedLinear", "FUSED_MAX_ROWS", "GROUPABLE", "ProjectionGroup", "compress_model",
+           "group_projections", "load_packed"]

@@ -34,6 +34,10 @@ class DecoderShapes:
             ("down_proj", h, i, "mlp"),
         ]
 
+    # Projections that multiply the same input, computed as one segmented
+    # matrix (one GEMV) when grouped: (group name, member names).
+    GROUPS = (("qkv_proj", ("q_proj", "k_proj", "v_proj")), ("gate_up_proj", ("gate_proj", "up_proj")))
+
     def lm_head(self) -> tuple:
         return ("lm_head", self.vocab, self.hidden, "hidden")
 

@@ -108,3 +108,60 @@ def test_packed_round_trip_into_fresh_model(tmp_path):
         want = ref.cuda()(ids).logits
         got = fresh(ids).logits
     assert torch.equal(got.view(torch.int16), want.view(torch.int16))
+
+
+@pytest.mark.gpu
+def test_grouped_projections_run_one_gemv_per_group():
+    """q/k/v and gate/up become one segmented matrix each; a block's
+    projections of one input run one fused GEMV, and the logits match both
+    the ungrouped fused model and the original within the fused tolerance."""
+    from se12_b200.runtime import ProjectionGroup, compress_model
+
+    ref = tiny_gemma().cuda()
+    ids = torch.randint(0, 1024, (1, 1), device="cuda", generator=torch.Generator("cuda").manual_seed(4))
+    grouped = compress_model(copy.deepcopy(ref), mode="fused")
+    plain = compress_model(copy.deepcopy(ref), mode="fused", group=False)
+    attn, mlp = grouped.model.layers[0].self_attn, grouped.model.layers[0].mlp
+    assert attn.q_proj.group is attn.k_proj.group is attn.v_proj.group is not None
+    assert mlp.gate_proj.group is mlp.up_proj.group is not None and mlp.down_proj.group is None
+    assert len(attn.q_proj.matrix.segments) == 3
+    for name in ("q_proj", "k_proj", "v_proj"):  # each member's rows decode to its own weight
+        want = getattr(ref.model.layers[0].self_attn, name).weight
+        assert torch.equal(getattr(attn, name).weight_bf16().view(torch.int16), want.view(torch.int16))
+
+    calls = []
+    for mod in grouped.modules():
+        if isinstance(getattr(mod, "group", None), ProjectionGroup) and mod.group not in calls:
+            group, gemv = mod.group, mod.group.matrix.gemv
+            group.matrix.gemv = lambda x, out=None, _g=gemv: (calls.append(1), _g(x, out))[1]
+            calls.append(group)
+    groups = sum(1 for c in calls if c != 1)
+    del calls[:]
+    with torch.no_grad():
+        want = ref(ids).logits.float()
+        got = grouped(ids).logits.float()
+        base = plain(ids).logits.float()
+    assert len(calls) == groups == 2 * 2  # two layers x (qkv, gate_up), one GEMV each
+    for other in (want, base):
+        err = ((got - other).abs() / other.abs().clamp_min(1.0)).max().item()
+        assert err <= 2e-2, err
+    assert torch.equal(got.argmax(-1), want.argmax(-1))
+
+
+@pytest.mark.gpu
+def test_projection_group_recomputes_for_a_new_input():
+    from se12_b200.runtime import compress_model
+
+    model = compress_model(tiny_gemma().cuda(), mode="fused")
+    attn = model.model.layers[0].self_attn
+    x1 = torch.randn(1, 256, device="cuda").to(torch.bfloat16)
+    x2 = torch.randn(1, 256, device="cuda").to(torch.bfloat16)
+    with torch.no_grad():
+        q1 = attn.q_proj(x1)
+        k2 = attn.k_proj(x2)  # another input: not the cached result
+        k2_alone = attn.k_proj(x2)
+        x1.mul_(2)  # same storage, new version
+        q1b = attn.q_proj(x1)
+    assert torch.equal(k2, k2_alone)
+    assert not torch.equal(q1, q1b)
+    assert torch.allclose(q1b.float(), 2 * q1.float(), rtol=1e-2, atol=1e-2)
