@@ -43,12 +43,13 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "SE12 decode+GEMV HBM GB/s (compressed bytes)"
 # DRAM bytes (read + write) per algorithmic byte of the fused GEMV, from one
-# ncu capture of this script's lm_head GEMV (--layers 0: 256000 x 2304,
-# batch 1): 896.71 MB of DRAM traffic for 888.09 MB of SE12 streams + x + y;
-# the difference is the derived escape-position table, the fallback index
-# and the stream-K partials. The step's GEMVs stream the same kinds of data
-# in proportion, so the step's traffic is scaled from it by algorithmic bytes.
-DRAM_BYTES_PER_ALGORITHMIC_BYTE = 896.71 / 888.09
+# ncu capture of this script's lm_head GEMV (--layers 0 --eager: 256000 x
+# 2304, batch 1): 901.10 MB of DRAM traffic for 888.09 MB of SE12 streams +
+# x + y; the difference is mostly the derived escape-position table (32 B
+# per tile) and the fallback index. The step's GEMVs stream the same kinds of
+# data in proportion, so the step's traffic is scaled from it by algorithmic
+# bytes.
+DRAM_BYTES_PER_ALGORITHMIC_BYTE = 901.10 / 888.09
 NOMINAL_HBM_GBS = 8000.0
 
 
@@ -65,6 +66,8 @@ def parse_args():
     p.add_argument("--no-dense", action="store_true", help="skip the dense BF16 comparisons")
     p.add_argument("--layers", type=int, default=None, help="override the layer count (profiling small cases)")
     p.add_argument("--no-lm-head", action="store_true")
+    p.add_argument("--eager", action="store_true",
+                   help="issue each step's launches one by one instead of replaying a CUDA graph (profiler runs)")
     p.add_argument("--no-group", action="store_true",
                    help="one GEMV per projection instead of q/k/v and gate/up as one segmented matrix each")
     p.add_argument("--tp", action="store_true",
@@ -323,10 +326,16 @@ def build_stack(torch, shapes, batch, device, layers, lm_head, keep_dense, seed_
     return mats, dense
 
 
-def time_stack(torch, stack, steps, warmup, device, sampler=None):
-    stack.capture()
+def time_stack(torch, stack, steps, warmup, device, sampler=None, eager=False):
+    """Device time of `steps` steps (one graph replay each; with `eager`, the
+    same launches issued one by one on the current stream)."""
+    if eager:
+        run = stack.run
+    else:
+        stack.capture()
+        run = stack.replay
     for _ in range(warmup):
-        stack.replay()
+        run()
     torch.cuda.synchronize()
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
@@ -334,7 +343,7 @@ def time_stack(torch, stack, steps, warmup, device, sampler=None):
     with ctx:
         start.record()
         for _ in range(steps):
-            stack.replay()
+            run()
         end.record()
         torch.cuda.synchronize()
     return start.elapsed_time(end)  # ms over `steps`
@@ -412,7 +421,7 @@ def run_ours(args) -> None:
     if world > 1:
         torch.distributed.barrier()
     torch.cuda.synchronize()
-    elapsed_ms = time_stack(torch, stack, args.steps, args.warmup, device, sampler)
+    elapsed_ms = time_stack(torch, stack, args.steps, args.warmup, device, sampler, eager=args.eager)
     if world > 1:
         torch.distributed.barrier()
         t = torch.tensor([elapsed_ms], device=device, dtype=torch.float64)
@@ -433,7 +442,7 @@ def run_ours(args) -> None:
         if b == batch:
             continue
         st_b, _, _ = stack_for(b)
-        ms = time_stack(torch, st_b, max(3, args.steps // 4), 3, device) / max(3, args.steps // 4)
+        ms = time_stack(torch, st_b, max(3, args.steps // 4), 3, device, eager=args.eager) / max(3, args.steps // 4)
         extra[f"batch{b}"] = {"ms_per_step": ms, "gbs": step_bytes(b) / (ms * 1e-3) / 1e9,
                               "bf16_equiv_gbs": (2 * weights + b * sum(m.cols * 2 + m.rows * 4 for _, m, _ in mats)) / (ms * 1e-3) / 1e9,
                               "tok_s": b / (ms * 1e-3)}
@@ -477,7 +486,8 @@ def run_ours(args) -> None:
         del g, outs_c
     # ----------------------------------------------------------- e2e through the public API
     e2e_stack, e2e_xs, e2e_outs = stack_for(batch)
-    e2e_stack.capture()
+    if not args.eager:
+        e2e_stack.capture()
     host_in = {k: torch.empty(v.shape, dtype=v.dtype, pin_memory=True).copy_(v.cpu()) for k, v in e2e_xs.items()}
     logits = e2e_outs[-1]
     host_out = torch.empty(logits.shape, dtype=logits.dtype, pin_memory=True)
@@ -489,7 +499,10 @@ def run_ours(args) -> None:
         with torch.cuda.stream(s_e2e):
             for k, v in host_in.items():
                 e2e_xs[k].copy_(v, non_blocking=True)
-            e2e_stack.graph.replay()
+            if args.eager:
+                e2e_stack.run()
+            else:
+                e2e_stack.graph.replay()
             host_out.copy_(logits, non_blocking=True)
         s_e2e.synchronize()
 
@@ -512,10 +525,12 @@ def run_ours(args) -> None:
         import se12_oracle as oracle
 
         host_streams = []
-        for (name, m, kind) in mats[:7]:
-            t = m.to_tensor()
-            host_streams.append((oracle.Streams(rows=t.rows, cols=t.cols, codebook=t.codebook, sm=t.sm, ec=t.ec, esc=t.esc,
-                                                fallback_bitmap=t.fallback_bitmap, fallback_raw=t.fallback_raw), kind))
+        for (name, m, kind) in mats:  # the first layer's seven matrices (segments of a group included)
+            for t in m.segment_tensors():
+                if len(host_streams) < 7:
+                    host_streams.append((oracle.Streams(rows=t.rows, cols=t.cols, codebook=t.codebook, sm=t.sm, ec=t.ec,
+                                                        esc=t.esc, fallback_bitmap=t.fallback_bitmap,
+                                                        fallback_raw=t.fallback_raw), kind))
         res = cpu_baseline_sample(shapes, batch, steps=2, warmup=1, host_streams=host_streams)
         cpu = {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")}
 
@@ -546,7 +561,8 @@ def run_ours(args) -> None:
                 "bits_per_weight": 8 * se12_bytes / weights,
                 "bytes_per_step": bytes_per_step,
                 "l2": "inputs larger than L2 (every step streams all SE12 bytes once)",
-                "graph": "one CUDA graph per step, programmatic dependent launch between GEMVs",
+                "graph": "eager launches, programmatic dependent launch between GEMVs" if args.eager else
+                "one CUDA graph per step, programmatic dependent launch between GEMVs",
                 "parallelism": f"sharded x{world}: every rank streams its own full step of distinct weights, "
                 "no collective" if world > 1 else "single GPU",
                 "setup_seconds": setup_s,
@@ -563,12 +579,14 @@ def run_ours(args) -> None:
                 "frac": achieved / peak,
                 "traffic": bytes_per_step * DRAM_BYTES_PER_ALGORITHMIC_BYTE,
                 "traffic_unit": "bytes per step (all launches), scaled from the ncu capture of the lm_head GEMV",
-                "kernel": f"se12::gemv_kernel<{1 if batch <= 8 else 2},SE12,x resident> (all {len(mats)} launches of the step)",
+                "kernel": f"se12::gemv_kernel<{1 if batch <= 8 else 2},SE12,...> (all {len(mats)} launches of the step, "
+                "4- and 8-tile-stage variants)",
                 "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)" if "source" not in peaks else "fallback",
             },
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "ms_per_step": e2e_s * 1e3, "api": "se12_b200.stack.GemvStack graph replay, pinned H2D inputs, D2H logits, sync per step"},
+                    "ms_per_step": e2e_s * 1e3, "api": "se12_b200.stack.GemvStack " + ("eager launches" if args.eager else "graph replay")
+                    + ", pinned H2D inputs, D2H logits, sync per step"},
             "gpu_launches": launches * args.steps,
             "clocks": sampler.summary(),
             "other_batches": extra,

@@ -162,10 +162,28 @@ class DeviceSe12Matrix:
         return cls(sum(m.rows for m in mats), cols, segments[0][1], torch.cat([m.sm for m in mats]),
                    torch.cat([m.ec for m in mats]), torch.cat([m.esc for m in mats]), bitmap, raw, segments=segments)
 
+    def segment_tensors(self) -> list:
+        """Host copies of the segments as separate Se12Tensors (the tensors
+        ``concatenate`` was given)."""
+        shifts = np.arange(7, -1, -1, dtype=np.uint8)
+        bits = ((self.fallback_bitmap.cpu().numpy()[:, None] >> shifts) & 1).reshape(-1)[: self.tiles]
+        sm, ec, esc = self.sm.cpu().numpy(), self.ec.cpu().numpy(), self.esc.cpu().numpy()
+        raw = self.fallback_raw[: self.fallback_tiles * TILE_SIZE].cpu().numpy()
+        out, t0, f0 = [], 0, 0
+        for rows, book in self.segments:
+            t1 = t0 + tile_grid(rows, self.cols)[0] * self.tile_cols
+            seg_bits = bits[t0:t1]
+            f1 = f0 + int(seg_bits.sum())
+            out.append(make_tensor(rows, self.cols, book, sm[t0 * TILE_SIZE:t1 * TILE_SIZE],
+                                   ec[t0 * TILE_SIZE // 2:t1 * TILE_SIZE // 2], esc[t0 * ESCAPE_BUDGET:t1 * ESCAPE_BUDGET],
+                                   np.packbits(seg_bits.astype(np.uint8)), raw[f0 * TILE_SIZE:f1 * TILE_SIZE]))
+            t0, f0 = t1, f1
+        return out
+
     def to_tensor(self) -> Se12Tensor:
         """Host copy of the streams as an Se12Tensor."""
         if len(self.segments) > 1:
-            raise ValueError("a segmented matrix has one codebook per segment: no single Se12Tensor holds it")
+            raise ValueError("a segmented matrix has one codebook per segment: use segment_tensors()")
         raw = self.fallback_raw[: self.fallback_tiles * TILE_SIZE]
         return make_tensor(self.rows, self.cols, self.codebook, self.sm.cpu().numpy(), self.ec.cpu().numpy(),
                            self.esc.cpu().numpy(), self.fallback_bitmap.cpu().numpy(), raw.cpu().numpy())

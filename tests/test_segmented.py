@@ -110,6 +110,11 @@ def test_segmented_matrix_keeps_the_byte_count_of_its_parts():
     assert seg.byte_size == sum(p[3].byte_size for p in parts)
     assert seg.tiles == sum(p[3].tiles for p in parts)
     assert seg.fallback_tiles == sum(p[3].fallback_tiles for p in parts) > 0
+    for part, back in zip(parts, seg.segment_tensors()):  # the segments come back as the tensors given
+        want = part[3].to_tensor()
+        assert (back.rows, back.cols, back.codebook) == (want.rows, want.cols, want.codebook)
+        for name in ("sm", "ec", "esc", "fallback_bitmap", "fallback_raw"):
+            assert np.array_equal(np.asarray(getattr(back, name)).reshape(-1), np.asarray(getattr(want, name)).reshape(-1)), name
 
 
 def test_concatenate_rejects_what_cannot_be_one_matrix():
