@@ -624,6 +624,33 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
     }
   };
 
+  // Decodes half hw + h of this warp's tile of stage s and multiplies it
+  // with x one 32-column group at a time, so that only one group's
+  // fragments are live (8 registers) and the compiler can overlap a group's
+  // decode with the previous group's MMAs. SE12 tiles that are neither
+  // fallback tiles nor hold infinite padding weights.
+  auto decode_mma = [&](int s, int kt, int h) {
+    const uint32_t wst = o_w + s * kWeightBytes;
+    const uint32_t wb = wst + w_base + (h ? 144u - ((static_cast<uint32_t>(lane) & 2u) << 4) : 0u);
+    const uint32_t eb = wst + e_base + (h ? 64u - ((static_cast<uint32_t>(lane) & 16u) << 3) : 0u);
+    const uint32_t xt = (XRES ? x_thread + kt * (kTileCols * 2) : x_thread + s * xstage) + 256 * h;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const uint32_t wo = wb + ((32u * k) ^ w_xor);
+      const uint32_t eo = eb + ((16u * k) ^ e_xor);
+      uint32_t f0[4], f1[4];
+      decode8(lds_at<uint2>(sm8, wo), lds_at<uint32_t>(sm8, eo), tab, f0);
+      decode8(lds_at<uint2>(sm8, wo + 16 * 128), lds_at<uint32_t>(sm8, eo + 8 * 128), tab, f1);
+#pragma unroll
+      for (int nb = 0; nb < NB; ++nb) {
+        uint4 xv = make_uint4(0, 0, 0, 0);
+        if (nb * 8 + g < B) xv = lds_at<uint4>(sm8, xt + nb * x_nb_step + 64 * k);
+        mma_bf16_16816(acc[k & 1][nb], f0[0], f1[0], f0[1], f1[1], xv.x, xv.y);
+        mma_bf16_16816(acc[k & 1][nb], f0[2], f1[2], f0[3], f1[3], xv.z, xv.w);
+      }
+    }
+  };
+
   // Adds the exact products of the warp's escaped weights: in the MMA they
   // decoded with exponent 0 (below 2^-126 in magnitude). Lane e < 16 holds
   // escape e as position | exponent << 16, or 0 for an unused slot and for
@@ -706,9 +733,9 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
   int ntl = 0, kt_mine = 0, fbi = -1;
   uint32_t esc_rec = 0u;  // this lane's escape record (fix_escapes)
 
-  // Waits for stage i's records and weights and decodes this warp's tile
-  // of it (SE12: its first half) into frag0 / frag1.
-  auto fetch_stage = [&]() {
+  // Waits for stage i's records and weights; with `predecode`, decodes this
+  // warp's tile of it (its first half, with 8-tile stages) into frag0 / frag1.
+  auto fetch_stage = [&](bool predecode) {
     ntl = min(kStage, tend - tile0);
     fbi = -1;
     esc_rec = 0u;
@@ -744,13 +771,16 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
         cur_seg = seg;
       }
     }
-    if (jw < ntl && ok) load_frags(s, kt_mine, fbi, 0);
+    if (predecode && jw < ntl && ok) load_frags(s, kt_mine, fbi, 0);
   };
 
   // The weights do not depend on the previous kernel in the stream: decode
   // this warp's first tile while that kernel finishes, then wait for it
   // (griddepcontrol.wait) before touching x, y or the workspace.
-  if (nstages > 0) fetch_stage();
+  // (8-tile stages do not: fragments live across the loop would cost the
+  // per-group decode its registers; measured slower)
+  constexpr bool kPredecodeFirst = !FULL;
+  if (nstages > 0) fetch_stage(kPredecodeFirst);
   grid_dependency_wait();
   if (XRES && !mbar_wait((K & 7) ? xready : xbar, 0)) ok = false;
 
@@ -769,13 +799,29 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
         pe += KT;
       }
       if (jw < ntl && ok) {
-        mma_tile(s, kt_mine, 0);
-        // the escape products before half 1, so that their record is dead
-        // during its decode
-        if (!RAW && fbi < 0) fix_escapes(s, kt_mine, esc_rec);
         if (FULL) {
-          load_frags(s, kt_mine, fbi, 1);
-          mma_tile(s, kt_mine, 1);
+          // half 0 was decoded by fetch_stage for the first stage
+          const bool plain = fbi < 0 && !pad_inf;
+          if (kPredecodeFirst && i == 0) {
+            mma_tile(s, kt_mine, 0);
+          } else if (plain) {
+            decode_mma(s, kt_mine, 0);
+          } else {
+            load_frags(s, kt_mine, fbi, 0);
+            mma_tile(s, kt_mine, 0);
+          }
+          // the escape products before half 1, so that their record is
+          // dead during its decode
+          if (fbi < 0) fix_escapes(s, kt_mine, esc_rec);
+          if (plain) {
+            decode_mma(s, kt_mine, 1);
+          } else {
+            load_frags(s, kt_mine, fbi, 1);
+            mma_tile(s, kt_mine, 1);
+          }
+        } else {
+          mma_tile(s, kt_mine, 0);
+          if (!RAW && fbi < 0) fix_escapes(s, kt_mine, esc_rec);
         }
       }
       while (pe < ntl) {
@@ -809,7 +855,9 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
       kt0 -= KT;
       ++tr0;
     }
-    if (i + 1 < nstages) fetch_stage();
+    // 8-tile stages decode in decode_mma (group by group) from the second
+    // stage on; 4-tile stages decode here, ahead of the stage's row ends
+    if (i + 1 < nstages) fetch_stage(!FULL);
   }
 }
 
