@@ -117,15 +117,16 @@ int tiles_of(int rows, int cols) {
 // whether x is resident, the grid and how tiles map to CTAs.
 //  * Shared memory: the first candidate (below) that lets two CTAs share an
 //    SM, for each stage size; only if no candidate does, one CTA per SM.
-//    8-tile stages need x resident and as many CTAs per SM as 4-tile ones.
+//    8-tile stages need x resident.
 //  * Work split: row mode (whole tile rows per CTA, no cross-CTA fixup) or
 //    stream-K (equal runs of stages, split rows finished across CTAs).
-//  * Among these, the smallest critical path of the longest CTA, in units of
-//    one warp's time for a half tile: a 4-tile stage costs 1 + r, an 8-tile
-//    stage 2 + r (each warp does a whole tile), with r = 0.65 the per-stage
-//    overhead (barriers, records, row ends), and a stream-K fixup three
-//    4-tile stages (a round trip through L2 on a loaded GPU). Measured on
-//    Gemma-2 shapes, these pick the faster configuration.
+//  * Among these, the smallest critical path of the longest CTA: stages x
+//    stage time + the stream-K fixup. In units of a 4-tile stage's overhead-
+//    inclusive half-tile time: a 4-tile stage (two CTAs per SM) costs 1.65,
+//    an 8-tile stage 2.65 (each warp does a whole tile); x 0.8 when one CTA
+//    has the SM to itself, x 1.5 when x is staged; a fixup 3.9 (a round trip
+//    through L2 on a loaded GPU). Fitted to timings of every choice on
+//    Gemma-2 2B/9B/27B shapes at batch 1, 4 and 16.
 struct LaunchConfig {
   int grid;
   int stages;
@@ -160,15 +161,17 @@ LaunchConfig choose_config(bool raw, int tiles, int cols, int batch, int sm_coun
   const int tile_cols = (cols + SE12_TILE_COLS - 1) / SE12_TILE_COLS;
   const int tile_rows = tiles / tile_cols;
   constexpr double kStageOverhead = 0.65;
-  constexpr double kFixup = 3 * (1 + kStageOverhead);
+  constexpr double kAloneFactor = 0.8;
+  constexpr double kStagedXFactor = 1.5;
+  constexpr double kFixup = 3.9;
   LaunchConfig best{};
   double best_cost = 0;
   for (const bool full : {false, true}) {
     const MemoryChoice& mem = full ? mem8 : mem4;
-    // 8-tile stages only where they keep the CTAs per SM of 4-tile stages
-    if (!mem.per_sm || (full && mem.per_sm < mem4.per_sm)) continue;
+    if (!mem.per_sm) continue;
     const int stage = se12::stage_tiles(full);
-    const double stage_cost = (full ? 2 : 1) + kStageOverhead;
+    const double stage_cost = ((full ? 2 : 1) + kStageOverhead) * (mem.per_sm == 1 ? kAloneFactor : 1.0) *
+                              (mem.x_resident ? 1.0 : kStagedXFactor);
     const int slots = mem.per_sm * sm_count;
     const int units = (tiles + stage - 1) / stage;
     const int grid_sk = std::max(1, std::min(units, slots));
