@@ -66,6 +66,9 @@ def parse_args():
     p.add_argument("--no-dense", action="store_true", help="skip the dense BF16 comparisons")
     p.add_argument("--layers", type=int, default=None, help="override the layer count (profiling small cases)")
     p.add_argument("--no-lm-head", action="store_true")
+    p.add_argument("--offload-gb", type=float, default=None,
+                   help="weight-offload mode: decoder layers beyond this VRAM budget (GB) stream from pinned host "
+                        "memory every token; SE12 and BF16 on the same pipeline")
     p.add_argument("--eager", action="store_true",
                    help="issue each step's launches one by one instead of replaying a CUDA graph (profiler runs)")
     p.add_argument("--no-group", action="store_true",
@@ -729,12 +732,154 @@ def run_tp(args) -> None:
         dist.destroy_process_group()
 
 
+def run_offload(args) -> None:
+    """Weight offload (the reference's weight-offload feature, spec.md
+    AC-029 / AC-030): the decode-step GEMVs of every layer, with the layers
+    beyond a VRAM budget streamed from pinned host memory over PCIe, double
+    buffered, SE12 and BF16 through the same pipeline. Reports per format
+    the time per token, streamed bytes per token, the measured host-to-device
+    bandwidth, the overlap efficiency (1 - exposed copy time / copy time) and
+    the time predicted from streamed bytes / bandwidth. One rank.
+    `overlap_efficiency` follows the reference's definition (copy time
+    hidden under compute); when transfer-bound, `compute_hidden` (compute
+    time hidden under the copies) and `transfer_bound_fraction` (copy-only
+    time / time per token) say how close the pipeline is to the bound."""
+    import torch
+
+    from se12_b200 import _build
+    from se12_b200.device import DeviceSe12Matrix, bf16_gemv, device_status, gemv_call
+    from se12_b200.codec import encode_device
+    from se12_b200.offload import LayerStreamer, layer_nbytes, place_layers
+    from se12_b200.shapes import CONFIGS
+
+    _build.build()
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    shapes = CONFIGS[args.config]
+    nlayers = args.layers if args.layers is not None else shapes.layers
+    batch = args.batch
+    budget = int(args.offload_gb * 1e9)
+    groups = dict(shapes.GROUPS)
+    members = {m: g for g, ms in shapes.GROUPS for m in ms}
+    t0 = time.perf_counter()
+    se12_layers, bf16_layers, kinds = [], [], []
+    for layer in range(nlayers):
+        enc, dense = {}, {}
+        for j, (name, rows, cols, kind) in enumerate(shapes.layer_matrices()):
+            w = synthetic_bf16(torch, rows, cols, 1000 * layer + j, device)
+            enc[name], dense[name] = encode_device(w), w
+        mats, ws, ks, done = [], [], [], set()
+        for name, _, _, kind in shapes.layer_matrices():
+            if name in done:
+                continue
+            names = groups[members[name]] if name in members else (name,)
+            mats.append(DeviceSe12Matrix.concatenate([enc[n] for n in names]) if len(names) > 1 else enc[name])
+            ws.append(torch.cat([dense[n] for n in names]) if len(names) > 1 else dense[name])
+            ks.append(kind)
+            done.update(names)
+        se12_layers.append(mats)
+        bf16_layers.append(ws)
+        kinds = ks
+        del enc, dense
+    setup_s = time.perf_counter() - t0
+    gen = torch.Generator(device=device)
+    gen.manual_seed(1)
+    xs = {k: torch.randn(batch, shapes.input_width(k), generator=gen, device=device).to(torch.bfloat16)
+          for k in ("hidden", "attn", "mlp")}
+
+    def measure(fmt):
+        layers = se12_layers if fmt == "se12" else bf16_layers
+        sizes = [layer_nbytes(layer) for layer in layers]
+        placement = place_layers(sizes, budget)
+        streamer = LayerStreamer([layers[i] for i in placement.streamed], device) if placement.streamed else None
+        ys = [[torch.empty(batch, (m.rows if fmt == "se12" else m.shape[0]), device=device) for m in layer] for layer in layers]
+
+        def gemvs(i, mats):
+            for m, kind, y in zip(mats, kinds, ys[i]):
+                if fmt == "se12":
+                    gemv_call(m, xs[kind], y)
+                else:
+                    bf16_gemv(m, xs[kind], y)
+
+        resident = set(placement.resident)
+
+        def step(compute=True, copy=True):
+            # copy=False: every layer computes from its resident device copy
+            # (kept for this comparison); compute=False: copies only
+            j = 0
+            for i, layer in enumerate(layers):
+                if i in resident or not copy:
+                    if compute:
+                        gemvs(i, layer)
+                    continue
+                views = streamer.acquire(j)
+                if compute:
+                    gemvs(i, views)
+                streamer.release(j)
+                j += 1
+
+        def timed(fn, n):
+            for _ in range(max(2, args.warmup)):
+                fn()
+            torch.cuda.synchronize()
+            times = []
+            for _ in range(n):
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                fn()
+                if streamer is not None:
+                    streamer.synchronize()
+                e1.record()
+                torch.cuda.synchronize()
+                times.append(e0.elapsed_time(e1))
+            times.sort()
+            return times[len(times) // 2], times[len(times) // 10], times[(9 * len(times)) // 10]
+
+        n = max(3, args.steps)
+        med, p10, p90 = timed(step, n)
+        res = {"placement": {"resident_layers": len(placement.resident), "streamed_layers": len(placement.streamed),
+                             "resident_bytes": placement.resident_bytes, "staging_bytes": placement.staging_bytes},
+               "ms_per_token": med, "ms_p10": p10, "ms_p90": p90,
+               "streamed_bytes_per_token": streamer.streamed_bytes if streamer else 0}
+        if streamer is not None:
+            compute_ms = timed(lambda: step(copy=False), n)[0]
+            copy_ms = timed(lambda: step(compute=False), n)[0]
+            h2d = streamer.streamed_bytes / (copy_ms * 1e-3) / 1e9
+            res.update({"compute_only_ms": compute_ms, "copy_only_ms": copy_ms, "h2d_gbs": h2d,
+                        "overlap_efficiency": max(0.0, min(1.0, 1.0 - (med - compute_ms) / copy_ms)),
+                        "compute_hidden": max(0.0, min(1.0, 1.0 - (med - copy_ms) / compute_ms)),
+                        "transfer_bound_fraction": copy_ms / med,
+                        "predicted_ms": streamer.streamed_bytes / (h2d * 1e9) * 1e3})
+        del streamer
+        torch.cuda.synchronize()
+        return res
+
+    out = {"se12": measure("se12"), "bf16": measure("bf16")}
+    if device_status():
+        raise RuntimeError("a kernel reported an error")
+    line = {
+        "metric": "decode-step GEMV time per token with weight offload", "unit": "ms",
+        "value": out["se12"]["ms_per_token"], "higher_is_better": False, "n_gpus": 1, "steps": args.steps,
+        "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"{shapes.name} decode-step GEMV set, {nlayers} layers (q/k/v and gate/up grouped), "
+                   f"batch {batch}, layers beyond {args.offload_gb} GB of VRAM streamed from pinned host memory",
+                   "vram_budget_bytes": budget, "lm_head": "not included", "setup_seconds": setup_s},
+        "se12": out["se12"], "bf16": out["bf16"],
+        "se12_over_bf16_time": out["se12"]["ms_per_token"] / out["bf16"]["ms_per_token"],
+        "se12_over_bf16_streamed_bytes": (out["se12"]["streamed_bytes_per_token"] / out["bf16"]["streamed_bytes_per_token"]
+                                          if out["bf16"]["streamed_bytes_per_token"] else None),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse_args()
     if args.impl == "reference":
         run_reference(args)
     elif args.tp:
         run_tp(args)
+    elif args.offload_gb is not None:
+        run_offload(args)
     else:
         run_ours(args)
 

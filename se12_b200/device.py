@@ -67,10 +67,16 @@ class DeviceSe12Matrix:
     tile-major concatenation of several SE12 matrices with the same columns,
     given as ``[(rows_i, codebook_i), ...]``; ``codebook`` is then ignored.
     ``concatenate`` builds one from separate matrices.
+
+    ``derived`` (optional): ``(escape_pos, fallback_index)`` device tensors
+    that already hold this matrix's derived tables (as computed for the same
+    streams by a prepared matrix); the matrix then uses them as they are
+    instead of allocating and preparing its own (the offload staging buffers
+    receive them with the streams).
     """
 
     def __init__(self, rows: int, cols: int, codebook, sm: torch.Tensor, ec: torch.Tensor, esc: torch.Tensor,
-                 fallback_bitmap: torch.Tensor, fallback_raw: torch.Tensor, segments=None):
+                 fallback_bitmap: torch.Tensor, fallback_raw: torch.Tensor, segments=None, derived=None):
         lib = _lib.load()
         self.rows, self.cols = int(rows), int(cols)
         if segments is None:
@@ -98,9 +104,15 @@ class DeviceSe12Matrix:
         # keep a non-empty allocation so the pointer is valid and aligned
         self.fallback_raw = raw if raw.numel() else torch.zeros(8, dtype=torch.int16, device=self.device)
         self.fallback_tiles = raw.numel() // TILE_SIZE
-        self.escape_pos = torch.empty(self.tiles * ESCAPE_BUDGET, dtype=torch.int16, device=self.device)
-        # padded to a multiple of 4 tiles (the GEMV copies it in 16-byte groups)
-        self.fallback_index = torch.empty((self.tiles + 3) // 4 * 4, dtype=torch.int32, device=self.device)
+        if derived is None:
+            self.escape_pos = torch.empty(self.tiles * ESCAPE_BUDGET, dtype=torch.int16, device=self.device)
+            # padded to a multiple of 4 tiles (the GEMV copies it in 16-byte groups)
+            self.fallback_index = torch.empty((self.tiles + 3) // 4 * 4, dtype=torch.int32, device=self.device)
+        else:
+            self.escape_pos, self.fallback_index = derived
+            if (self.escape_pos.numel() != self.tiles * ESCAPE_BUDGET or self.escape_pos.dtype != torch.int16
+                    or self.fallback_index.numel() != (self.tiles + 3) // 4 * 4 or self.fallback_index.dtype != torch.int32):
+                raise ValueError("derived tables have the wrong size or type for this matrix")
 
         s = _lib.Se12StreamsStruct()
         s.rows, s.cols = self.rows, self.cols
@@ -119,7 +131,8 @@ class DeviceSe12Matrix:
                        "se12_matrix_create_segmented")
             self._handle = handle
             self._finalizer = weakref.finalize(self, lib.se12_matrix_destroy, handle)
-            _lib.check(lib.se12_matrix_prepare(handle, ctypes.c_void_p(stream_handle(self.device))), "se12_matrix_prepare")
+            if derived is None:
+                _lib.check(lib.se12_matrix_prepare(handle, ctypes.c_void_p(stream_handle(self.device))), "se12_matrix_prepare")
 
     # ------------------------------------------------------------------ construction
     @classmethod
