@@ -94,7 +94,7 @@ __host__ __device__ __forceinline__ uint32_t table_byte(const uint8_t* codebook,
 //    twice, [b, b].
 __device__ __forceinline__ void decode8(uint2 s, uint32_t e, const uint32_t (&tab)[4], uint32_t (&p)[4]) {
   const uint32_t sel03 = e & 0x77777777u;   // selectors for weights 0..3 (low 16 bits)
-  const uint32_t sel47 = sel03 >> 16;        // weights 4..7
+  const uint32_t sel47 = __umulhi(sel03, 0x10000u);  // weights 4..7: sel03 >> 16 on the multiply pipe (the shift pipe is the busier one)
   const uint32_t e4 = e << 4;                // bit 3 of the even codes at a byte's top bit
   const uint32_t hi03 = prmt(e4, e, 0xD9C8u);  // 0xFF where code >= 8: bytes of e4/e for weights 0,1,2,3
   const uint32_t hi47 = prmt(e4, e, 0xFBEAu);  // weights 4..7
