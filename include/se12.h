@@ -36,6 +36,7 @@ extern "C" {
 #define SE12_FORMAT_VERSION 1
 #define SE12_MAX_BATCH 16
 #define SE12_MAX_SEGMENTS 4
+#define SE12_MAX_PEERS 8
 
 typedef enum se12_status {
   SE12_OK = 0,
@@ -146,6 +147,51 @@ int se12_gemv_launch_config(const se12_matrix* m, int batch, se12_launch_config*
  */
 int se12_gemv(const se12_matrix* m, const uint16_t* x_dev, int batch, int ldx, float* y_dev, int ldy,
               void* workspace_dev, size_t workspace_bytes, void* stream);
+
+/*
+ * Fused GEMV + all-reduce for tensor parallelism with the input columns
+ * sharded (the attention-output and MLP-down projections of a Megatron
+ * split): every rank of a peer group calls it, in the same order, on its
+ * column shard of the same rows x cols matrix, and each gets
+ *   y = sum over ranks of (its shard's GEMV),
+ * summed in rank order, so all ranks hold the same bits. No counterpart in
+ * the reference, which runs on one GPU at a time
+ * (.spec/features/fused-decode-gemv/spec.md:159); it replaces a GEMV
+ * followed by an NCCL all-reduce: each finished tile row is stored into
+ * every rank's receive buffer over peer memory (NVLink) and flagged there,
+ * inside the GEMV kernel.
+ *
+ * The group describes buffers every rank allocated and mapped into every
+ * other rank (CUDA IPC or any peer mapping), indexed by rank:
+ *   recv[r]:  se12_peer_recv_bytes(world, rows_cap) bytes, 16-byte aligned;
+ *   flags[r]: se12_peer_flag_bytes(world, rows_cap) bytes, zeroed once;
+ *   epoch:    this rank's own int32 call counter, zeroed once.
+ * All ranks must make the same sequence of calls on a group (each call
+ * bumps the counter on the stream after the GEMV); a call waits (bounded,
+ * then reports SE12_ERR_DEVICE_FAULT through se12_device_status) for every
+ * rank's rows. Calls on one group must be ordered on one stream per rank.
+ */
+typedef struct se12_peer_group {
+  int32_t world, rank, rows_cap;
+  float* recv[SE12_MAX_PEERS];
+  int32_t* flags[SE12_MAX_PEERS];
+  int32_t* epoch;
+} se12_peer_group;
+
+/* Mapping another process's device buffer (CUDA IPC), for the peer group's
+ * buffers: se12_ipc_handle gives the 64-byte handle of the allocation that
+ * holds dev_ptr and dev_ptr's offset in it; se12_ipc_open maps it on the
+ * current device (enabling peer access) and returns the pointer for that
+ * offset plus the mapping to pass to se12_ipc_close. An allocation can be
+ * opened once per process. */
+int se12_ipc_handle(const void* dev_ptr, uint8_t* handle_out /* [64] */, uint64_t* offset_out);
+int se12_ipc_open(const uint8_t* handle /* [64] */, uint64_t offset, void** dev_ptr_out, void** mapping_out);
+int se12_ipc_close(void* mapping);
+
+size_t se12_peer_recv_bytes(int world, int rows_cap);
+size_t se12_peer_flag_bytes(int world, int rows_cap);
+int se12_gemv_allreduce(const se12_matrix* m, const uint16_t* x_dev, int batch, int ldx, float* y_dev, int ldy,
+                        void* workspace_dev, size_t workspace_bytes, const se12_peer_group* peers, void* stream);
 
 /*
  * se12_gemv without a caller workspace, for callers that cannot allocate

@@ -47,6 +47,19 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   return fn;
 }
 
+PFN_cuMemGetAddressRange_v3020 address_range_query() {
+  static PFN_cuMemGetAddressRange_v3020 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuMemGetAddressRange_v3020>(p);
+  });
+  return fn;
+}
+
 int encode_map(CUtensorMap* map, CUtensorMapDataType type, int rank, const void* base, const cuuint64_t* dims,
                const cuuint64_t* strides, const cuuint32_t* box) {
   auto fn = tensor_map_encoder();
@@ -389,6 +402,103 @@ int se12_gemv(const se12_matrix* m, const uint16_t* x, int batch, int ldx, float
   cudaError_t err = se12::launch_gemv(false, m->sm_map, m->ec_map, a, c.nblocks, c.smem,
                                       static_cast<cudaStream_t>(stream), true);
   if (err != cudaSuccess) return cuda_fail(err, "se12_gemv launch");
+  return SE12_OK;
+}
+
+int se12_ipc_handle(const void* dev_ptr, uint8_t* handle_out, uint64_t* offset_out) {
+  if (!dev_ptr || !handle_out || !offset_out) return fail(SE12_ERR_INVALID_ARGUMENT, "null argument");
+  auto range = address_range_query();
+  if (!range) return fail(SE12_ERR_CUDA, "cuMemGetAddressRange is not available");
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (range(&base, &size, reinterpret_cast<CUdeviceptr>(dev_ptr)) != CUDA_SUCCESS)
+    return fail(SE12_ERR_INVALID_ARGUMENT, "not a device allocation");
+  cudaIpcMemHandle_t h;
+  cudaError_t err = cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base));
+  if (err != cudaSuccess) return cuda_fail(err, "cudaIpcGetMemHandle");
+  std::memcpy(handle_out, &h, sizeof(h));
+  *offset_out = reinterpret_cast<uint64_t>(dev_ptr) - static_cast<uint64_t>(base);
+  return SE12_OK;
+}
+
+int se12_ipc_open(const uint8_t* handle, uint64_t offset, void** dev_ptr_out, void** mapping_out) {
+  if (!handle || !dev_ptr_out || !mapping_out) return fail(SE12_ERR_INVALID_ARGUMENT, "null argument");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  void* p = nullptr;
+  cudaError_t err = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+  if (err != cudaSuccess) return cuda_fail(err, "cudaIpcOpenMemHandle");
+  *mapping_out = p;
+  *dev_ptr_out = static_cast<char*>(p) + offset;
+  return SE12_OK;
+}
+
+int se12_ipc_close(void* mapping) {
+  if (!mapping) return SE12_OK;
+  cudaError_t err = cudaIpcCloseMemHandle(mapping);
+  if (err != cudaSuccess) return cuda_fail(err, "cudaIpcCloseMemHandle");
+  return SE12_OK;
+}
+
+size_t se12_peer_recv_bytes(int world, int rows_cap) {
+  if (world < 1 || world > SE12_MAX_PEERS || rows_cap < 1) return 0;
+  return static_cast<size_t>(2) * world * 16 * rows_cap * sizeof(float);
+}
+
+size_t se12_peer_flag_bytes(int world, int rows_cap) {
+  if (world < 1 || world > SE12_MAX_PEERS || rows_cap < 1) return 0;
+  return static_cast<size_t>(world) * ((rows_cap + SE12_TILE_ROWS - 1) / SE12_TILE_ROWS) * sizeof(int32_t);
+}
+
+int se12_gemv_allreduce(const se12_matrix* m, const uint16_t* x, int batch, int ldx, float* y, int ldy, void* workspace,
+                        size_t workspace_bytes, const se12_peer_group* g, void* stream) {
+  if (!m || !g) return fail(SE12_ERR_INVALID_ARGUMENT, "null matrix or peer group");
+  if (g->world < 2 || g->world > SE12_MAX_PEERS || g->rank < 0 || g->rank >= g->world)
+    return fail(SE12_ERR_INVALID_ARGUMENT, "peer group needs 2.." + std::to_string(SE12_MAX_PEERS) +
+                                               " ranks and 0 <= rank < world");
+  if (m->view.rows > g->rows_cap)
+    return fail(SE12_ERR_INVALID_ARGUMENT, "matrix has " + std::to_string(m->view.rows) +
+                                               " rows, the peer buffers hold " + std::to_string(g->rows_cap));
+  if (!g->epoch) return fail(SE12_ERR_INVALID_ARGUMENT, "null epoch counter");
+  for (int r = 0; r < g->world; ++r) {
+    if (!g->recv[r] || !g->flags[r]) return fail(SE12_ERR_INVALID_ARGUMENT, "null peer buffer");
+    if (!aligned16(g->recv[r]) || !aligned16(g->flags[r]))
+      return fail(SE12_ERR_MISALIGNED, "peer buffers must be 16-byte aligned");
+  }
+  int st = check_gemv_io(m->view.rows, m->view.cols, x, batch, ldx, y, ldy);
+  if (st != SE12_OK) return st;
+  const LaunchConfig c = choose_config(false, m->view.tiles, m->view.cols, batch, m->sm_count);
+  const size_t need = workspace_bytes_for(m->view.tile_rows, m->sm_count);
+  if (!workspace || workspace_bytes < need)
+    return fail(SE12_ERR_WORKSPACE_TOO_SMALL, "workspace needs " + std::to_string(need) + " bytes");
+  se12::GemvArgs a{};
+  a.m = m->view;
+  a.x = x;
+  a.ldx = ldx;
+  a.batch = batch;
+  a.y = y;
+  a.ldy = ldy;
+  a.partials = static_cast<float*>(workspace);
+  a.counters = reinterpret_cast<int*>(static_cast<char*>(workspace) + partials_region_bytes(m->sm_count));
+  a.grid = c.grid;
+  a.stages = c.stages;
+  a.x_resident = c.x_resident;
+  a.row_mode = c.row_mode;
+  a.full_tiles = c.full_tiles;
+  a.peers.world = g->world;
+  a.peers.rank = g->rank;
+  a.peers.rows_cap = g->rows_cap;
+  a.peers.tile_rows_cap = (g->rows_cap + SE12_TILE_ROWS - 1) / SE12_TILE_ROWS;
+  for (int r = 0; r < g->world; ++r) {
+    a.peers.recv[r] = g->recv[r];
+    a.peers.flags[r] = g->flags[r];
+  }
+  a.peers.epoch = g->epoch;
+  cudaError_t err = se12::launch_gemv(false, m->sm_map, m->ec_map, a, c.nblocks, c.smem,
+                                      static_cast<cudaStream_t>(stream), true);
+  if (err != cudaSuccess) return cuda_fail(err, "se12_gemv_allreduce launch");
+  err = se12::launch_bump_epoch(g->epoch, static_cast<cudaStream_t>(stream));
+  if (err != cudaSuccess) return cuda_fail(err, "se12_gemv_allreduce epoch launch");
   return SE12_OK;
 }
 

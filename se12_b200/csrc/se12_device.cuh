@@ -162,6 +162,36 @@ __device__ __forceinline__ bool wait_flag_gpu(const int* flag) {
   return true;
 }
 
+// System-scope (all GPUs of the node) release store and acquire load, for
+// flags written into another GPU's memory over peer mappings.
+__device__ __forceinline__ void st_release_sys(int* p, int v) {
+  asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ int ld_acquire_sys(const int* p) {
+  int v;
+  asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Waits until *flag has reached epoch e (flags only grow; compared modulo
+// 2^32). Returns false (and raises kStatusWaitTimeout) after kWaitLimitNs.
+__device__ __forceinline__ bool wait_epoch_sys(const int* flag, int e) {
+  auto reached = [flag, e]() {
+    return static_cast<int>(static_cast<unsigned>(ld_acquire_sys(flag)) - static_cast<unsigned>(e)) >= 0;
+  };
+  if (reached()) return true;
+  const unsigned long long start = global_ns();
+  while (!reached()) {
+    __nanosleep(32);
+    if (global_ns() - start > kWaitLimitNs) {
+      raise_status(kStatusWaitTimeout);
+      return false;
+    }
+  }
+  return true;
+}
+
 // ------------------------------------------------------------------ L2 policy
 
 __device__ __forceinline__ uint64_t policy_evict_first() {

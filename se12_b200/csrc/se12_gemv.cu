@@ -414,6 +414,9 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
     const int tr_last = (tend - 1) / KT;
     const int outs = 16 * B;  // <= 256: up to 8 values per lane
     grid_dependency_wait();   // y and the workspace may be in use by the previous kernel
+    // peer all-reduce: this call's epoch (the counter is bumped after each call)
+    const PeerArgs& P = a.peers;
+    const int epoch = (P.world > 1) ? __ldcg(P.epoch) + 1 : 0;
     for (int tr = tr_first; tr <= tr_last; ++tr) {
       const int lr = tr - tr_first, pb = lr & 1;
       if (!mbar_wait(&deposited[pb], static_cast<uint32_t>(lr >> 1) & 1u)) break;
@@ -466,6 +469,46 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
           }
 #pragma unroll
           for (int j = 0; j < 8; ++j) v[j] += p[j];
+        }
+      }
+      if (P.world > 1 && good) {
+        // All-reduce of the row across the peer group: store it into every
+        // rank's receive slot (this rank's own included) for this epoch's
+        // parity, flag it at every rank, wait for every rank's flag in
+        // this rank's memory, then sum the slots in rank order, so that
+        // every rank writes the same bits. A rank can be at most one call
+        // ahead of another (it needs the other's rows of the call in
+        // between), so two parities keep a slot from being overwritten
+        // while it is read.
+        const size_t slot = static_cast<size_t>(16) * P.rows_cap;
+        const size_t base = static_cast<size_t>((epoch & 1) * P.world) * slot;
+        for (int r = 0; r < P.world; ++r) {
+          float* dst = P.recv[r] + base + P.rank * slot;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const int idx = lane + 32 * j;
+            const int row = idx / B, b = idx - row * B;
+            const int grow = tr * kTileRows + row;
+            if (idx < outs && grow < N) dst[static_cast<size_t>(b) * P.rows_cap + grow] = v[j];
+          }
+        }
+        __threadfence_system();
+        __syncwarp();
+        if (lane < P.world) st_release_sys(P.flags[lane] + P.rank * P.tile_rows_cap + tr, epoch);
+        bool arrived = true;
+        if (lane < P.world) arrived = wait_epoch_sys(P.flags[P.rank] + lane * P.tile_rows_cap + tr, epoch);
+        good = __all_sync(0xFFFFFFFFu, arrived);
+        const float* mine = P.recv[P.rank] + base;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int idx = lane + 32 * j;
+          const int row = idx / B, b = idx - row * B;
+          const int grow = tr * kTileRows + row;
+          if (idx < outs && grow < N) {
+            float sum = 0.f;
+            for (int r = 0; r < P.world; ++r) sum += __ldcv(mine + r * slot + static_cast<size_t>(b) * P.rows_cap + grow);
+            v[j] = sum;
+          }
         }
       }
 #pragma unroll
@@ -859,6 +902,17 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
     // stage on; 4-tile stages decode here, ahead of the stage's row ends
     if (i + 1 < nstages) fetch_stage(!FULL);
   }
+}
+
+// The peer all-reduce's call counter, bumped once the GEMV has finished
+// (stream order), so that every CTA of a call reads the same epoch.
+__global__ void bump_epoch_kernel(int* epoch) {
+  if (threadIdx.x == 0) *epoch += 1;
+}
+
+cudaError_t launch_bump_epoch(int* epoch, cudaStream_t stream) {
+  bump_epoch_kernel<<<1, 32, 0, stream>>>(epoch);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_gemv(bool raw, const CUtensorMap& map0, const CUtensorMap& map1, const GemvArgs& a, int nblocks,

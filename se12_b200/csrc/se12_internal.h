@@ -40,6 +40,22 @@ __host__ __device__ __forceinline__ int segment_of(const MatrixView& m, int tr) 
   return (tr >= m.seg_end[0]) + (tr >= m.seg_end[1]) + (tr >= m.seg_end[2]);
 }
 
+// All-reduce of y across the GPUs of a peer group (tensor parallelism with
+// the input columns sharded), fused into the GEMV: each finished tile row is
+// stored into every rank's receive buffer over peer memory, flagged with the
+// call's epoch, and summed in rank order once every rank's row is there.
+constexpr int kMaxPeers = 8;
+
+struct PeerArgs {
+  int world;                 // 1: no all-reduce
+  int rank;
+  int rows_cap;              // rows a receive slot holds (>= the matrix rows)
+  int tile_rows_cap;         // tile rows a flag slot holds
+  float* recv[kMaxPeers];    // rank s's receive buffer (peer-mapped): [2 parities][world][16 batch][rows_cap] fp32
+  int* flags[kMaxPeers];     // rank s's flags (peer-mapped): [world][tile_rows_cap], last epoch received
+  const int* epoch;          // this rank's call counter; a call uses epoch + 1 (bumped after the call)
+};
+
 // Arguments of one fused (or dense baseline) GEMV launch: y = x . W^T.
 struct GemvArgs {
   MatrixView m;        // for the dense baseline only rows/cols/tile_* are used
@@ -56,6 +72,7 @@ struct GemvArgs {
   int x_resident;      // 1: all of x in shared memory; 0: x staged per stage
   int row_mode;        // 1: each CTA owns whole tile rows; 0: stream-K over stages
   int full_tiles;      // SE12: 1 = 8-tile stages, a warp per tile; 0 = 4-tile stages, a warp per half tile
+  PeerArgs peers;      // world == 1: plain GEMV
 };
 
 // Pipeline geometry of the GEMV kernels. One stage holds consecutive tiles
@@ -115,6 +132,7 @@ inline size_t gemv_smem_bytes(bool raw, bool full_tiles, bool x_resident, int st
 }
 
 // Kernel launchers (defined in the .cu files).
+cudaError_t launch_bump_epoch(int* epoch, cudaStream_t stream);
 cudaError_t launch_gemv(bool raw, const CUtensorMap& map0, const CUtensorMap& map1, const GemvArgs& a, int nblocks,
                         size_t smem, cudaStream_t stream, bool pdl);
 cudaError_t launch_prepare(const MatrixView& m, uint16_t* escape_pos, int32_t* fallback_index, cudaStream_t stream);

@@ -106,11 +106,14 @@ class ShardedLinear(torch.nn.Module):
     full output is all-gathered) or ``"cols"`` (this rank holds input
     columns ``col_range``; the partial sums are all-reduced). ``local``
     computes this rank's product (by default the fused GEMV of ``matrix``:
-    x [B, k_local] -> fp32 [B, n_local]).
+    x [B, k_local] -> fp32 [B, n_local]). With ``peers`` (a
+    ``peers.PeerGroup``), a ``"cols"`` layer runs the GEMV and its
+    all-reduce as one kernel over peer memory instead of a GEMV followed by
+    an NCCL all-reduce.
     """
 
     def __init__(self, kind: str, rows: int, cols: int, world: int, rank: int, matrix=None,
-                 local: typing.Callable | None = None, group=None):
+                 local: typing.Callable | None = None, group=None, peers=None):
         super().__init__()
         if kind not in ("rows", "cols"):
             raise ValueError("kind must be 'rows' or 'cols'")
@@ -118,6 +121,7 @@ class ShardedLinear(torch.nn.Module):
         self.matrix = matrix
         self.local = local if local is not None else (lambda x: matrix.gemv(x))
         self.group = group
+        self.peers = peers
         self.row_bounds = [row_range(rows, world, r) for r in range(world)]
         self.col_bounds = [col_range(cols, world, r) for r in range(world)]
 
@@ -127,6 +131,9 @@ class ShardedLinear(torch.nn.Module):
         x2 = x.reshape(-1, x.shape[-1])
         if self.kind == "cols":
             c0, c1 = self.col_bounds[self.rank]
+            if self.peers is not None and self.world > 1:
+                y = self.peers.gemv_allreduce(self.matrix, x2[:, c0:c1].contiguous().to(torch.bfloat16))
+                return y.reshape(*x.shape[:-1], self.rows)
             y = self.local(x2[:, c0:c1].contiguous()).float()
             if self.world > 1:
                 dist.all_reduce(y, group=self.group)
@@ -153,13 +160,15 @@ def megatron_plan(name: str) -> str:
     return "cols" if leaf in ("o_proj", "down_proj", "out_proj", "wo", "w2") else "rows"
 
 
-def shard_matrix(tensor, kind: str, world: int, rank: int, device="cuda", group=None) -> ShardedLinear:
-    """Uploads rank ``rank``'s shard of an SE12 tensor and wraps it."""
+def shard_matrix(tensor, kind: str, world: int, rank: int, device="cuda", group=None, peers=None) -> ShardedLinear:
+    """Uploads rank ``rank``'s shard of an SE12 tensor and wraps it (``peers``:
+    fused GEMV + all-reduce for column shards)."""
     from .device import DeviceSe12Matrix
 
     t = as_tensor(tensor)
     part = shard_rows(t, world, rank) if kind == "rows" else shard_cols(t, world, rank)
-    return ShardedLinear(kind, t.rows, t.cols, world, rank, DeviceSe12Matrix.from_tensor(part, device), group=group)
+    return ShardedLinear(kind, t.rows, t.cols, world, rank, DeviceSe12Matrix.from_tensor(part, device), group=group,
+                         peers=peers)
 
 
 __all__ = [

@@ -65,3 +65,85 @@ def test_row_and_column_sharded_layers_over_nccl(tmp_path):
     for r in range(2):
         errs = torch.load(tmp_path / f"errs.{r}")
         assert max(errs) <= TOLERANCE, errs
+
+
+def _allreduce_main(rank, world, port, result_path):
+    import datetime
+
+    import torch.distributed as dist
+
+    from se12_b200.device import device_status
+    from se12_b200.format import make_tensor
+    from se12_b200.peers import PeerGroup
+    from se12_b200.sharding import col_range, shard_matrix
+
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", rank))
+    out = {}
+    try:
+        mats = {}
+        for name, rows, cols, seed in (("a", 1040, 4608, 8), ("b", 2304, 2048, 9)):  # 65 tile rows: a ragged last row
+            bits, _, _ = cases.synthetic_weights(rows, cols, seed=seed, outlier_rate=2e-3, outlier_scale=256.0)
+            s = oracle.encode(np.asarray(bits, dtype=np.uint16), rows, cols)
+            t = make_tensor(s.rows, s.cols, s.codebook, s.sm, s.ec, s.esc, s.fallback_bitmap, s.fallback_raw)
+            mats[name] = (bits, rows, cols, t)
+        peers = PeerGroup(rows_cap=2304)
+        layers = {n: shard_matrix(t, "cols", world, rank, device=f"cuda:{rank}", peers=peers) for n, (_, _, _, t) in mats.items()}
+        errs, same = [], []
+        # calls in a row, alternating matrices and batch sizes (20: two calls of 16 + 4)
+        for call, (name, batch) in enumerate((("a", 1), ("b", 3), ("a", 16), ("b", 20), ("a", 2))):
+            bits, rows, cols, _ = mats[name]
+            xb = oracle.bf16_round(np.random.default_rng(call).normal(size=(batch, cols)).astype(np.float32))
+            x = torch.from_numpy(xb.view(np.int16)).view(torch.bfloat16).cuda()
+            y = layers[name](x)
+            y64 = oracle.gemv_fp64(bits, rows, cols, oracle.bits_to_float32(xb))
+            errs.append(oracle.max_relative_error(y.cpu().numpy(), y64))
+            everyone = [torch.empty_like(y) for _ in range(world)]
+            dist.all_gather(everyone, y)
+            same.append(all(torch.equal(everyone[0], e) for e in everyone))
+        # the same calls from a CUDA graph: the call counter lives in device memory
+        bits, rows, cols, _ = mats["b"]
+        xb = oracle.bf16_round(np.random.default_rng(99).normal(size=(4, cols)).astype(np.float32))
+        x = torch.from_numpy(xb.view(np.int16)).view(torch.bfloat16).cuda()
+        c0, c1 = col_range(cols, world, rank)
+        xs = x[:, c0:c1].contiguous()
+        y = torch.empty(4, rows, device="cuda")
+        stream = torch.cuda.Stream()
+        stream.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(stream):
+            peers.gemv_allreduce(layers["b"].matrix, xs, y)
+        stream.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            peers.gemv_allreduce(layers["b"].matrix, xs, y)
+            peers.gemv_allreduce(layers["b"].matrix, xs, y)
+        y64 = oracle.gemv_fp64(bits, rows, cols, oracle.bits_to_float32(xb))
+        for _ in range(3):
+            y.zero_()
+            graph.replay()
+            torch.cuda.synchronize()
+            errs.append(oracle.max_relative_error(y.cpu().numpy(), y64))
+        del graph
+        torch.cuda.synchronize()
+        out = {"errs": errs, "same": same, "status": device_status()}
+        peers.close()
+    finally:
+        torch.save(out, f"{result_path}.{rank}")
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_fused_gemv_allreduce_over_peer_memory(tmp_path):
+    """Column shards whose GEMV and all-reduce are one kernel (peer memory,
+    no NCCL on the data path): within 1e-3 of the fp64 oracle, the same bits
+    on both ranks, over calls in a row and from a replayed CUDA graph."""
+    import torch.multiprocessing as mp
+
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    mp.spawn(_allreduce_main, args=(2, _free_port(), str(tmp_path / "ar")), nprocs=2, join=True)
+    for r in range(2):
+        res = torch.load(tmp_path / f"ar.{r}")
+        assert res["status"] == 0, res
+        assert max(res["errs"]) <= TOLERANCE, res["errs"]
+        assert all(res["same"]), res["same"]
