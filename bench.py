@@ -66,6 +66,9 @@ def parse_args():
     p.add_argument("--no-dense", action="store_true", help="skip the dense BF16 comparisons")
     p.add_argument("--layers", type=int, default=None, help="override the layer count (profiling small cases)")
     p.add_argument("--no-lm-head", action="store_true")
+    p.add_argument("--tp-allreduce", choices=("fused", "nccl"), default="fused",
+                   help="--tp: column-sharded layers as one GEMV + all-reduce kernel over peer memory (fused) or a "
+                        "GEMV followed by an NCCL all-reduce")
     p.add_argument("--offload-gb", type=float, default=None,
                    help="weight-offload mode: decoder layers beyond this VRAM budget (GB) stream from pinned host "
                         "memory every token; SE12 and BF16 on the same pipeline")
@@ -666,9 +669,18 @@ def run_tp(args) -> None:
     setup_s = time.perf_counter() - t_setup
     lm_rows = ops[-1][2].shape[1] if not args.no_lm_head else 0
     logits = torch.empty(world, batch, lm_rows, dtype=torch.float32, device=device) if lm_rows else None
+    fused = world > 1 and args.tp_allreduce == "fused"
+    peers = None
+    if fused:
+        from se12_b200.peers import PeerGroup
+
+        peers = PeerGroup(rows_cap=max(m.rows for m, _, _, coll in ops if coll == "all_reduce"), device=device)
 
     def step():
         for m, x, y, coll in ops:
+            if fused and coll == "all_reduce":
+                peers.gemv_allreduce(m, x, y)
+                continue
             gemv_call(m, x, y)
             if world > 1 and coll == "all_reduce":
                 dist.all_reduce(y)
@@ -718,15 +730,19 @@ def run_tp(args) -> None:
             "config": {"workload": f"{shapes.name} tensor-parallel decode-step GEMV set: {layers} layers x 7 + lm_head, "
                        f"batch {batch}", "batch": batch, "weights": weights,
                        "bytes_per_step": float(total_bytes.item()),
-                       "parallelism": f"tp{world}: q/k/v/gate/up by rows, o/down by columns + NCCL all-reduce, "
-                       "lm_head by rows + all-gather; one CUDA graph per step", "setup_seconds": setup_s},
+                       "parallelism": f"tp{world}: q/k/v/gate/up by rows, o/down by columns + "
+                       + ("all-reduce fused into the GEMV (peer memory)" if fused else "NCCL all-reduce")
+                       + ", lm_head by rows + NCCL all-gather; one CUDA graph per step", "setup_seconds": setup_s},
             "tok_s": batch / (ms * 1e-3),
             "per_gpu_gbs": value / world,
-            "collectives_per_step": (2 * layers + (0 if args.no_lm_head else 1)) if world > 1 else 0,
+            "nccl_collectives_per_step": ((0 if fused else 2 * layers) + (0 if args.no_lm_head else 1)) if world > 1 else 0,
+            "fused_allreduces_per_step": 2 * layers if fused else 0,
             "clocks": sampler.summary(),
         }
         print(json.dumps(line), flush=True)
     del graph
+    if peers is not None:
+        peers.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

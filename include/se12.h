@@ -157,24 +157,26 @@ int se12_gemv(const se12_matrix* m, const uint16_t* x_dev, int batch, int ldx, f
  * summed in rank order, so all ranks hold the same bits. No counterpart in
  * the reference, which runs on one GPU at a time
  * (.spec/features/fused-decode-gemv/spec.md:159); it replaces a GEMV
- * followed by an NCCL all-reduce: each finished tile row is stored into
- * every rank's receive buffer over peer memory (NVLink) and flagged there,
- * inside the GEMV kernel.
+ * followed by an NCCL all-reduce: inside the GEMV kernel, each finished tile
+ * row is stored into every rank's receive buffer over peer memory (NVLink),
+ * every value in one 64-bit word with the call's epoch, and read back once
+ * all ranks' words carry it.
  *
  * The group describes buffers every rank allocated and mapped into every
- * other rank (CUDA IPC or any peer mapping), indexed by rank:
- *   recv[r]:  se12_peer_recv_bytes(world, rows_cap) bytes, 16-byte aligned;
- *   flags[r]: se12_peer_flag_bytes(world, rows_cap) bytes, zeroed once;
- *   epoch:    this rank's own int32 call counter, zeroed once.
- * All ranks must make the same sequence of calls on a group (each call
- * bumps the counter on the stream after the GEMV); a call waits (bounded,
- * then reports SE12_ERR_DEVICE_FAULT through se12_device_status) for every
- * rank's rows. Calls on one group must be ordered on one stream per rank.
+ * other rank (se12_ipc_handle / se12_ipc_open, or any peer mapping),
+ * indexed by rank:
+ *   recv[r]:  se12_peer_recv_bytes(world, rows_cap) bytes, 16-byte aligned,
+ *             zeroed once;
+ *   epoch:    this rank's own two int32 (call counter, CTAs finished),
+ *             zeroed once, not shared with the other ranks.
+ * All ranks must make the same sequence of calls on a group (the last CTA
+ * of each call bumps the counter); a call waits (bounded, then reports
+ * SE12_ERR_DEVICE_FAULT through se12_device_status) for every rank's rows.
+ * Calls on one group must be ordered on one stream per rank.
  */
 typedef struct se12_peer_group {
   int32_t world, rank, rows_cap;
-  float* recv[SE12_MAX_PEERS];
-  int32_t* flags[SE12_MAX_PEERS];
+  void* recv[SE12_MAX_PEERS];
   int32_t* epoch;
 } se12_peer_group;
 
@@ -189,7 +191,6 @@ int se12_ipc_open(const uint8_t* handle /* [64] */, uint64_t offset, void** dev_
 int se12_ipc_close(void* mapping);
 
 size_t se12_peer_recv_bytes(int world, int rows_cap);
-size_t se12_peer_flag_bytes(int world, int rows_cap);
 int se12_gemv_allreduce(const se12_matrix* m, const uint16_t* x_dev, int batch, int ldx, float* y_dev, int ldy,
                         void* workspace_dev, size_t workspace_bytes, const se12_peer_group* peers, void* stream);
 

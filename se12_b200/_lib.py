@@ -59,7 +59,7 @@ class Se12PeerGroupStruct(ctypes.Structure):
     """Mirror of ``se12_peer_group`` in include/se12.h (SE12_MAX_PEERS = 8)."""
 
     _fields_ = [("world", ctypes.c_int32), ("rank", ctypes.c_int32), ("rows_cap", ctypes.c_int32),
-                ("recv", c_void_p * 8), ("flags", c_void_p * 8), ("epoch", c_void_p)]
+                ("recv", c_void_p * 8), ("epoch", c_void_p)]
 
 
 # name -> (restype, argtypes)
@@ -80,7 +80,6 @@ SIGNATURES = {
     "se12_ipc_open": (c_int, [ctypes.POINTER(ctypes.c_uint8), ctypes.c_uint64, ctypes.POINTER(c_void_p), ctypes.POINTER(c_void_p)]),
     "se12_ipc_close": (c_int, [c_void_p]),
     "se12_peer_recv_bytes": (c_size_t, [c_int, c_int]),
-    "se12_peer_flag_bytes": (c_size_t, [c_int, c_int]),
     "se12_gemv_allreduce": (c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p, c_int, c_void_p, c_size_t,
                                     ctypes.POINTER(Se12PeerGroupStruct), c_void_p]),
     "se12_decode": (c_int, [c_void_p, c_void_p, c_int, c_void_p]),

@@ -442,12 +442,7 @@ int se12_ipc_close(void* mapping) {
 
 size_t se12_peer_recv_bytes(int world, int rows_cap) {
   if (world < 1 || world > SE12_MAX_PEERS || rows_cap < 1) return 0;
-  return static_cast<size_t>(2) * world * 16 * rows_cap * sizeof(float);
-}
-
-size_t se12_peer_flag_bytes(int world, int rows_cap) {
-  if (world < 1 || world > SE12_MAX_PEERS || rows_cap < 1) return 0;
-  return static_cast<size_t>(world) * ((rows_cap + SE12_TILE_ROWS - 1) / SE12_TILE_ROWS) * sizeof(int32_t);
+  return static_cast<size_t>(2) * world * 16 * rows_cap * sizeof(uint64_t);
 }
 
 int se12_gemv_allreduce(const se12_matrix* m, const uint16_t* x, int batch, int ldx, float* y, int ldy, void* workspace,
@@ -461,8 +456,8 @@ int se12_gemv_allreduce(const se12_matrix* m, const uint16_t* x, int batch, int 
                                                " rows, the peer buffers hold " + std::to_string(g->rows_cap));
   if (!g->epoch) return fail(SE12_ERR_INVALID_ARGUMENT, "null epoch counter");
   for (int r = 0; r < g->world; ++r) {
-    if (!g->recv[r] || !g->flags[r]) return fail(SE12_ERR_INVALID_ARGUMENT, "null peer buffer");
-    if (!aligned16(g->recv[r]) || !aligned16(g->flags[r]))
+    if (!g->recv[r]) return fail(SE12_ERR_INVALID_ARGUMENT, "null peer buffer");
+    if (!aligned16(g->recv[r]))
       return fail(SE12_ERR_MISALIGNED, "peer buffers must be 16-byte aligned");
   }
   int st = check_gemv_io(m->view.rows, m->view.cols, x, batch, ldx, y, ldy);
@@ -488,17 +483,13 @@ int se12_gemv_allreduce(const se12_matrix* m, const uint16_t* x, int batch, int 
   a.peers.world = g->world;
   a.peers.rank = g->rank;
   a.peers.rows_cap = g->rows_cap;
-  a.peers.tile_rows_cap = (g->rows_cap + SE12_TILE_ROWS - 1) / SE12_TILE_ROWS;
   for (int r = 0; r < g->world; ++r) {
-    a.peers.recv[r] = g->recv[r];
-    a.peers.flags[r] = g->flags[r];
+    a.peers.recv[r] = static_cast<unsigned long long*>(g->recv[r]);
   }
   a.peers.epoch = g->epoch;
   cudaError_t err = se12::launch_gemv(false, m->sm_map, m->ec_map, a, c.nblocks, c.smem,
                                       static_cast<cudaStream_t>(stream), true);
   if (err != cudaSuccess) return cuda_fail(err, "se12_gemv_allreduce launch");
-  err = se12::launch_bump_epoch(g->epoch, static_cast<cudaStream_t>(stream));
-  if (err != cudaSuccess) return cuda_fail(err, "se12_gemv_allreduce epoch launch");
   return SE12_OK;
 }
 

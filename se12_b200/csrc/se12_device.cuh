@@ -192,6 +192,37 @@ __device__ __forceinline__ bool wait_epoch_sys(const int* flag, int e) {
   return true;
 }
 
+// 64-bit relaxed stores and loads at system scope: a value and its epoch in
+// one naturally aligned word, which a reader sees whole or not at all.
+__device__ __forceinline__ void st_word_sys(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned long long ld_word_sys(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Waits until *p holds epoch e in its high half; returns its low half in
+// *value. False (and kStatusWaitTimeout raised) after kWaitLimitNs.
+__device__ __forceinline__ bool wait_word_sys(const unsigned long long* p, unsigned e, unsigned* value) {
+  unsigned long long w = ld_word_sys(p);
+  if (static_cast<unsigned>(w >> 32) != e) {
+    const unsigned long long start = global_ns();
+    do {
+      __nanosleep(20);
+      if (global_ns() - start > kWaitLimitNs) {
+        raise_status(kStatusWaitTimeout);
+        return false;
+      }
+      w = ld_word_sys(p);
+    } while (static_cast<unsigned>(w >> 32) != e);
+  }
+  *value = static_cast<unsigned>(w);
+  return true;
+}
+
 // ------------------------------------------------------------------ L2 policy
 
 __device__ __forceinline__ uint64_t policy_evict_first() {

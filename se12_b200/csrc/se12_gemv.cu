@@ -410,12 +410,29 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
     // Deterministic (CTA order), no atomics. Every CTA of the grid is
     // resident or done before a dependent grid may launch, so the flag
     // waits cannot be starved; they are bounded all the same.
-    if (tend <= tstart) return;
+    // Peer all-reduce: this call's epoch is the rank's call counter + 1; the
+    // last CTA to finish (every CTA counts itself once, after reading the
+    // counter) bumps it, so that every CTA of a call reads the same value.
+    const PeerArgs& P = a.peers;
+    auto finish_call = [&]() {
+      if (P.world > 1 && lane == 0) {
+        __threadfence();
+        if (atomicAdd(P.epoch + 1, 1) == G - 1) {
+          atomicExch(P.epoch + 1, 0);
+          atomicAdd(P.epoch, 1);
+        }
+      }
+    };
+    if (tend <= tstart) {
+      if (P.world > 1) {
+        grid_dependency_wait();
+        finish_call();
+      }
+      return;
+    }
     const int tr_last = (tend - 1) / KT;
     const int outs = 16 * B;  // <= 256: up to 8 values per lane
     grid_dependency_wait();   // y and the workspace may be in use by the previous kernel
-    // peer all-reduce: this call's epoch (the counter is bumped after each call)
-    const PeerArgs& P = a.peers;
     const int epoch = (P.world > 1) ? __ldcg(P.epoch) + 1 : 0;
     for (int tr = tr_first; tr <= tr_last; ++tr) {
       const int lr = tr - tr_first, pb = lr & 1;
@@ -472,33 +489,31 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
         }
       }
       if (P.world > 1 && good) {
-        // All-reduce of the row across the peer group: store it into every
-        // rank's receive slot (this rank's own included) for this epoch's
-        // parity, flag it at every rank, wait for every rank's flag in
-        // this rank's memory, then sum the slots in rank order, so that
-        // every rank writes the same bits. A rank can be at most one call
-        // ahead of another (it needs the other's rows of the call in
-        // between), so two parities keep a slot from being overwritten
-        // while it is read.
+        // All-reduce of the row across the peer group: store each value,
+        // with this call's epoch in the same 64-bit word, into every rank's
+        // receive slot (this rank's own included) for this epoch's parity;
+        // then wait until every rank's words for the row carry the epoch and
+        // sum them in rank order, so that every rank writes the same bits.
+        // A word is stored whole, so the data is its own flag (no fence).
+        // A rank can be at most one call ahead of another (it needs the
+        // other's rows of the call in between), so two parities keep a slot
+        // from being overwritten while it is read.
         const size_t slot = static_cast<size_t>(16) * P.rows_cap;
         const size_t base = static_cast<size_t>((epoch & 1) * P.world) * slot;
+        const unsigned long long tag = static_cast<unsigned long long>(static_cast<unsigned>(epoch)) << 32;
         for (int r = 0; r < P.world; ++r) {
-          float* dst = P.recv[r] + base + P.rank * slot;
+          unsigned long long* dst = P.recv[r] + base + P.rank * slot;
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
             const int idx = lane + 32 * j;
             const int row = idx / B, b = idx - row * B;
             const int grow = tr * kTileRows + row;
-            if (idx < outs && grow < N) dst[static_cast<size_t>(b) * P.rows_cap + grow] = v[j];
+            if (idx < outs && grow < N)
+              st_word_sys(dst + static_cast<size_t>(b) * P.rows_cap + grow, tag | __float_as_uint(v[j]));
           }
         }
-        __threadfence_system();
-        __syncwarp();
-        if (lane < P.world) st_release_sys(P.flags[lane] + P.rank * P.tile_rows_cap + tr, epoch);
+        const unsigned long long* mine = P.recv[P.rank] + base;
         bool arrived = true;
-        if (lane < P.world) arrived = wait_epoch_sys(P.flags[P.rank] + lane * P.tile_rows_cap + tr, epoch);
-        good = __all_sync(0xFFFFFFFFu, arrived);
-        const float* mine = P.recv[P.rank] + base;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const int idx = lane + 32 * j;
@@ -506,10 +521,16 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
           const int grow = tr * kTileRows + row;
           if (idx < outs && grow < N) {
             float sum = 0.f;
-            for (int r = 0; r < P.world; ++r) sum += __ldcv(mine + r * slot + static_cast<size_t>(b) * P.rows_cap + grow);
+            for (int r = 0; r < P.world && arrived; ++r) {
+              unsigned bits = 0u;
+              arrived = wait_word_sys(mine + r * slot + static_cast<size_t>(b) * P.rows_cap + grow,
+                                      static_cast<unsigned>(epoch), &bits);
+              sum += __uint_as_float(bits);
+            }
             v[j] = sum;
           }
         }
+        good = __all_sync(0xFFFFFFFFu, arrived);
       }
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
@@ -522,6 +543,8 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
       }
       for (int c = blockIdx.x + 1 + lane; c <= c_hi; c += 32) counters[c] = 0;
     }
+    __syncwarp();
+    finish_call();
     return;
   }
 
@@ -902,17 +925,6 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
     // stage on; 4-tile stages decode here, ahead of the stage's row ends
     if (i + 1 < nstages) fetch_stage(!FULL);
   }
-}
-
-// The peer all-reduce's call counter, bumped once the GEMV has finished
-// (stream order), so that every CTA of a call reads the same epoch.
-__global__ void bump_epoch_kernel(int* epoch) {
-  if (threadIdx.x == 0) *epoch += 1;
-}
-
-cudaError_t launch_bump_epoch(int* epoch, cudaStream_t stream) {
-  bump_epoch_kernel<<<1, 32, 0, stream>>>(epoch);
-  return cudaGetLastError();
 }
 
 cudaError_t launch_gemv(bool raw, const CUtensorMap& map0, const CUtensorMap& map1, const GemvArgs& a, int nblocks,

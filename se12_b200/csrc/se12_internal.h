@@ -50,10 +50,9 @@ struct PeerArgs {
   int world;                 // 1: no all-reduce
   int rank;
   int rows_cap;              // rows a receive slot holds (>= the matrix rows)
-  int tile_rows_cap;         // tile rows a flag slot holds
-  float* recv[kMaxPeers];    // rank s's receive buffer (peer-mapped): [2 parities][world][16 batch][rows_cap] fp32
-  int* flags[kMaxPeers];     // rank s's flags (peer-mapped): [world][tile_rows_cap], last epoch received
-  const int* epoch;          // this rank's call counter; a call uses epoch + 1 (bumped after the call)
+  unsigned long long* recv[kMaxPeers];  // rank s's receive buffer (peer-mapped): [2 parities][world][16 batch][rows_cap]
+                                        // words, each epoch << 32 | fp32 bits
+  int* epoch;                // this rank's [call counter, CTAs finished]; a call uses counter + 1 (its last CTA bumps it)
 };
 
 // Arguments of one fused (or dense baseline) GEMV launch: y = x . W^T.
@@ -132,7 +131,6 @@ inline size_t gemv_smem_bytes(bool raw, bool full_tiles, bool x_resident, int st
 }
 
 // Kernel launchers (defined in the .cu files).
-cudaError_t launch_bump_epoch(int* epoch, cudaStream_t stream);
 cudaError_t launch_gemv(bool raw, const CUtensorMap& map0, const CUtensorMap& map1, const GemvArgs& a, int nblocks,
                         size_t smem, cudaStream_t stream, bool pdl);
 cudaError_t launch_prepare(const MatrixView& m, uint16_t* escape_pos, int32_t* fallback_index, cudaStream_t stream);

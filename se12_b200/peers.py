@@ -4,8 +4,9 @@ Tensor parallelism with the input columns sharded (attention output and MLP
 down projections) needs, after each rank's GEMV of its column shard, the sum
 of all ranks' outputs on every rank. ``PeerGroup`` sets up what the fused
 kernel needs for that across the ranks of a ``torch.distributed`` group,
-one GPU per rank on one node: a receive buffer and a flag array per rank,
-mapped into every other rank's address space with CUDA IPC
+one GPU per rank on one node: a receive buffer per rank (values tagged
+with the call's epoch), mapped into every other rank's address space with
+CUDA IPC
 (``se12_ipc_handle`` / ``se12_ipc_open``: plain peer memory over NVLink, no
 multicast object), and a per-rank call counter.
 ``gemv_allreduce`` then runs one kernel per call: no NCCL on this path.
@@ -42,12 +43,8 @@ class PeerGroup:
         self.rows_cap = int(rows_cap)
         lib = _lib.load()
         recv_bytes = lib.se12_peer_recv_bytes(self.world, self.rows_cap)
-        flag_bytes = lib.se12_peer_flag_bytes(self.world, self.rows_cap)
-        # one buffer per rank, mapped once into every other rank: [recv][flags]
-        flag_off = (recv_bytes + 255) // 256 * 256
-        self.buffer = torch.zeros(flag_off + (flag_bytes + 255) // 256 * 256, dtype=torch.uint8, device=self.device)
-        self.recv = self.buffer[:recv_bytes].view(torch.float32)
-        self.flags = self.buffer[flag_off:flag_off + flag_bytes].view(torch.int32)
+        # one buffer per rank, mapped once into every other rank
+        self.buffer = torch.zeros(recv_bytes, dtype=torch.uint8, device=self.device)
         self.epoch = torch.zeros(4, dtype=torch.int32, device=self.device)  # this rank's call counter (not shared)
         torch.cuda.synchronize(self.device)
         handle = (ctypes.c_uint8 * 64)()
@@ -71,7 +68,6 @@ class PeerGroup:
         self.struct.world, self.struct.rank, self.struct.rows_cap = self.world, self.rank, self.rows_cap
         for r in range(self.world):
             self.struct.recv[r] = bases[r]
-            self.struct.flags[r] = bases[r] + flag_off
         self.struct.epoch = self.epoch.data_ptr()
         self._group = group
         dist.barrier(group=group)
