@@ -636,33 +636,54 @@ def run_tp(args) -> None:
     shapes = CONFIGS[args.config if args.config != "gemma2-2b" else "gemma2-27b"]
     layers = args.layers if args.layers is not None else shapes.layers
     batch = args.batch
-    specs = []
-    for layer in range(layers):
-        for j, (name, rows, cols, kind) in enumerate(shapes.layer_matrices()):
-            specs.append((name, rows, cols, kind, 1000 * layer + j))
-    if not args.no_lm_head:
-        name, rows, cols, kind = shapes.lm_head()
-        specs.append((name, rows, cols, kind, 999_999))
+    from se12_b200.device import DeviceSe12Matrix
+
+    # (names, kind) per GEMV of a layer: row-sharded projections that read the
+    # same input (q/k/v, gate/up) are one segmented matrix of their shards
+    groups, members = dict(shapes.GROUPS), {m: g for g, ms in shapes.GROUPS for m in ms}
+    specs, done = [], set()
+    for name, _, _, _ in shapes.layer_matrices():
+        if name in done:
+            continue
+        names = groups[members[name]] if (name in members and not args.no_group) else (name,)
+        specs.append(names)
+        done.update(names)
+    dims = {name: (rows, cols) for name, rows, cols, _ in shapes.layer_matrices()}
     t_setup = time.perf_counter()
     gen = torch.Generator(device=device)
     gen.manual_seed(1)
     x_full = torch.randn(batch, shapes.hidden, generator=gen, device=device).to(torch.bfloat16)
     ops = []  # (matrix, x, y, collective) in step order
     local_bytes = 0
-    for name, rows, cols, kind, seed in specs:
+    plan_of = {}
+
+    def shard(name, rows, cols, seed):
         plan = megatron_plan(name)
         if plan == "rows":
             r0, r1 = row_range(rows, world, rank)
-            w = synthetic_bf16(torch, r1 - r0, cols, seed * 64 + rank, device)
+            return encode_device(synthetic_bf16(torch, r1 - r0, cols, seed * 64 + rank, device)), plan
+        c0, c1 = col_range(cols, world, rank)
+        return encode_device(synthetic_bf16(torch, rows, c1 - c0, seed * 64 + rank, device)), plan
+
+    seqs = [(layer, names) for layer in range(layers) for names in specs]
+    if not args.no_lm_head:
+        seqs.append((None, ("lm_head",)))
+    order = {name: j for j, (name, _, _, _) in enumerate(shapes.layer_matrices())}
+    for layer, names in seqs:
+        parts = []
+        for name in names:
+            rows, cols = dims[name] if layer is not None else shapes.lm_head()[1:3]
+            seed = 1000 * layer + order[name] if layer is not None else 999_999
+            m, plan = shard(name, rows, cols, seed)
+            parts.append(m)
+        m = DeviceSe12Matrix.concatenate(parts) if len(parts) > 1 else parts[0]
+        del parts
+        if plan == "rows":
             x = x_full
         else:
-            c0, c1 = col_range(cols, world, rank)
-            w = synthetic_bf16(torch, rows, c1 - c0, seed * 64 + rank, device)
-            x = torch.randn(batch, c1 - c0, generator=gen, device=device).to(torch.bfloat16)
-        m = encode_device(w)
-        del w
+            x = torch.randn(batch, m.cols, generator=gen, device=device).to(torch.bfloat16)
         y = torch.empty(batch, m.rows, dtype=torch.float32, device=device)
-        coll = "all_reduce" if plan == "cols" else ("all_gather" if name == "lm_head" else None)
+        coll = "all_reduce" if plan == "cols" else ("all_gather" if names[0] == "lm_head" else None)
         ops.append((m, x, y, coll))
         local_bytes += m.byte_size + batch * m.cols * 2 + batch * m.rows * 4
     torch.cuda.synchronize()
@@ -728,7 +749,8 @@ def run_tp(args) -> None:
             "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic",
             "config": {"workload": f"{shapes.name} tensor-parallel decode-step GEMV set: {layers} layers x 7 + lm_head, "
-                       f"batch {batch}", "batch": batch, "weights": weights,
+                       f"batch {batch}", "batch": batch, "weights": weights, "gemvs_per_step": len(ops),
+                       "grouping": "none" if args.no_group else "row shards of q/k/v and of gate/up as one segmented matrix each",
                        "bytes_per_step": float(total_bytes.item()),
                        "parallelism": f"tp{world}: q/k/v/gate/up by rows, o/down by columns + "
                        + ("all-reduce fused into the GEMV (peer memory)" if fused else "NCCL all-reduce")
@@ -737,6 +759,7 @@ def run_tp(args) -> None:
             "per_gpu_gbs": value / world,
             "nccl_collectives_per_step": ((0 if fused else 2 * layers) + (0 if args.no_lm_head else 1)) if world > 1 else 0,
             "fused_allreduces_per_step": 2 * layers if fused else 0,
+            "allreduce": ("fused into the GEMV over peer memory" if fused else "NCCL") if world > 1 else None,
             "clocks": sampler.summary(),
         }
         print(json.dumps(line), flush=True)

@@ -132,7 +132,7 @@ __device__ __forceinline__ T lds_at(const uint8_t* smem, uint32_t offset) {
   return *reinterpret_cast<const T*>(smem + offset);
 }
 
-template <int NB, bool RAW, bool XRES, bool FULL>
+template <int NB, bool RAW, bool XRES, bool FULL, bool AR>
 __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_constant__ CUtensorMap map0,
                                                                const __grid_constant__ CUtensorMap map1,
                                                                const GemvArgs a) {
@@ -415,7 +415,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
     // counter) bumps it, so that every CTA of a call reads the same value.
     const PeerArgs& P = a.peers;
     auto finish_call = [&]() {
-      if (P.world > 1 && lane == 0) {
+      if (AR && lane == 0) {
         __threadfence();
         if (atomicAdd(P.epoch + 1, 1) == G - 1) {
           atomicExch(P.epoch + 1, 0);
@@ -424,7 +424,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
       }
     };
     if (tend <= tstart) {
-      if (P.world > 1) {
+      if (AR) {
         grid_dependency_wait();
         finish_call();
       }
@@ -433,7 +433,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
     const int tr_last = (tend - 1) / KT;
     const int outs = 16 * B;  // <= 256: up to 8 values per lane
     grid_dependency_wait();   // y and the workspace may be in use by the previous kernel
-    const int epoch = (P.world > 1) ? __ldcg(P.epoch) + 1 : 0;
+    const int epoch = AR ? __ldcg(P.epoch) + 1 : 0;
     for (int tr = tr_first; tr <= tr_last; ++tr) {
       const int lr = tr - tr_first, pb = lr & 1;
       if (!mbar_wait(&deposited[pb], static_cast<uint32_t>(lr >> 1) & 1u)) break;
@@ -488,7 +488,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
           for (int j = 0; j < 8; ++j) v[j] += p[j];
         }
       }
-      if (P.world > 1 && good) {
+      if (AR && good) {
         // All-reduce of the row across the peer group: store each value,
         // with this call's epoch in the same 64-bit word, into every rank's
         // receive slot (this rank's own included) for this epoch's parity;
@@ -933,14 +933,23 @@ cudaError_t launch_gemv(bool raw, const CUtensorMap& map0, const CUtensorMap& ma
   // [batch blocks][kind: SE12 4-tile, SE12 8-tile, dense][x resident];
   // 8-tile stages always hold x resident
   static const Kernel table[2][3][2] = {
-      {{gemv_kernel<1, false, false, false>, gemv_kernel<1, false, true, false>},
-       {nullptr, gemv_kernel<1, false, true, true>},
-       {gemv_kernel<1, true, false, false>, gemv_kernel<1, true, true, false>}},
-      {{gemv_kernel<2, false, false, false>, gemv_kernel<2, false, true, false>},
-       {nullptr, gemv_kernel<2, false, true, true>},
-       {gemv_kernel<2, true, false, false>, gemv_kernel<2, true, true, false>}}};
+      {{gemv_kernel<1, false, false, false, false>, gemv_kernel<1, false, true, false, false>},
+       {nullptr, gemv_kernel<1, false, true, true, false>},
+       {gemv_kernel<1, true, false, false, false>, gemv_kernel<1, true, true, false, false>}},
+      {{gemv_kernel<2, false, false, false, false>, gemv_kernel<2, false, true, false, false>},
+       {nullptr, gemv_kernel<2, false, true, true, false>},
+       {gemv_kernel<2, true, false, false, false>, gemv_kernel<2, true, true, false, false>}}};
+  // with the peer all-reduce (SE12 only): [batch blocks][4-tile, 8-tile][x resident]
+  static const Kernel table_ar[2][2][2] = {
+      {{gemv_kernel<1, false, false, false, true>, gemv_kernel<1, false, true, false, true>},
+       {nullptr, gemv_kernel<1, false, true, true, true>}},
+      {{gemv_kernel<2, false, false, false, true>, gemv_kernel<2, false, true, false, true>},
+       {nullptr, gemv_kernel<2, false, true, true, true>}}};
   const int kind = raw ? 2 : (a.full_tiles ? 1 : 0);
-  const Kernel kernel = table[nblocks == 1 ? 0 : 1][kind][a.x_resident ? 1 : 0];
+  const int blocks = nblocks == 1 ? 0 : 1;
+  const bool ar = a.peers.world > 1;
+  if (ar && raw) return cudaErrorInvalidValue;
+  const Kernel kernel = ar ? table_ar[blocks][kind][a.x_resident ? 1 : 0] : table[blocks][kind][a.x_resident ? 1 : 0];
   if (!kernel) return cudaErrorInvalidValue;
   cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (err != cudaSuccess) return err;
