@@ -520,12 +520,22 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
           const int row = idx / B, b = idx - row * B;
           const int grow = tr * kTileRows + row;
           if (idx < outs && grow < N) {
+            const unsigned long long* src = mine + static_cast<size_t>(b) * P.rows_cap + grow;
+            // every rank's word in flight at once; poll again only those
+            // that have not arrived
+            unsigned long long w[kMaxPeers];
+#pragma unroll
+            for (int r = 0; r < kMaxPeers; ++r)
+              if (r < P.world) w[r] = ld_word_sys(src + r * slot);
             float sum = 0.f;
-            for (int r = 0; r < P.world && arrived; ++r) {
-              unsigned bits = 0u;
-              arrived = wait_word_sys(mine + r * slot + static_cast<size_t>(b) * P.rows_cap + grow,
-                                      static_cast<unsigned>(epoch), &bits);
-              sum += __uint_as_float(bits);
+#pragma unroll
+            for (int r = 0; r < kMaxPeers; ++r) {
+              if (r < P.world) {
+                unsigned bits = static_cast<unsigned>(w[r]);
+                if (static_cast<unsigned>(w[r] >> 32) != static_cast<unsigned>(epoch))
+                  arrived = wait_word_sys(src + r * slot, static_cast<unsigned>(epoch), &bits) && arrived;
+                sum += __uint_as_float(bits);
+              }
             }
             v[j] = sum;
           }
