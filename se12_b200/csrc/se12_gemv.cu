@@ -74,8 +74,9 @@ __device__ __forceinline__ uint32_t select_bits(uint32_t a, uint32_t b, uint32_t
 }
 
 // Exponent byte of code c as the decode table stores it: rotated right by
-// one bit, so that the byte placed twice in a half word ([b, b]) has the
-// exponent in bits 7..14. The escape code maps to exponent 0.
+// one bit, so that its top bit is the exponent's lowest bit (bit 7 of the
+// BF16, in its low byte) and its low 7 bits the exponent's upper bits (bits
+// 8..14, in its high byte). The escape code maps to exponent 0.
 __host__ __device__ __forceinline__ uint32_t table_byte(const uint8_t* codebook, int c) {
   const uint32_t e = (c == kEscapeCode) ? 0u : codebook[c];
   return ((e >> 1) | (e << 7)) & 0xFFu;
@@ -89,9 +90,11 @@ __host__ __device__ __forceinline__ uint32_t table_byte(const uint8_t* codebook,
 //    and tab[2..3] in two permutes per 4 codes, and a byte mask built from
 //    each code's bit 3 (a selector nibble with bit 3 set copies a byte's
 //    top bit) picks between them.
-//  * Each BF16 is the sign and mantissa bits (0x807F) of its sm byte placed
-//    twice, [s, s], and the exponent bits (0x7F80) of its table byte placed
-//    twice, [b, b].
+//  * A BF16's low byte is the mantissa bits (0x7F) of its sm byte and the
+//    top bit of its table byte (the exponent's lowest bit); its high byte
+//    is the sm byte's sign bit and the table byte's other 7 bits. Two
+//    selects build the four low and the four high bytes of 4 weights at
+//    once, two permutes interleave them: 4 instructions per 4 weights.
 __device__ __forceinline__ void decode8(uint2 s, uint32_t e, const uint32_t (&tab)[4], uint32_t (&p)[4]) {
   const uint32_t sel03 = e & 0x77777777u;   // selectors for weights 0..3 (low 16 bits)
   const uint32_t sel47 = __umulhi(sel03, 0x10000u);  // weights 4..7: sel03 >> 16 on the multiply pipe (the shift pipe is the busier one)
@@ -100,10 +103,14 @@ __device__ __forceinline__ void decode8(uint2 s, uint32_t e, const uint32_t (&ta
   const uint32_t hi47 = prmt(e4, e, 0xFBEAu);  // weights 4..7
   const uint32_t x03 = select_bits(prmt(tab[2], tab[3], sel03), prmt(tab[0], tab[1], sel03), hi03);
   const uint32_t x47 = select_bits(prmt(tab[2], tab[3], sel47), prmt(tab[0], tab[1], sel47), hi47);
-  p[0] = select_bits(prmt(s.x, 0, 0x1100u), prmt(x03, 0, 0x1100u), 0x807F807Fu);
-  p[1] = select_bits(prmt(s.x, 0, 0x3322u), prmt(x03, 0, 0x3322u), 0x807F807Fu);
-  p[2] = select_bits(prmt(s.y, 0, 0x1100u), prmt(x47, 0, 0x1100u), 0x807F807Fu);
-  p[3] = select_bits(prmt(s.y, 0, 0x3322u), prmt(x47, 0, 0x3322u), 0x807F807Fu);
+  const uint32_t lo03 = select_bits(s.x, x03, 0x7F7F7F7Fu);  // low bytes of weights 0..3
+  const uint32_t up03 = select_bits(s.x, x03, 0x80808080u);  // high bytes
+  const uint32_t lo47 = select_bits(s.y, x47, 0x7F7F7F7Fu);
+  const uint32_t up47 = select_bits(s.y, x47, 0x80808080u);
+  p[0] = prmt(lo03, up03, 0x5140u);  // [lo0, up0, lo1, up1]
+  p[1] = prmt(lo03, up03, 0x7362u);  // [lo2, up2, lo3, up3]
+  p[2] = prmt(lo47, up47, 0x5140u);
+  p[3] = prmt(lo47, up47, 0x7362u);
 }
 
 // Padding weights (columns >= K of the last tile column) are +0.0 in the
