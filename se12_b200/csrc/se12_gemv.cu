@@ -885,22 +885,22 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
         if (FULL) {
           // half 0 was decoded by fetch_stage for the first stage
           const bool plain = fbi < 0 && !pad_inf;
-          if (kPredecodeFirst && i == 0) {
-            mma_tile(s, kt_mine, 0);
-          } else if (plain) {
-            decode_mma(s, kt_mine, 0);
-          } else {
-            load_frags(s, kt_mine, fbi, 0);
-            mma_tile(s, kt_mine, 0);
-          }
-          // the escape products before half 1, so that their record is
-          // dead during its decode
-          if (fbi < 0) fix_escapes(s, kt_mine, esc_rec);
+          // The two halves run as a loop, not unrolled: one copy of the
+          // decode in the instruction cache. The escape products come
+          // after half 0, so that their record is dead during half 1.
           if (plain) {
-            decode_mma(s, kt_mine, 1);
+#pragma unroll 1
+            for (int h = 0; h < 2; ++h) {
+              decode_mma(s, kt_mine, h);
+              if (h == 0) fix_escapes(s, kt_mine, esc_rec);
+            }
           } else {
-            load_frags(s, kt_mine, fbi, 1);
-            mma_tile(s, kt_mine, 1);
+#pragma unroll 1
+            for (int h = 0; h < 2; ++h) {
+              if (!(kPredecodeFirst && i == 0 && h == 0)) load_frags(s, kt_mine, fbi, h);
+              mma_tile(s, kt_mine, h);
+              if (h == 0 && fbi < 0) fix_escapes(s, kt_mine, esc_rec);
+            }
           }
         } else {
           mma_tile(s, kt_mine, 0);
