@@ -136,10 +136,11 @@ int tiles_of(int rows, int cols) {
 //  * Among these, the smallest critical path of the longest CTA: stages x
 //    stage time + the stream-K fixup. In units of a 4-tile stage's overhead-
 //    inclusive half-tile time: a 4-tile stage (two CTAs per SM) costs 1.65,
-//    an 8-tile stage 2.65 (each warp does a whole tile); x 0.8 when one CTA
-//    has the SM to itself, x 1.5 when x is staged; a fixup 3.9 (a round trip
-//    through L2 on a loaded GPU). Fitted to timings of every choice on
-//    Gemma-2 2B/9B/27B shapes at batch 1, 4 and 16.
+//    an 8-tile stage 2.0 (each warp does a whole tile, decoding it group by
+//    group); x 0.95 when one CTA has the SM to itself, x 1.5 when x is
+//    staged; a fixup 3.0 (a round trip through L2 on a loaded GPU). Fitted
+//    to stacked timings of every choice on Gemma-2 2B/9B/27B shapes at batch
+//    1, 4 and 16.
 struct LaunchConfig {
   int grid;
   int stages;
@@ -173,17 +174,18 @@ LaunchConfig choose_config(bool raw, int tiles, int cols, int batch, int sm_coun
   const MemoryChoice mem8 = raw ? MemoryChoice{0, 0, 0} : choose_memory(raw, true, batch, cols);
   const int tile_cols = (cols + SE12_TILE_COLS - 1) / SE12_TILE_COLS;
   const int tile_rows = tiles / tile_cols;
-  constexpr double kStageOverhead = 0.65;
-  constexpr double kAloneFactor = 0.8;
+  constexpr double kStageCost4 = 1.65;  // a 4-tile stage, two CTAs per SM, x resident
+  constexpr double kStageCost8 = 2.0;   // an 8-tile stage
+  constexpr double kAloneFactor = 0.95;
   constexpr double kStagedXFactor = 1.5;
-  constexpr double kFixup = 3.9;
+  constexpr double kFixup = 3.0;
   LaunchConfig best{};
   double best_cost = 0;
   for (const bool full : {false, true}) {
     const MemoryChoice& mem = full ? mem8 : mem4;
     if (!mem.per_sm) continue;
     const int stage = se12::stage_tiles(full);
-    const double stage_cost = ((full ? 2 : 1) + kStageOverhead) * (mem.per_sm == 1 ? kAloneFactor : 1.0) *
+    const double stage_cost = (full ? kStageCost8 : kStageCost4) * (mem.per_sm == 1 ? kAloneFactor : 1.0) *
                               (mem.x_resident ? 1.0 : kStagedXFactor);
     const int slots = mem.per_sm * sm_count;
     const int units = (tiles + stage - 1) / stage;
