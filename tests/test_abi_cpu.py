@@ -93,3 +93,32 @@ def test_null_and_range_arguments_are_rejected(lib):
     assert lib.se12_gemv(None, None, 1, 256, None, 16, None, 0, None) == 1
     assert lib.se12_matrix_create(None, None) == 1
     assert lib.bf16_gemv(None, 16, 256, 256, None, 1, 256, None, 16, None, 0, None) == 1
+
+
+def test_peer_group_sizes_and_argument_checks(lib):
+    """The fused GEMV + all-reduce's host checks (no device needed): buffer
+    sizes, and a call without a matrix or with a bad group is refused."""
+    from se12_b200 import _lib
+
+    assert lib.se12_peer_recv_bytes(2, 4608) == 2 * 2 * 16 * 4608 * 8
+    assert lib.se12_peer_recv_bytes(9, 16) == 0 and lib.se12_peer_recv_bytes(2, 0) == 0
+    g = _lib.Se12PeerGroupStruct()
+    g.world, g.rank, g.rows_cap = 1, 0, 16
+    assert lib.se12_gemv_allreduce(None, None, 1, 256, None, 16, None, 0, ctypes.byref(g), None) == 1
+    assert "null matrix" in lib.se12_last_error().decode()
+    assert lib.se12_ipc_close(None) == 0
+    assert lib.se12_ipc_handle(None, None, None) == 1
+
+
+def test_segmented_create_rejects_bad_segments(lib):
+    from se12_b200 import _lib
+
+    s = _lib.Se12StreamsStruct()
+    s.rows, s.cols, s.tile_rows, s.tile_cols, s.escape_budget, s.format_version = 40, 256, 16, 256, 16, 1
+    rows = (ctypes.c_int32 * 2)(20, 20)  # the first segment is not a multiple of 16 rows
+    books = (ctypes.c_uint8 * 30)()
+    handle = ctypes.c_void_p()
+    assert lib.se12_matrix_create_segmented(ctypes.byref(s), 2, rows, books, ctypes.byref(handle)) == 1
+    assert "multiple of 16" in lib.se12_last_error().decode()
+    rows = (ctypes.c_int32 * 5)(16, 16, 16, 16, 16)
+    assert lib.se12_matrix_create_segmented(ctypes.byref(s), 5, rows, books, ctypes.byref(handle)) == 1
