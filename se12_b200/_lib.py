@@ -52,7 +52,7 @@ class Se12LaunchConfigStruct(ctypes.Structure):
     """Mirror of ``se12_launch_config`` in include/se12.h."""
 
     _fields_ = [(name, ctypes.c_int32) for name in
-                ("grid", "threads", "smem_bytes", "ctas_per_sm", "stage_tiles", "stages", "x_resident", "row_mode")]
+                ("grid", "threads", "smem_bytes", "ctas_per_sm", "stage_tiles", "stages", "x_resident", "row_mode", "wide")]
 
 
 class Se12PeerGroupStruct(ctypes.Structure):

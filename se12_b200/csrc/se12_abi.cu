@@ -138,7 +138,11 @@ int tiles_of(int rows, int cols) {
 //    inclusive half-tile time: a 4-tile stage (two CTAs per SM) costs 1.65,
 //    an 8-tile stage 2.0 (each warp does a whole tile, decoding it group by
 //    group); x 0.95 when one CTA has the SM to itself, x 1.5 when x is
-//    staged; a fixup 3.0 (a round trip through L2 on a loaded GPU). Fitted
+//    staged; a fixup 3.0 (a round trip through L2 on a loaded GPU). The
+//    wide layout (SE12, x resident, one CTA per SM with kWideGroups 4-tile
+//    stages in work at once, row mode only) costs 3.0 per CTA (its longer
+//    fill and drain) + 0.48 per 4-tile stage: it streams a little faster and
+//    starts slower, so it wins on large matrices only. Fitted
 //    to stacked timings of every choice on Gemma-2 2B/9B/27B shapes at batch
 //    1, 4 and 16.
 struct LaunchConfig {
@@ -148,6 +152,7 @@ struct LaunchConfig {
   int x_resident;
   int row_mode;
   int full_tiles;
+  int wide;
   size_t smem;
 };
 
@@ -169,7 +174,19 @@ MemoryChoice choose_memory(bool raw, bool full, int batch, int cols) {
   return {0, 0, 0};
 }
 
-LaunchConfig choose_config(bool raw, int tiles, int cols, int batch, int sm_count) {
+// The wide layout (one CTA per SM, kWideGroups stages in work at once):
+// x resident and the deepest pipeline of at least kWideGroups + 2 stages
+// that fits (with 1 KB to spare for the kernel's static shared memory), so
+// that two stages or more are in flight.
+MemoryChoice choose_memory_wide(int batch, int cols) {
+  if (batch > 8) return {0, 0, 0};  // one block of 8 batch columns (more spill at 80 registers)
+  for (int stages = se12::kWideGroups + 4; stages >= se12::kWideGroups + 2; --stages)
+    if (se12::gemv_smem_bytes(false, false, true, stages, batch, cols, true) + 1024 <= se12::kMaxSmemPerCta)
+      return {1, stages, 1};
+  return {0, 0, 0};
+}
+
+LaunchConfig choose_config(bool raw, int tiles, int cols, int batch, int sm_count, bool allow_wide = true) {
   const MemoryChoice mem4 = choose_memory(raw, false, batch, cols);
   const MemoryChoice mem8 = raw ? MemoryChoice{0, 0, 0} : choose_memory(raw, true, batch, cols);
   const int tile_cols = (cols + SE12_TILE_COLS - 1) / SE12_TILE_COLS;
@@ -179,6 +196,8 @@ LaunchConfig choose_config(bool raw, int tiles, int cols, int batch, int sm_coun
   constexpr double kAloneFactor = 0.95;
   constexpr double kStagedXFactor = 1.5;
   constexpr double kFixup = 3.0;
+  constexpr double kWideFixed = 3.0;   // the wide layout: a longer pipeline fill and drain per CTA,
+  constexpr double kWideStage = 0.48;  // then a 4-tile stage (kWideGroups in work at once, one CTA per SM)
   LaunchConfig best{};
   double best_cost = 0;
   for (const bool full : {false, true}) {
@@ -205,12 +224,32 @@ LaunchConfig choose_config(bool raw, int tiles, int cols, int batch, int sm_coun
       best.grid = row_mode ? grid_rows : grid_sk;
     }
   }
+  const MemoryChoice memw = (raw || !allow_wide) ? MemoryChoice{0, 0, 0} : choose_memory_wide(batch, cols);
+  if (memw.per_sm) {
+    // row mode only: with the fixup, stream-K in the wide layout never
+    // beats stream-K in the others (finer grained, two CTAs per SM)
+    const int stage = se12::stage_tiles(false);
+    const int grid_rows = std::max(1, std::min(tile_rows, sm_count));
+    const int rows_per_cta = (tile_rows + grid_rows - 1) / grid_rows;
+    const int stages_rows = (rows_per_cta * tile_cols + stage - 1) / stage;
+    const double cost = kWideFixed + stages_rows * kWideStage;
+    if (!best.stages || cost < best_cost) {
+      best_cost = cost;
+      best.full_tiles = 0;
+      best.wide = 1;
+      best.x_resident = 1;
+      best.stages = memw.stages;
+      best.row_mode = 1;
+      best.grid = grid_rows;
+    }
+  }
   if (!best.stages) {  // not reached for batch <= 16: 4-tile stages with staged x, 2 stages, fit one CTA per SM
     best.stages = 2;
     best.grid = std::max(1, std::min((tiles + 3) / 4, sm_count));
   }
   best.nblocks = batch <= 8 ? 1 : 2;
-  best.smem = se12::gemv_smem_bytes(raw, best.full_tiles != 0, best.x_resident != 0, best.stages, batch, cols);
+  best.smem = se12::gemv_smem_bytes(raw, best.full_tiles != 0, best.x_resident != 0, best.stages, batch, cols,
+                                    best.wide != 0);
   return best;
 }
 
@@ -368,13 +407,14 @@ int se12_gemv_launch_config(const se12_matrix* m, int batch, se12_launch_config*
     return fail(SE12_ERR_INVALID_ARGUMENT, "batch must be in 1.." + std::to_string(SE12_MAX_BATCH));
   const LaunchConfig c = choose_config(false, m->view.tiles, m->view.cols, batch, m->sm_count);
   out->grid = c.grid;
-  out->threads = se12::kGemvThreads;
+  out->threads = se12::gemv_threads(c.wide != 0);
   out->smem_bytes = static_cast<int>(c.smem);
-  out->ctas_per_sm = c.smem <= se12::kCoResidentSmem ? 2 : 1;
+  out->ctas_per_sm = (c.smem <= se12::kCoResidentSmem && !c.wide) ? 2 : 1;
   out->stage_tiles = se12::stage_tiles(c.full_tiles != 0);
   out->stages = c.stages;
   out->x_resident = c.x_resident;
   out->row_mode = c.row_mode;
+  out->wide = c.wide;
   return SE12_OK;
 }
 
@@ -401,6 +441,7 @@ int se12_gemv(const se12_matrix* m, const uint16_t* x, int batch, int ldx, float
   a.x_resident = c.x_resident;
   a.row_mode = c.row_mode;
   a.full_tiles = c.full_tiles;
+  a.wide = c.wide;
   cudaError_t err = se12::launch_gemv(false, m->sm_map, m->ec_map, a, c.nblocks, c.smem,
                                       static_cast<cudaStream_t>(stream), true);
   if (err != cudaSuccess) return cuda_fail(err, "se12_gemv launch");
@@ -464,7 +505,7 @@ int se12_gemv_allreduce(const se12_matrix* m, const uint16_t* x, int batch, int 
   }
   int st = check_gemv_io(m->view.rows, m->view.cols, x, batch, ldx, y, ldy);
   if (st != SE12_OK) return st;
-  const LaunchConfig c = choose_config(false, m->view.tiles, m->view.cols, batch, m->sm_count);
+  const LaunchConfig c = choose_config(false, m->view.tiles, m->view.cols, batch, m->sm_count, false);
   const size_t need = workspace_bytes_for(m->view.tile_rows, m->sm_count);
   if (!workspace || workspace_bytes < need)
     return fail(SE12_ERR_WORKSPACE_TOO_SMALL, "workspace needs " + std::to_string(need) + " bytes");
@@ -482,6 +523,7 @@ int se12_gemv_allreduce(const se12_matrix* m, const uint16_t* x, int batch, int 
   a.x_resident = c.x_resident;
   a.row_mode = c.row_mode;
   a.full_tiles = c.full_tiles;
+  a.wide = c.wide;
   a.peers.world = g->world;
   a.peers.rank = g->rank;
   a.peers.rows_cap = g->rows_cap;
@@ -570,6 +612,7 @@ int se12_gemv_noalloc(const se12_matrix* m, const uint16_t* x, int batch, int ld
   a.x_resident = c.x_resident;
   a.row_mode = c.row_mode;
   a.full_tiles = c.full_tiles;
+  a.wide = c.wide;
   err = se12::launch_gemv(false, m->sm_map, m->ec_map, a, c.nblocks, c.smem, static_cast<cudaStream_t>(stream), false);
   if (err != cudaSuccess) return cuda_fail(err, "se12_gemv_noalloc launch");
   return SE12_OK;
@@ -639,6 +682,7 @@ int bf16_gemv(const uint16_t* w, int rows, int cols, int ldw, const uint16_t* x,
   a.x_resident = c.x_resident;
   a.row_mode = c.row_mode;
   a.full_tiles = c.full_tiles;
+  a.wide = c.wide;
   cudaError_t err = se12::launch_gemv(true, wmap, wmap, a, c.nblocks, c.smem, static_cast<cudaStream_t>(stream), true);
   if (err != cudaSuccess) return cuda_fail(err, "bf16_gemv launch");
   return SE12_OK;

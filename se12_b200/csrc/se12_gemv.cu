@@ -139,14 +139,22 @@ __device__ __forceinline__ T lds_at(const uint8_t* smem, uint32_t offset) {
   return *reinterpret_cast<const T*>(smem + offset);
 }
 
-template <int NB, bool RAW, bool XRES, bool FULL, bool AR>
-__global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_constant__ CUtensorMap map0,
-                                                               const __grid_constant__ CUtensorMap map1,
-                                                               const GemvArgs a) {
+template <int NB, bool RAW, bool XRES, bool FULL, bool AR, bool WIDE>
+__global__ void __launch_bounds__(gemv_threads(WIDE), WIDE ? 1 : 2) gemv_kernel(const __grid_constant__ CUtensorMap map0,
+                                                                                const __grid_constant__ CUtensorMap map1,
+                                                                                const GemvArgs a) {
   static_assert(!(RAW && FULL), "the dense baseline runs 4-tile stages");
+  static_assert(!WIDE || (!RAW && XRES && !FULL && !AR), "the wide layout is SE12 with x resident");
   constexpr int kWeightBytes = stage_weight_bytes(RAW, FULL);
   constexpr int kStage = stage_tiles(FULL);             // tiles per stage
   constexpr int kRecStages = kRecGroupTiles / kStage;   // stages per escape-record slot
+  constexpr bool kTilePerWarp = FULL || WIDE;           // a consumer warp multiplies whole tiles
+  constexpr int kCons = consumer_warps(WIDE);           // consumer warps
+  constexpr int kStageWarps = WIDE ? kStage : kConsumerWarps;  // consumer warps that take each stage
+  constexpr int kProducer = kCons;                      // TMA / bulk copies
+  constexpr int kReducer = kCons + 1;                   // sums the consumers' row partials
+  constexpr int kRS = rec_slots(WIDE);                  // escape-record slots
+  static_assert(!WIDE || kWideGroups >= kRecStages, "a wide-layout warp takes at most one stage of a record group");
   extern __shared__ __align__(1024) uint8_t smem_dynamic[];
   // All dynamic shared memory is addressed as smem_dynamic + 32-bit offset,
   // so every access compiles to a shared-memory instruction with 32-bit
@@ -181,16 +189,16 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
   const uint32_t o_w = pad;                                                            // S x weights
   const uint32_t o_x = o_w + S * kWeightBytes;                                         // x (resident or staged)
   const uint32_t o_red = o_x + (XRES ? B * xrs : S * xstage);                          // [2][8][16][B] floats
-  const uint32_t o_rec = o_red + 2 * kConsumerWarps * 16 * B * 4;                      // escape record slots
-  const uint32_t o_bar = o_rec + (RAW ? 0 : kRecSlots * kRecSlotBytes);
+  const uint32_t o_rec = o_red + 2 * kCons * 16 * B * 4;                               // escape record slots
+  const uint32_t o_bar = o_rec + (RAW ? 0 : kRS * kRecSlotBytes);
   uint64_t* const full = reinterpret_cast<uint64_t*>(sm8 + o_bar);  // [S] stage loaded
   uint64_t* const empty = full + S;                                 // [S] stage consumed
   uint64_t* const xbar = empty + S;                                 // resident x loaded
   uint64_t* const xready = xbar + 1;                                // resident x loaded and its tail zeroed
   uint64_t* const deposited = xready + 1;                           // [2] all warps' row partials written
   uint64_t* const redfree = deposited + 2;                          // [2] row partials summed
-  uint64_t* const rec_full = redfree + 2;                           // [kRecSlots] records loaded
-  uint64_t* const rec_empty = rec_full + kRecSlots;                 // [kRecSlots] records consumed
+  uint64_t* const rec_full = redfree + 2;                           // [kRS] records loaded
+  uint64_t* const rec_empty = rec_full + kRS;                       // [kRS] records consumed
   float* const red = reinterpret_cast<float*>(sm8 + o_red);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -213,17 +221,17 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
     for (int s = 0; s < S; ++s) {
       // resident x: the weights' expect_tx arrival; staged x: + the "x issued" arrival
       mbar_init(&full[s], XRES ? 1 : 2);
-      mbar_init(&empty[s], kConsumerWarps);
+      mbar_init(&empty[s], kStageWarps);
     }
     mbar_init(xbar, 1);
     mbar_init(xready, 1);
     for (int p = 0; p < 2; ++p) {
-      mbar_init(&deposited[p], kConsumerWarps);
+      mbar_init(&deposited[p], kCons);
       mbar_init(&redfree[p], 1);
     }
-    for (int r = 0; r < kRecSlots; ++r) {
+    for (int r = 0; r < kRS; ++r) {
       mbar_init(&rec_full[r], 1);
-      mbar_init(&rec_empty[r], kConsumerWarps);
+      mbar_init(&rec_empty[r], kCons);
     }
     fence_barrier_init();
   }
@@ -246,7 +254,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
   __syncthreads();
   grid_launch_dependents();
 
-  if (warp == kProducerWarp) {
+  if (warp == kProducer) {
     // ------------------------------------------------------------ producer
     const uint64_t pol_w = policy_evict_first();
     const uint64_t pol_x = policy_evict_last();
@@ -327,7 +335,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
       __syncwarp();
     };
     // Escape records of record group r (tiles 16 r .. 16 r + 15 of this
-    // CTA's run): three bulk copies into slot r % kRecSlots. Positions (32 B per
+    // CTA's run): three bulk copies into slot r % kRS. Positions (32 B per
     // tile) and slots (16 B per tile) start 16-byte aligned at any tile; the
     // fallback indices (4 B per tile) are copied from the 4-tile-aligned tile
     // at or before the group (the table is padded to a multiple of 4 tiles).
@@ -336,8 +344,8 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
       if (RAW || r * kRecStages >= nstages) return true;
       bool good = true;
       if (lane == 0) {
-        const int slot = r % kRecSlots;
-        if (r >= kRecSlots) good = mbar_wait_sleep(&rec_empty[slot], static_cast<uint32_t>(r / kRecSlots - 1) & 1u);
+        const int slot = r % kRS;
+        if (r >= kRS) good = mbar_wait_sleep(&rec_empty[slot], static_cast<uint32_t>(r / kRS - 1) & 1u);
         if (good) {
           const int t0 = tstart + r * kRecGroupTiles;
           const int n = min(kRecGroupTiles, tend - t0);
@@ -403,7 +411,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
     return;
   }
 
-  if (warp == kReducerWarp) {
+  if (warp == kReducer) {
     // ------------------------------------------------------------ reducer
     // Tile rows tr_first .. tr_last end in this CTA, in order. For each: wait
     // for the eight consumer warps' partials and sum them in warp order.
@@ -444,7 +452,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
     for (int tr = tr_first; tr <= tr_last; ++tr) {
       const int lr = tr - tr_first, pb = lr & 1;
       if (!mbar_wait(&deposited[pb], static_cast<uint32_t>(lr >> 1) & 1u)) break;
-      const float* buf = red + pb * kConsumerWarps * 16 * B;
+      const float* buf = red + pb * kCons * 16 * B;
       float v[8];
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
@@ -452,7 +460,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
         v[j] = 0.f;
         if (idx < outs) {
 #pragma unroll
-          for (int ww = 0; ww < kConsumerWarps; ++ww) v[j] += buf[ww * 16 * B + idx];
+          for (int ww = 0; ww < kCons; ++ww) v[j] += buf[ww * 16 * B + idx];
         }
       }
       __syncwarp();
@@ -568,9 +576,10 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
   // -------------------------------------------------------------- consumers
   // 8-tile stages (FULL): warp w decodes tile w of every stage, its two
   // 128-column halves in turn. 4-tile stages: warp w takes half w % 2 of
-  // tile w / 2.
-  const int jw = FULL ? warp : (warp >> 1);  // tile of the stage this warp multiplies
-  const int hw = FULL ? 0 : (warp & 1);      // its (first) half
+  // tile w / 2. Wide layout: warp w decodes tile w % 4 of the stages of its
+  // group w / 4, both halves in turn.
+  const int jw = FULL ? warp : (WIDE ? (warp & 3) : (warp >> 1));  // tile of the stage this warp multiplies
+  const int hw = kTilePerWarp ? 0 : (warp & 1);                     // its (first) half
   const int g = lane >> 2, t = lane & 3;
   // decode table of the current tile's segment (seg_tab[cur_seg]), loaded
   // when a tile of another segment comes up
@@ -585,7 +594,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
   // the column groups 32 k + 8 t .. + 7 for k = 0..3. Row g + 8 lies a
   // constant distance after row g; the group offset is a compile-time value
   // XOR a per-thread swizzle term, so four registers hold the layout (with
-  // FULL, half 1 lies a lane-dependent distance after half 0, recomputed
+  // whole tiles, half 1 lies a lane-dependent distance after half 0, recomputed
   // where it is used).
   uint32_t w_base, w_xor, e_base, e_xor;
   if (RAW) {
@@ -607,7 +616,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
     e_xor = (R0 & 3) << 4;                  // group k: + ((16 k) ^ e_xor)
   }
   // x of batch row g + 8 nb at column 128 hw + 8 t (+ 32 k, + 128 for half
-  // 1 with FULL) of a tile
+  // 1 with whole tiles) of a tile
   const uint32_t x_thread = XRES ? o_x + static_cast<uint32_t>(g) * xrs + (128 * hw + 8 * t) * 2
                                  : o_x + (jw * B + g) * kXRowStride + (128 * hw + 8 * t) * 2;
   const uint32_t x_nb_step = XRES ? 8 * xrs : 8 * kXRowStride;
@@ -626,7 +635,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
   uint32_t frag0[4][4], frag1[4][4];
 
   // Fills frag0 / frag1 with half hw + h of this warp's tile of stage s (h =
-  // 1 only with FULL): decoded SE12 weights, the raw bits of a fallback tile
+  // 1 only with whole tiles): decoded SE12 weights, the raw bits of a fallback tile
   // (fbi >= 0), or dense BF16 weights. Needs no x, so it may run before the
   // dependency wait.
   auto load_frags = [&](int s, int kt, int fbi, int h) {
@@ -741,8 +750,8 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
   // already).
   auto fix_escapes = [&](int s, int kt, uint32_t rec) {
     const uint32_t wst = o_w + s * kWeightBytes;
-    // FULL: all of the tile's escapes; else those in this warp's half
-    const bool mine = rec > 0xFFFFu && (FULL || ((rec >> 7) & 1u) == static_cast<uint32_t>(hw));
+    // whole tiles: all of the tile's escapes; else those in this warp's half
+    const bool mine = rec > 0xFFFFu && (kTilePerWarp || ((rec >> 7) & 1u) == static_cast<uint32_t>(hw));
     unsigned pending = __ballot_sync(0xFFFFFFFFu, mine);
     while (pending) {
       const int e = __ffs(pending) - 1;
@@ -783,7 +792,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
     const uint32_t use = static_cast<uint32_t>(lr >> 1) & 1u;
     if (ok && !mbar_wait(&redfree[pb], use ^ 1u)) ok = false;
     if (ok) {
-      float* rw = red + (pb * kConsumerWarps + warp) * 16 * B;
+      float* rw = red + (pb * kCons + warp) * 16 * B;
 #pragma unroll
       for (int nb = 0; nb < NB; ++nb) {
         const int b0 = nb * 8 + 2 * t;
@@ -805,142 +814,255 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
       for (int nb = 0; nb < NB; ++nb) acc[h][nb][0] = acc[h][nb][1] = acc[h][nb][2] = acc[h][nb][3] = 0.f;
   };
 
-  int s = 0;                 // stage slot of stage i, i % S
-  uint32_t ph = 0u;          // parity of its full-barrier phase, (i / S) & 1
-  int rq = 0, rslot = 0;     // stage within its record group, the group's slot
-  uint32_t rph = 0u;         // parity of the record slot's phase
-  int tile0 = tstart;
-  int tr0 = tile0 / KT, kt0 = tile0 - tr0 * KT;  // row and column of the stage's first tile
   const int fb_shift = tstart & 3;  // the fallback indices of a record slot start at its 4-aligned tile
-  // The current stage's tile count, this warp's tile column and records.
-  int ntl = 0, kt_mine = 0, fbi = -1;
-  uint32_t esc_rec = 0u;  // this lane's escape record (fix_escapes)
 
-  // Waits for stage i's records and weights; with `predecode`, decodes this
-  // warp's tile of it (its first half, with 8-tile stages) into frag0 / frag1.
-  auto fetch_stage = [&](bool predecode) {
-    ntl = min(kStage, tend - tile0);
-    fbi = -1;
-    esc_rec = 0u;
-    if (!RAW) {
-      if (rq == 0 && ok) ok = mbar_wait(&rec_full[rslot], rph);
-      if (jw < ntl) {
-        const uint32_t rb = o_rec + rslot * kRecSlotBytes;
-        const int lt = rq * kStage + jw;
-        fbi = lds_at<int>(sm8, rb + kRecFbOffset + (lt + fb_shift) * 4);
-        if (lane < kEscapeBudget) {
-          const uint32_t pos = lds_at<uint16_t>(sm8, rb + kRecPosOffset + lt * 32 + lane * 2);
-          const uint32_t ex = lds_at<uint8_t>(sm8, rb + kRecEscOffset + lt * 16 + lane);
-          if (pos != kNoEscape) esc_rec = pos | (ex << 16);
-        }
-      }
-    }
-    if (ok) ok = mbar_wait(&full[s], ph);
-    kt_mine = kt0 + jw;
-    int tr_mine = tr0;
-    while (kt_mine >= KT) {
-      kt_mine -= KT;
-      ++tr_mine;
-    }
-    if (!RAW) {
-      const int seg = segment_of(a.m, tr_mine);
-      if (seg != cur_seg) {
-        const uint4 v = seg_tab[seg];
-        tab[0] = v.x;
-        tab[1] = v.y;
-        tab[2] = v.z;
-        tab[3] = v.w;
-        pad_inf = (K & (kTileCols - 1)) && (v.x & 0xFFu) == 0xFFu;
-        cur_seg = seg;
-      }
-    }
-    if (predecode && jw < ntl && ok) load_frags(s, kt_mine, fbi, 0);
-  };
-
-  // The weights do not depend on the previous kernel in the stream: decode
-  // this warp's first tile while that kernel finishes, then wait for it
-  // (griddepcontrol.wait) before touching x, y or the workspace.
-  // (8-tile stages do not: fragments live across the loop would cost the
-  // per-group decode its registers; measured slower)
-  constexpr bool kPredecodeFirst = !FULL;
-  if (nstages > 0) fetch_stage(kPredecodeFirst);
-  grid_dependency_wait();
-  if (XRES && !mbar_wait((K & 7) ? xready : xbar, 0)) ok = false;
-
-  for (int i = 0; i < nstages; ++i) {
-    // Tile rows end at stage positions pe, pe + KT, ... (column KT - 1);
-    // the CTA's last tile (position ntl - 1 of its last stage) ends its
-    // last row. This warp finishes the rows that end before its tile jw,
-    // multiplies tile jw, then finishes the rows that end at or after it,
-    // in the order of the tile sequence.
-    {
-      int pe = KT - 1 - kt0;  // first row end in this stage
-      int tr = tr0;
-      while (pe < jw && pe < ntl) {
-        finish_row(tr);
-        ++tr;
-        pe += KT;
-      }
-      if (jw < ntl && ok) {
-        if (FULL) {
-          // half 0 was decoded by fetch_stage for the first stage
-          const bool plain = fbi < 0 && !pad_inf;
-          // The two halves run as a loop, not unrolled: one copy of the
-          // decode in the instruction cache. The escape products come
-          // after half 0, so that their record is dead during half 1.
-          if (plain) {
-#pragma unroll 1
-            for (int h = 0; h < 2; ++h) {
-              decode_mma(s, kt_mine, h);
-              if (h == 0) fix_escapes(s, kt_mine, esc_rec);
-            }
-          } else {
-#pragma unroll 1
-            for (int h = 0; h < 2; ++h) {
-              if (!(kPredecodeFirst && i == 0 && h == 0)) load_frags(s, kt_mine, fbi, h);
-              mma_tile(s, kt_mine, h);
-              if (h == 0 && fbi < 0) fix_escapes(s, kt_mine, esc_rec);
-            }
-          }
-        } else {
-          mma_tile(s, kt_mine, 0);
-          if (!RAW && fbi < 0) fix_escapes(s, kt_mine, esc_rec);
-        }
-      }
-      while (pe < ntl) {
-        finish_row(tr);
-        ++tr;
-        pe += KT;
-      }
-      // pe is now the first row end past the stage: the stage's last tile
-      // ended a row iff pe - KT == ntl - 1
-      if (i == nstages - 1 && pe - KT != ntl - 1) finish_row(tr);
-    }
-    __syncwarp();
-    if (lane == 0) {
-      mbar_arrive(&empty[s]);
-      if (!RAW && (rq == kRecStages - 1 || i == nstages - 1)) mbar_arrive(&rec_empty[rslot]);
-    }
-    if (++s == S) {
-      s = 0;
-      ph ^= 1u;
-    }
-    if (++rq == kRecStages) {
-      rq = 0;
-      if (++rslot == kRecSlots) {
+  if constexpr (WIDE) {
+    // Group c = warp / 4 takes stages c, c + kWideGroups, c + 2 kWideGroups,
+    // ...; warp w multiplies tile w % 4 of each. Before each of its tiles a
+    // warp deposits its partials of the rows that end before the tile
+    // (zeros for rows it has no tile in), then settles the escape-record
+    // groups in order: it waits for each and arrives on its empty barrier
+    // once, the groups whose stages it skips included (a warp takes at most
+    // one stage of a group). Rows come first, so that no warp waits for
+    // records or weights while another needs its partial. A stage's slot is
+    // released by the group's 4 warps once its data has landed.
+    constexpr int kG = kWideGroups;
+    const int grp = warp >> 2;
+    const int tr_end = (tend > tstart) ? (tend - 1) / KT : tr_first - 1;
+    const int ngroups = (nstages + kRecStages - 1) / kRecStages;
+    int row_next = tr_first;  // the next row this warp deposits
+    int rg = 0, rslot = 0;    // the next record group this warp settles, its slot
+    uint32_t rph = 0u;        // parity of that slot's phase
+    auto next_group = [&]() {
+      ++rg;
+      if (++rslot == kRS) {
         rslot = 0;
         rph ^= 1u;
       }
+    };
+    auto settle_records = [&](int upto) {
+      while (rg < upto) {
+        if (ok) ok = mbar_wait(&rec_full[rslot], rph);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&rec_empty[rslot]);
+        next_group();
+      }
+    };
+    grid_dependency_wait();
+    if (!mbar_wait((K & 7) ? xready : xbar, 0)) ok = false;
+    int s = grp;  // stage slot, i % S (S > kG)
+    uint32_t ph = 0u;
+    int tile0 = tstart + grp * kStage;
+    int tr0 = tile0 / KT, kt0 = tile0 - tr0 * KT;
+    for (int i = grp; i < nstages; i += kG) {
+      const bool have = jw < min(kStage, tend - tile0);
+      int kt_w = kt0 + jw, tr_w = tr0;
+      while (kt_w >= KT) {
+        kt_w -= KT;
+        ++tr_w;
+      }
+      if (have)
+        while (row_next < tr_w) finish_row(row_next++);
+      const int R = i / kRecStages;
+      settle_records(R);
+      if (ok) ok = mbar_wait(&rec_full[rslot], rph);
+      int fbi_w = -1;
+      uint32_t rec_w = 0u;
+      if (have) {
+        const uint32_t rb = o_rec + rslot * kRecSlotBytes;
+        const int lt = (i - R * kRecStages) * kStage + jw;
+        fbi_w = lds_at<int>(sm8, rb + kRecFbOffset + (lt + fb_shift) * 4);
+        if (lane < kEscapeBudget) {
+          const uint32_t pos = lds_at<uint16_t>(sm8, rb + kRecPosOffset + lt * 32 + lane * 2);
+          const uint32_t ex = lds_at<uint8_t>(sm8, rb + kRecEscOffset + lt * 16 + lane);
+          if (pos != kNoEscape) rec_w = pos | (ex << 16);
+        }
+        const int seg = segment_of(a.m, tr_w);
+        if (seg != cur_seg) {
+          const uint4 v = seg_tab[seg];
+          tab[0] = v.x;
+          tab[1] = v.y;
+          tab[2] = v.z;
+          tab[3] = v.w;
+          pad_inf = (K & (kTileCols - 1)) && (v.x & 0xFFu) == 0xFFu;
+          cur_seg = seg;
+        }
+      }
+      if (ok) ok = mbar_wait(&full[s], ph);
+      if (have && ok) {
+        if (fbi_w < 0 && !pad_inf) {
+#pragma unroll 1
+          for (int h = 0; h < 2; ++h) {
+            decode_mma(s, kt_w, h);
+            if (h == 0) fix_escapes(s, kt_w, rec_w);
+          }
+        } else {
+#pragma unroll 1
+          for (int h = 0; h < 2; ++h) {
+            load_frags(s, kt_w, fbi_w, h);
+            mma_tile(s, kt_w, h);
+            if (h == 0 && fbi_w < 0) fix_escapes(s, kt_w, rec_w);
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&empty[s]);
+        mbar_arrive(&rec_empty[rslot]);
+      }
+      next_group();
+      s += kG;
+      if (s >= S) {
+        s -= S;
+        ph ^= 1u;
+      }
+      tile0 += kG * kStage;
+      kt0 += kG * kStage;
+      while (kt0 >= KT) {
+        kt0 -= KT;
+        ++tr0;
+      }
     }
-    tile0 += kStage;
-    kt0 += kStage;
-    while (kt0 >= KT) {
-      kt0 -= KT;
-      ++tr0;
+    while (row_next <= tr_end) finish_row(row_next++);
+    settle_records(ngroups);
+  } else {
+    int s = 0;                 // stage slot of stage i, i % S
+    uint32_t ph = 0u;          // parity of its full-barrier phase, (i / S) & 1
+    int rq = 0, rslot = 0;     // stage within its record group, the group's slot
+    uint32_t rph = 0u;         // parity of the record slot's phase
+    int tile0 = tstart;
+    int tr0 = tile0 / KT, kt0 = tile0 - tr0 * KT;  // row and column of the stage's first tile
+    // The current stage's tile count, this warp's tile column and records.
+    int ntl = 0, kt_mine = 0, fbi = -1;
+    uint32_t esc_rec = 0u;  // this lane's escape record (fix_escapes)
+
+    // Waits for stage i's records and weights; with `predecode`, decodes this
+    // warp's tile of it (its first half, with 8-tile stages) into frag0 / frag1.
+    auto fetch_stage = [&](bool predecode) {
+      ntl = min(kStage, tend - tile0);
+      fbi = -1;
+      esc_rec = 0u;
+      if (!RAW) {
+        if (rq == 0 && ok) ok = mbar_wait(&rec_full[rslot], rph);
+        if (jw < ntl) {
+          const uint32_t rb = o_rec + rslot * kRecSlotBytes;
+          const int lt = rq * kStage + jw;
+          fbi = lds_at<int>(sm8, rb + kRecFbOffset + (lt + fb_shift) * 4);
+          if (lane < kEscapeBudget) {
+            const uint32_t pos = lds_at<uint16_t>(sm8, rb + kRecPosOffset + lt * 32 + lane * 2);
+            const uint32_t ex = lds_at<uint8_t>(sm8, rb + kRecEscOffset + lt * 16 + lane);
+            if (pos != kNoEscape) esc_rec = pos | (ex << 16);
+          }
+        }
+      }
+      if (ok) ok = mbar_wait(&full[s], ph);
+      kt_mine = kt0 + jw;
+      int tr_mine = tr0;
+      while (kt_mine >= KT) {
+        kt_mine -= KT;
+        ++tr_mine;
+      }
+      if (!RAW) {
+        const int seg = segment_of(a.m, tr_mine);
+        if (seg != cur_seg) {
+          const uint4 v = seg_tab[seg];
+          tab[0] = v.x;
+          tab[1] = v.y;
+          tab[2] = v.z;
+          tab[3] = v.w;
+          pad_inf = (K & (kTileCols - 1)) && (v.x & 0xFFu) == 0xFFu;
+          cur_seg = seg;
+        }
+      }
+      if (predecode && jw < ntl && ok) load_frags(s, kt_mine, fbi, 0);
+    };
+
+    // The weights do not depend on the previous kernel in the stream: decode
+    // this warp's first tile while that kernel finishes, then wait for it
+    // (griddepcontrol.wait) before touching x, y or the workspace.
+    // (8-tile stages do not: fragments live across the loop would cost the
+    // per-group decode its registers; measured slower)
+    constexpr bool kPredecodeFirst = !FULL;
+    if (nstages > 0) fetch_stage(kPredecodeFirst);
+    grid_dependency_wait();
+    if (XRES && !mbar_wait((K & 7) ? xready : xbar, 0)) ok = false;
+
+    for (int i = 0; i < nstages; ++i) {
+      // Tile rows end at stage positions pe, pe + KT, ... (column KT - 1);
+      // the CTA's last tile (position ntl - 1 of its last stage) ends its
+      // last row. This warp finishes the rows that end before its tile jw,
+      // multiplies tile jw, then finishes the rows that end at or after it,
+      // in the order of the tile sequence.
+      {
+        int pe = KT - 1 - kt0;  // first row end in this stage
+        int tr = tr0;
+        while (pe < jw && pe < ntl) {
+          finish_row(tr);
+          ++tr;
+          pe += KT;
+        }
+        if (jw < ntl && ok) {
+          if (FULL) {
+            // half 0 was decoded by fetch_stage for the first stage
+            const bool plain = fbi < 0 && !pad_inf;
+            // The two halves run as a loop, not unrolled: one copy of the
+            // decode in the instruction cache. The escape products come
+            // after half 0, so that their record is dead during half 1.
+            if (plain) {
+  #pragma unroll 1
+              for (int h = 0; h < 2; ++h) {
+                decode_mma(s, kt_mine, h);
+                if (h == 0) fix_escapes(s, kt_mine, esc_rec);
+              }
+            } else {
+  #pragma unroll 1
+              for (int h = 0; h < 2; ++h) {
+                if (!(kPredecodeFirst && i == 0 && h == 0)) load_frags(s, kt_mine, fbi, h);
+                mma_tile(s, kt_mine, h);
+                if (h == 0 && fbi < 0) fix_escapes(s, kt_mine, esc_rec);
+              }
+            }
+          } else {
+            mma_tile(s, kt_mine, 0);
+            if (!RAW && fbi < 0) fix_escapes(s, kt_mine, esc_rec);
+          }
+        }
+        while (pe < ntl) {
+          finish_row(tr);
+          ++tr;
+          pe += KT;
+        }
+        // pe is now the first row end past the stage: the stage's last tile
+        // ended a row iff pe - KT == ntl - 1
+        if (i == nstages - 1 && pe - KT != ntl - 1) finish_row(tr);
+      }
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&empty[s]);
+        if (!RAW && (rq == kRecStages - 1 || i == nstages - 1)) mbar_arrive(&rec_empty[rslot]);
+      }
+      if (++s == S) {
+        s = 0;
+        ph ^= 1u;
+      }
+      if (++rq == kRecStages) {
+        rq = 0;
+        if (++rslot == kRS) {
+          rslot = 0;
+          rph ^= 1u;
+        }
+      }
+      tile0 += kStage;
+      kt0 += kStage;
+      while (kt0 >= KT) {
+        kt0 -= KT;
+        ++tr0;
+      }
+      // 8-tile stages decode in decode_mma (group by group) from the second
+      // stage on; 4-tile stages decode here, ahead of the stage's row ends
+      if (i + 1 < nstages) fetch_stage(!FULL);
     }
-    // 8-tile stages decode in decode_mma (group by group) from the second
-    // stage on; 4-tile stages decode here, ahead of the stage's row ends
-    if (i + 1 < nstages) fetch_stage(!FULL);
+
   }
 }
 
@@ -950,29 +1072,35 @@ cudaError_t launch_gemv(bool raw, const CUtensorMap& map0, const CUtensorMap& ma
   // [batch blocks][kind: SE12 4-tile, SE12 8-tile, dense][x resident];
   // 8-tile stages always hold x resident
   static const Kernel table[2][3][2] = {
-      {{gemv_kernel<1, false, false, false, false>, gemv_kernel<1, false, true, false, false>},
-       {nullptr, gemv_kernel<1, false, true, true, false>},
-       {gemv_kernel<1, true, false, false, false>, gemv_kernel<1, true, true, false, false>}},
-      {{gemv_kernel<2, false, false, false, false>, gemv_kernel<2, false, true, false, false>},
-       {nullptr, gemv_kernel<2, false, true, true, false>},
-       {gemv_kernel<2, true, false, false, false>, gemv_kernel<2, true, true, false, false>}}};
+      {{gemv_kernel<1, false, false, false, false, false>, gemv_kernel<1, false, true, false, false, false>},
+       {nullptr, gemv_kernel<1, false, true, true, false, false>},
+       {gemv_kernel<1, true, false, false, false, false>, gemv_kernel<1, true, true, false, false, false>}},
+      {{gemv_kernel<2, false, false, false, false, false>, gemv_kernel<2, false, true, false, false, false>},
+       {nullptr, gemv_kernel<2, false, true, true, false, false>},
+       {gemv_kernel<2, true, false, false, false, false>, gemv_kernel<2, true, true, false, false, false>}}};
   // with the peer all-reduce (SE12 only): [batch blocks][4-tile, 8-tile][x resident]
   static const Kernel table_ar[2][2][2] = {
-      {{gemv_kernel<1, false, false, false, true>, gemv_kernel<1, false, true, false, true>},
-       {nullptr, gemv_kernel<1, false, true, true, true>}},
-      {{gemv_kernel<2, false, false, false, true>, gemv_kernel<2, false, true, false, true>},
-       {nullptr, gemv_kernel<2, false, true, true, true>}}};
+      {{gemv_kernel<1, false, false, false, true, false>, gemv_kernel<1, false, true, false, true, false>},
+       {nullptr, gemv_kernel<1, false, true, true, true, false>}},
+      {{gemv_kernel<2, false, false, false, true, false>, gemv_kernel<2, false, true, false, true, false>},
+       {nullptr, gemv_kernel<2, false, true, true, true, false>}}};
+  // the wide layout (SE12, x resident, no all-reduce, batch <= 8: at 80
+  // registers the two-block accumulators spill)
+  static const Kernel table_wide[2] = {gemv_kernel<1, false, true, false, false, true>, nullptr};
   const int kind = raw ? 2 : (a.full_tiles ? 1 : 0);
   const int blocks = nblocks == 1 ? 0 : 1;
   const bool ar = a.peers.world > 1;
   if (ar && raw) return cudaErrorInvalidValue;
-  const Kernel kernel = ar ? table_ar[blocks][kind][a.x_resident ? 1 : 0] : table[blocks][kind][a.x_resident ? 1 : 0];
+  if (a.wide && (raw || ar || a.full_tiles || !a.x_resident || a.stages <= kWideGroups)) return cudaErrorInvalidValue;
+  const Kernel kernel = a.wide ? table_wide[blocks]
+                        : ar   ? table_ar[blocks][kind][a.x_resident ? 1 : 0]
+                               : table[blocks][kind][a.x_resident ? 1 : 0];
   if (!kernel) return cudaErrorInvalidValue;
   cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (err != cudaSuccess) return err;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.grid);
-  cfg.blockDim = dim3(kGemvThreads);
+  cfg.blockDim = dim3(gemv_threads(a.wide != 0));
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];

@@ -71,6 +71,7 @@ struct GemvArgs {
   int x_resident;      // 1: all of x in shared memory; 0: x staged per stage
   int row_mode;        // 1: each CTA owns whole tile rows; 0: stream-K over stages
   int full_tiles;      // SE12: 1 = 8-tile stages, a warp per tile; 0 = 4-tile stages, a warp per half tile
+  int wide;            // SE12, x resident: 1 = one CTA per SM, kWideGroups groups of 4 warps taking 4-tile stages in turn
   PeerArgs peers;      // world == 1: plain GEMV
 };
 
@@ -78,7 +79,12 @@ struct GemvArgs {
 // of the linear tile sequence, either
 //   4 tiles, consumer warp w taking half w % 2 (128 columns) of tile w / 2, or
 //   8 tiles, consumer warp w taking tile w, its two halves in turn (SE12
-//   only: half the per-stage overhead per weight, twice the staged x).
+//   only: half the per-stage overhead per weight, twice the staged x), or
+//   4 tiles in the wide layout (SE12 with x resident, one CTA per SM):
+//   kWideGroups groups of 4 consumer warps take the stages in turn (group
+//   c the stages i with i % kWideGroups == c), warp w taking tile w % 4.
+//   22 warps leave 80 registers a thread, with 5 consumer warps per SM
+//   sub-partition instead of 4.
 // SE12 weights arrive as 3-D TMA boxes [64 rows][2 halves][128 B] of sm
 // (16 KB) and 2-D boxes [64 rows][128 B] of ec (8 KB), both with the 128-byte
 // swizzle: one of each per 4 tiles, the ec boxes after the stage's sm boxes.
@@ -96,12 +102,18 @@ constexpr int kConsumerWarps = 8;
 constexpr int kProducerWarp = kConsumerWarps;      // TMA / bulk copies
 constexpr int kReducerWarp = kConsumerWarps + 1;   // sums the consumers' row partials
 constexpr int kGemvThreads = (kConsumerWarps + 2) * 32;
+constexpr int kWideGroups = 5;
+__host__ __device__ constexpr int consumer_warps(bool wide) { return wide ? kWideGroups * 4 : kConsumerWarps; }
+__host__ __device__ constexpr int gemv_threads(bool wide) { return (consumer_warps(wide) + 2) * 32; }
 // Escape records (escape positions, escape slots, fallback indices) of
 // kRecGroupTiles consecutive tiles (two SE12 stages) are copied into shared
 // memory together, into one of kRecSlots slots: [16 tiles][16] u16
 // positions, [16][16] u8 slots, [16 + 4] i32 fallback indices.
 constexpr int kRecGroupTiles = 16;
 constexpr int kRecSlots = 3;
+// The wide layout keeps more stages in flight (its record groups are 4
+// stages, up to 3 of them live at once, plus the one issued ahead).
+__host__ __device__ constexpr int rec_slots(bool wide) { return wide ? 4 : kRecSlots; }
 constexpr int kRecPosOffset = 0;
 constexpr int kRecEscOffset = kRecGroupTiles * 32;
 constexpr int kRecFbOffset = kRecEscOffset + kRecGroupTiles * 16;
@@ -119,13 +131,15 @@ inline size_t x_stage_bytes(bool full_tiles, int batch) {
   return ((size_t)stage_tiles(full_tiles) * batch * kXRowStride + 127) / 128 * 128;
 }
 
-inline size_t gemv_smem_bytes(bool raw, bool full_tiles, bool x_resident, int stages, int batch, int cols) {
+// (wide: the wide layout, whose stages are 4 tiles: full_tiles must be false)
+inline size_t gemv_smem_bytes(bool raw, bool full_tiles, bool x_resident, int stages, int batch, int cols,
+                              bool wide = false) {
   size_t per_stage = stage_weight_bytes(raw, full_tiles) + (x_resident ? 0 : x_stage_bytes(full_tiles, batch));
   size_t bytes = 1024;                                                  // alignment slack
   bytes += (size_t)stages * per_stage;
   if (x_resident) bytes += (size_t)batch * x_resident_stride(cols);
-  bytes += 2 * (size_t)kConsumerWarps * 16 * batch * 4;                // two row-reduction buffers
-  if (!raw) bytes += (size_t)kRecSlots * kRecSlotBytes;                 // escape records
+  bytes += 2 * (size_t)consumer_warps(wide) * 16 * batch * 4;          // two row-reduction buffers
+  if (!raw) bytes += (size_t)rec_slots(wide) * kRecSlotBytes;           // escape records
   bytes += (size_t)stages * 16 + 128;                                   // barriers
   return bytes;
 }

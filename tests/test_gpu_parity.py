@@ -196,21 +196,29 @@ def test_fused_gemv_matches_fp64_oracle(kind, rows, cols, batch):
 def test_launch_table_reaches_every_configuration():
     """The parity shapes above run every kernel configuration: 4-tile stages
     with x resident or staged, 8-tile stages (x always resident), each in row
-    mode and stream-K, and 8-tile stages with a pipeline deeper than 2."""
+    mode and stream-K, 8-tile stages with a pipeline deeper than 2, and the
+    wide layout (one CTA per SM, x resident, 4-tile stages taken in turn by
+    its warp groups; row mode only)."""
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
     seen, deep = set(), False
     for kind, rows, cols in GEMV_SHAPES:
         m = gemv_fixture(kind, rows, cols)[2]
         for batch in (1, 2, 4, 8, 16):
             c = m.launch_config(batch)
-            assert c["threads"] == 320 and 1 <= c["grid"] <= 2 * torch.cuda.get_device_properties(0).multi_processor_count
-            seen.add((c["stage_tiles"], c["x_resident"], c["row_mode"]))
+            if c["wide"]:
+                assert c["threads"] == 704 and c["stage_tiles"] == 4 and c["x_resident"] == 1 and c["stages"] >= 7
+                assert c["ctas_per_sm"] == 1 and 1 <= c["grid"] <= sms and batch <= 8 and c["row_mode"] == 1
+            else:
+                assert c["threads"] == 320 and 1 <= c["grid"] <= 2 * sms
+            layout = "wide" if c["wide"] else c["stage_tiles"]
+            seen.add((layout, c["x_resident"], c["row_mode"]))
             deep = deep or (c["stage_tiles"] == 8 and c["stages"] > 2)
-    if torch.cuda.get_device_properties(0).multi_processor_count != 148:
+    if sms != 148:
         pytest.skip("the shapes are chosen for 148 SMs")
-    assert all(x == 1 for t, x, _ in seen if t == 8), "8-tile stages with staged x"
-    missing = {(4, x, r) for x in (0, 1) for r in (0, 1)} | {(8, 1, r) for r in (0, 1)}
+    assert all(x == 1 for t, x, _ in seen if t in (8, "wide")), "8-tile stages or the wide layout with staged x"
+    missing = {(4, x, r) for x in (0, 1) for r in (0, 1)} | {(8, 1, r) for r in (0, 1)} | {("wide", 1, 1)}
     missing -= seen
-    assert not missing, f"configurations no parity shape reaches: {sorted(missing)}"
+    assert not missing, f"configurations no parity shape reaches: {sorted(missing, key=str)}"
     assert deep
 
 
