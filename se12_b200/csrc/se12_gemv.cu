@@ -888,6 +888,14 @@ __global__ void __launch_bounds__(gemv_threads(WIDE), WIDE ? 1 : 2) gemv_kernel(
           cur_seg = seg;
         }
       }
+      // The groups take the stages in turn, so this group never waited on
+      // stage i - S of its slot, and a parity wait for stage i would pass on
+      // that stage's phase if it had not landed yet. First wait (by parity)
+      // until stage i - S is consumed: that phase's predecessor, stage
+      // i - 2S, is consumed already (stage i - S was issued, as stage i - 5
+      // was, in order), and stage i is not, so the parity tells. Then stage
+      // i - S has landed, and the wait for stage i is exact too.
+      if (ok && i >= S) ok = mbar_wait(&empty[s], ph ^ 1u);
       if (ok) ok = mbar_wait(&full[s], ph);
       if (have && ok) {
         if (fbi_w < 0 && !pad_inf) {

@@ -103,6 +103,7 @@ constexpr int kProducerWarp = kConsumerWarps;      // TMA / bulk copies
 constexpr int kReducerWarp = kConsumerWarps + 1;   // sums the consumers' row partials
 constexpr int kGemvThreads = (kConsumerWarps + 2) * 32;
 constexpr int kWideGroups = 5;
+constexpr int kMaxWideStages = kWideGroups + 4;  // the deepest wide pipeline the launch table picks
 __host__ __device__ constexpr int consumer_warps(bool wide) { return wide ? kWideGroups * 4 : kConsumerWarps; }
 __host__ __device__ constexpr int gemv_threads(bool wide) { return (consumer_warps(wide) + 2) * 32; }
 // Escape records (escape positions, escape slots, fallback indices) of
