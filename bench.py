@@ -332,9 +332,10 @@ def build_stack(torch, shapes, batch, device, layers, lm_head, keep_dense, seed_
     return mats, dense
 
 
-def time_stack(torch, stack, steps, warmup, device, sampler=None, eager=False):
+def time_stack(torch, stack, steps, warmup, device, sampler=None, eager=False, per_step=None):
     """Device time of `steps` steps (one graph replay each; with `eager`, the
-    same launches issued one by one on the current stream)."""
+    same launches issued one by one on the current stream). With a list as
+    `per_step`, an event after every step appends each step's own time (ms)."""
     if eager:
         run = stack.run
     else:
@@ -345,14 +346,32 @@ def time_stack(torch, stack, steps, warmup, device, sampler=None, eager=False):
     torch.cuda.synchronize()
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
+    marks = [torch.cuda.Event(enable_timing=True) for _ in range(steps - 1)] if per_step is not None else []
     ctx = sampler if sampler is not None else _Null()
     with ctx:
         start.record()
-        for _ in range(steps):
+        for i in range(steps):
             run()
+            if i < len(marks):
+                marks[i].record()
         end.record()
         torch.cuda.synchronize()
+    if per_step is not None:
+        bounds = [start] + marks + [end]
+        per_step.extend(a.elapsed_time(b) for a, b in zip(bounds, bounds[1:]))
     return start.elapsed_time(end)  # ms over `steps`
+
+
+def step_percentiles(times):
+    """p10 / median / p90 of this rank's per-step device times (ms)."""
+    if not times:
+        return None
+    ordered = sorted(times)
+
+    def at(q):
+        return ordered[min(len(ordered) - 1, int(q * (len(ordered) - 1) + 0.5))]
+
+    return {"p10": at(0.1), "median": at(0.5), "p90": at(0.9), "steps": len(ordered), "rank": "0"}
 
 
 class _Null:
@@ -427,7 +446,8 @@ def run_ours(args) -> None:
     if world > 1:
         torch.distributed.barrier()
     torch.cuda.synchronize()
-    elapsed_ms = time_stack(torch, stack, args.steps, args.warmup, device, sampler, eager=args.eager)
+    step_times = []
+    elapsed_ms = time_stack(torch, stack, args.steps, args.warmup, device, sampler, eager=args.eager, per_step=step_times)
     if world > 1:
         torch.distributed.barrier()
         t = torch.tensor([elapsed_ms], device=device, dtype=torch.float64)
@@ -594,6 +614,7 @@ def run_ours(args) -> None:
                     "ms_per_step": e2e_s * 1e3, "api": "se12_b200.stack.GemvStack " + ("eager launches" if args.eager else "graph replay")
                     + ", pinned H2D inputs, D2H logits, sync per step"},
             "gpu_launches": launches * args.steps,
+            "step_ms": step_percentiles(step_times),
             "clocks": sampler.summary(),
             "other_batches": extra,
             "dense": dense_info,
