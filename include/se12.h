@@ -138,6 +138,11 @@ typedef struct se12_launch_config {
 
 int se12_gemv_launch_config(const se12_matrix* m, int batch, se12_launch_config* out);
 
+/* The same answer from the shape alone, for a device of sm_count SMs
+ * (host only: no GPU, no matrix; what se12_gemv_launch_config returns for
+ * a matrix of rows x cols on such a device). */
+int se12_gemv_plan(int rows, int cols, int batch, int sm_count, se12_launch_config* out);
+
 /*
  * Fused decode + GEMV:  y[b, n] = sum_k W[n, k] * x[b, k],  fp32 accumulate,
  * fp32 output. x: device BF16 [batch, ldx], y: device fp32 [batch, ldy].

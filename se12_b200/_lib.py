@@ -74,6 +74,7 @@ SIGNATURES = {
     "se12_gemv_workspace_bytes": (c_size_t, [c_void_p, c_int]),
     "se12_workspace_clear": (c_int, [c_void_p, c_size_t, c_void_p]),
     "se12_gemv_launch_config": (c_int, [c_void_p, c_int, ctypes.POINTER(Se12LaunchConfigStruct)]),
+    "se12_gemv_plan": (c_int, [c_int, c_int, c_int, c_int, ctypes.POINTER(Se12LaunchConfigStruct)]),
     "se12_gemv": (c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p, c_int, c_void_p, c_size_t, c_void_p]),
     "se12_gemv_noalloc": (c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p, c_int, c_void_p]),
     "se12_ipc_handle": (c_int, [c_void_p, ctypes.POINTER(ctypes.c_uint8), ctypes.POINTER(ctypes.c_uint64)]),

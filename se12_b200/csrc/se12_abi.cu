@@ -401,11 +401,7 @@ static int check_gemv_io(int rows, int cols, const uint16_t* x, int batch, int l
   return SE12_OK;
 }
 
-int se12_gemv_launch_config(const se12_matrix* m, int batch, se12_launch_config* out) {
-  if (!m || !out) return fail(SE12_ERR_INVALID_ARGUMENT, "null argument");
-  if (batch < 1 || batch > SE12_MAX_BATCH)
-    return fail(SE12_ERR_INVALID_ARGUMENT, "batch must be in 1.." + std::to_string(SE12_MAX_BATCH));
-  const LaunchConfig c = choose_config(false, m->view.tiles, m->view.cols, batch, m->sm_count);
+static void fill_launch_config(const LaunchConfig& c, se12_launch_config* out) {
   out->grid = c.grid;
   out->threads = se12::gemv_threads(c.wide != 0);
   out->smem_bytes = static_cast<int>(c.smem);
@@ -415,6 +411,23 @@ int se12_gemv_launch_config(const se12_matrix* m, int batch, se12_launch_config*
   out->x_resident = c.x_resident;
   out->row_mode = c.row_mode;
   out->wide = c.wide;
+}
+
+int se12_gemv_launch_config(const se12_matrix* m, int batch, se12_launch_config* out) {
+  if (!m || !out) return fail(SE12_ERR_INVALID_ARGUMENT, "null argument");
+  if (batch < 1 || batch > SE12_MAX_BATCH)
+    return fail(SE12_ERR_INVALID_ARGUMENT, "batch must be in 1.." + std::to_string(SE12_MAX_BATCH));
+  fill_launch_config(choose_config(false, m->view.tiles, m->view.cols, batch, m->sm_count), out);
+  return SE12_OK;
+}
+
+int se12_gemv_plan(int rows, int cols, int batch, int sm_count, se12_launch_config* out) {
+  if (!out) return fail(SE12_ERR_INVALID_ARGUMENT, "null argument");
+  if (rows <= 0 || cols <= 0) return fail(SE12_ERR_INVALID_ARGUMENT, "rows and cols must be positive");
+  if (batch < 1 || batch > SE12_MAX_BATCH)
+    return fail(SE12_ERR_INVALID_ARGUMENT, "batch must be in 1.." + std::to_string(SE12_MAX_BATCH));
+  if (sm_count < 1 || sm_count > 1024) return fail(SE12_ERR_INVALID_ARGUMENT, "sm_count must be in 1..1024");
+  fill_launch_config(choose_config(false, tiles_of(rows, cols), cols, batch, sm_count), out);
   return SE12_OK;
 }
 

@@ -122,3 +122,65 @@ def test_segmented_create_rejects_bad_segments(lib):
     assert "multiple of 16" in lib.se12_last_error().decode()
     rows = (ctypes.c_int32 * 5)(16, 16, 16, 16, 16)
     assert lib.se12_matrix_create_segmented(ctypes.byref(s), 5, rows, books, ctypes.byref(handle)) == 1
+
+
+def plan(lib, rows, cols, batch, sm_count):
+    from se12_b200 import _lib
+
+    cfg = _lib.Se12LaunchConfigStruct()
+    status = lib.se12_gemv_plan(rows, cols, batch, sm_count, ctypes.byref(cfg))
+    return status, {name: getattr(cfg, name) for name, _ in cfg._fields_}
+
+
+SWEEP_ROWS = [1, 16, 33, 272, 2048, 2304, 4096, 9216, 18432, 57344, 256000, 1048592]
+SWEEP_COLS = [1, 256, 300, 2048, 2304, 4096, 9216, 14336, 36864, 65536]
+
+
+@pytest.mark.parametrize("sm_count", [148, 132, 80, 1])
+def test_launch_table_stays_within_the_hardware(lib, sm_count):
+    """Every configuration the table picks fits the SM: shared memory (with
+    the kernel's 1 KB of static shared memory) within 227 KB per CTA, and
+    within 112 KB when two CTAs share an SM; the grid within the stream-K
+    workspace (two CTAs per SM); the wide layout only with x resident, row
+    mode, batch <= 8 and a pipeline of at least 7 stages."""
+    for rows in SWEEP_ROWS:
+        for cols in SWEEP_COLS:
+            tiles = -(-rows // 16) * -(-cols // 256)
+            for batch in (1, 2, 4, 8, 9, 16):
+                status, c = plan(lib, rows, cols, batch, sm_count)
+                assert status == 0
+                where = (rows, cols, batch, sm_count, c)
+                assert c["smem_bytes"] + 1024 <= 227 * 1024, where
+                assert 1 <= c["grid"] <= c["ctas_per_sm"] * sm_count and c["grid"] <= 2 * sm_count, where
+                assert c["grid"] <= tiles, where
+                assert c["ctas_per_sm"] in (1, 2) and (c["ctas_per_sm"] == 1 or c["smem_bytes"] <= 112 * 1024), where
+                if c["wide"]:
+                    assert c["threads"] == 704 and c["ctas_per_sm"] == 1 and batch <= 8, where
+                    assert c["stage_tiles"] == 4 and c["x_resident"] == 1 and c["row_mode"] == 1 and c["stages"] >= 7, where
+                else:
+                    assert c["threads"] == 320 and c["stage_tiles"] in (4, 8) and 2 <= c["stages"] <= 4, where
+                if c["stage_tiles"] == 8:
+                    assert c["x_resident"] == 1, where
+
+
+def test_launch_table_choices_for_gemma2_2b(lib):
+    """On 148 SMs at batch 1 the table follows the measured stacked timings:
+    the wide layout for the lm_head (197 us against 199 us) and the down
+    projection (12.6 against 13.8 us), 8-tile stages with two CTAs per SM for
+    q/k/v, o and gate_up (where the wide layout measured 1.8-2 us slower)."""
+    layout = {}
+    for name, rows, cols in [("lm_head", 256000, 2304), ("down", 2304, 9216), ("gate_up", 18432, 2304),
+                             ("qkv", 4096, 2304), ("o", 2304, 2048)]:
+        status, c = plan(lib, rows, cols, 1, 148)
+        assert status == 0
+        layout[name] = "wide" if c["wide"] else c["stage_tiles"]
+    assert layout == {"lm_head": "wide", "down": "wide", "gate_up": 8, "qkv": 8, "o": 8}
+
+
+def test_plan_rejects_bad_arguments(lib):
+    from se12_b200 import _lib
+
+    cfg = _lib.Se12LaunchConfigStruct()
+    for args in [(0, 256, 1, 148), (16, 0, 1, 148), (16, 256, 0, 148), (16, 256, 17, 148), (16, 256, 1, 0)]:
+        assert lib.se12_gemv_plan(*args, ctypes.byref(cfg)) == 1, args
+    assert lib.se12_gemv_plan(16, 256, 1, 148, None) == 1

@@ -11,6 +11,7 @@
 
 from __future__ import annotations
 
+import ctypes
 import hashlib
 
 import numpy as np
@@ -199,12 +200,18 @@ def test_launch_table_reaches_every_configuration():
     mode and stream-K, 8-tile stages with a pipeline deeper than 2, and the
     wide layout (one CTA per SM, x resident, 4-tile stages taken in turn by
     its warp groups; row mode only)."""
+    from se12_b200 import _lib
+
     sms = torch.cuda.get_device_properties(0).multi_processor_count
     seen, deep = set(), False
     for kind, rows, cols in GEMV_SHAPES:
         m = gemv_fixture(kind, rows, cols)[2]
         for batch in (1, 2, 4, 8, 16):
             c = m.launch_config(batch)
+            # the host-only plan from the shape gives the same answer
+            cfg = _lib.Se12LaunchConfigStruct()
+            assert _lib.load().se12_gemv_plan(rows, cols, batch, sms, ctypes.byref(cfg)) == 0
+            assert {name: getattr(cfg, name) for name, _ in cfg._fields_} == c
             if c["wide"]:
                 assert c["threads"] == 704 and c["stage_tiles"] == 4 and c["x_resident"] == 1 and c["stages"] >= 7
                 assert c["ctas_per_sm"] == 1 and 1 <= c["grid"] <= sms and batch <= 8 and c["row_mode"] == 1
