@@ -98,10 +98,10 @@ __host__ __device__ constexpr int stage_weight_bytes(bool raw, bool full_tiles) 
   return stage_tiles(full_tiles) * (raw ? 8192 : 6144);
 }
 constexpr int kXRowStride = 576;        // bytes per (tile, batch row) x slice when staged: 512 + 64 pad
+// A GEMV CTA: its consumer warps (8, or 20 in the wide layout), then the
+// producer warp (TMA / bulk copies), then the reducer warp (sums the
+// consumers' row partials).
 constexpr int kConsumerWarps = 8;
-constexpr int kProducerWarp = kConsumerWarps;      // TMA / bulk copies
-constexpr int kReducerWarp = kConsumerWarps + 1;   // sums the consumers' row partials
-constexpr int kGemvThreads = (kConsumerWarps + 2) * 32;
 constexpr int kWideGroups = 5;
 constexpr int kMaxWideStages = kWideGroups + 4;  // the deepest wide pipeline the launch table picks
 __host__ __device__ constexpr int consumer_warps(bool wide) { return wide ? kWideGroups * 4 : kConsumerWarps; }
