@@ -824,8 +824,11 @@ __global__ void __launch_bounds__(gemv_threads(WIDE), WIDE ? 1 : 2) gemv_kernel(
     // groups in order: it waits for each and arrives on its empty barrier
     // once, the groups whose stages it skips included (a warp takes at most
     // one stage of a group). Rows come first, so that no warp waits for
-    // records or weights while another needs its partial. A stage's slot is
-    // released by the group's 4 warps once its data has landed.
+    // records or weights while another needs its partial. Every warp
+    // deposits every row, in order: its waits on a reduction buffer's
+    // barrier then stay within one phase of the reducer, which is all a
+    // parity wait can tell apart. A stage's slot is released by the group's
+    // 4 warps once its data has landed.
     constexpr int kG = kWideGroups;
     const int grp = warp >> 2;
     const int tr_end = (tend > tstart) ? (tend - 1) / KT : tr_first - 1;
