@@ -626,7 +626,7 @@ def run_ours(args) -> None:
 
 
 def run_tp(args) -> None:
-    """Tensor-parallel decode step (SURVEY configs 2-4): every rank holds
+    """Tensor-parallel decode step (baseline configs 2-4): every rank holds
     its Megatron shards of every matrix -- q/k/v/gate/up by output rows, o
     and down by input columns followed by an NCCL all-reduce of the fp32
     partial sums, the LM head by rows followed by an all-gather of the

@@ -115,7 +115,10 @@ void se12_matrix_destroy(se12_matrix* m);
  * must be zeroed once (se12_workspace_clear) before first use; every
  * completed call leaves it ready for the next. Its layout does not depend on
  * the matrix, so one workspace (sized for the largest matrix) serves every
- * call on a stream; calls that may overlap on the GPU need separate ones. */
+ * call on a stream; calls that may overlap on the GPU need separate ones.
+ * After se12_device_status reports a timed-out wait (bit 0), zero every
+ * workspace that such a call used again before reusing it: a CTA that
+ * published its partial row after its finisher gave up leaves its flag set. */
 size_t se12_gemv_workspace_bytes(const se12_matrix* m, int batch);
 int se12_workspace_clear(void* workspace_dev, size_t bytes, void* stream);
 
@@ -214,7 +217,10 @@ int se12_gemv_allreduce(const se12_matrix* m, const uint16_t* x_dev, int batch, 
  *    message and without launching anything. Matrix size is not limited.
  *  - The current device must be the matrix's device. The first call on a
  *    device looks up the scratch's address (cudaGetSymbolAddress); make that
- *    first call before any stream capture.
+ *    first call before any stream capture. The address is kept for the life
+ *    of the process: after cudaDeviceReset (or anything else that replaces
+ *    the device's primary context) this entry point must not be called
+ *    again on that device in the same process.
  *  - Every call clears the scratch's flags on `stream` (cudaMemsetAsync)
  *    and then launches the GEMV; it allocates nothing.
  *  - All calls on a device share the one scratch, which keeps the last

@@ -53,6 +53,13 @@ class _WorkspacePool:
     def clear(self):
         self._buffers.clear()
 
+    def reset(self):
+        """Zeroes every pooled workspace again (after a kernel gave up on a
+        wait, its flags may not be back at zero)."""
+        for (index, stream), buf in self._buffers.items():
+            with torch.cuda.device(index):
+                _lib.call("se12_workspace_clear", ctypes.c_void_p(buf.data_ptr()), buf.numel(), ctypes.c_void_p(stream))
+
 
 WORKSPACES = _WorkspacePool()
 
@@ -332,8 +339,17 @@ def bf16_gemv(weights: torch.Tensor, x: torch.Tensor, out: torch.Tensor | None =
     return gemv_call(None, x, out, raw_weights=w)
 
 
+STATUS_WAIT_TIMEOUT = 1
+
+
 def device_status(clear: bool = True) -> int:
-    """Device status word of the library (non-zero after a kernel-side error)."""
+    """Device status word of the library (non-zero after a kernel-side error).
+
+    After a timed-out wait (bit 0) a stream-K workspace may hold a flag that
+    a late contributor set after its finisher gave up, so the pooled
+    workspaces are zeroed again before any further call uses them."""
     v = ctypes.c_uint(0)
     _lib.call("se12_device_status", ctypes.byref(v), 1 if clear else 0)
+    if v.value & STATUS_WAIT_TIMEOUT:
+        WORKSPACES.reset()
     return v.value

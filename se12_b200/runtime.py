@@ -10,9 +10,11 @@ built).
       bit to the uncompressed model (AC-016);
     - ``"fused"``: the fused decode + GEMV kernel, fp32 accumulation, output
       cast to the activation dtype (chunks of 16 rows for larger batches);
-    - ``"auto"``: fused for decode-sized inputs (at most ``FUSED_MAX_ROWS``
-      rows), exact for prefill (AC-025's dispatch rule with this GPU's
-      measured path: the fused kernel is the product's only GEMV).
+    - ``"by_rows"`` (the default): a fixed rule on the input's row count,
+      fused for decode-sized inputs (at most ``FUSED_MAX_ROWS`` rows), exact
+      for prefill (AC-025's dispatch rule). The rule depends on the shape
+      only: there is no run-time choice and no dense fallback of the fused
+      path, which stays the product's only GEMV.
 * ``CompressedEmbedding`` replaces an ``nn.Embedding``: a lookup decodes
   only the requested rows (row-tile decode); as a tied LM head it serves
   through the GEMV path (``as_linear``).
@@ -37,7 +39,7 @@ import torch.nn.functional as F
 from .device import DeviceSe12Matrix
 
 FUSED_MAX_ROWS = 16
-MODES = ("exact", "fused", "auto")
+MODES = ("exact", "fused", "by_rows")
 
 
 def _check_mode(mode: str) -> str:
@@ -52,31 +54,45 @@ class ProjectionGroup:
 
     ``output(member, x)`` returns the whole group's fused GEMV of x. The
     result of a call is kept for the other members: each of them takes it
-    once, for an input with the same storage, version, shape and stream;
-    any other call computes afresh. So a block that runs q_proj, k_proj and
-    v_proj on one hidden state (also while a CUDA graph captures it) runs one
-    GEMV."""
+    once, for the same input; any other call computes afresh. So a block
+    that runs q_proj, k_proj and v_proj on one hidden state (also while a
+    CUDA graph captures it) runs one GEMV.
+
+    "The same input" is checked against the tensor the result was computed
+    from, which the group holds a reference to until every other member has
+    taken the result: its storage stays allocated, so no other tensor can
+    appear at its address in the meantime, and an in-place write to it bumps
+    its version. A member whose input has another storage offset, shape,
+    dtype, version or stream computes afresh."""
 
     def __init__(self, matrix: DeviceSe12Matrix, members: tuple):
         self.matrix = matrix
         self.members = tuple(members)
+        self._x = None        # the input of the kept result (kept alive while members are pending)
         self._key = None
         self._y = None
         self._pending: set = set()
 
     @staticmethod
     def _key_of(x: torch.Tensor):
-        return (x.data_ptr(), x._version, tuple(x.shape), x.dtype, torch.cuda.current_stream(x.device).cuda_stream)
+        stream = torch.cuda.current_stream(x.device).cuda_stream if x.is_cuda else None
+        return (x.untyped_storage().data_ptr(), x.storage_offset(), tuple(x.stride()), x._version, tuple(x.shape),
+                x.dtype, stream)
 
     def output(self, member: str, x: torch.Tensor) -> torch.Tensor:
-        key = self._key_of(x)
-        if member in self._pending and key == self._key:
+        if member in self._pending and self._x is not None and self._key_of(x) == self._key:
             self._pending.discard(member)
-            return self._y
-        self._y = self.matrix.gemv(x)
-        self._key = key
+            y = self._y
+            if not self._pending:
+                self._x = self._y = self._key = None
+            return y
+        y = self.matrix.gemv(x)
         self._pending = set(self.members) - {member}
-        return self._y
+        if self._pending:
+            self._x, self._key, self._y = x, self._key_of(x), y
+        else:
+            self._x = self._y = self._key = None
+        return y
 
 
 class CompressedLinear(torch.nn.Module):
@@ -86,7 +102,7 @@ class CompressedLinear(torch.nn.Module):
     matrix (its own segment): the fused path takes its slice of the group's
     GEMV, the exact path decodes just those rows."""
 
-    def __init__(self, matrix: DeviceSe12Matrix, bias: torch.Tensor | None = None, mode: str = "auto",
+    def __init__(self, matrix: DeviceSe12Matrix, bias: torch.Tensor | None = None, mode: str = "by_rows",
                  group: ProjectionGroup | None = None, member: str | None = None, rows: tuple | None = None):
         super().__init__()
         self.matrix = matrix
@@ -101,7 +117,7 @@ class CompressedLinear(torch.nn.Module):
             self.bias = None
 
     @classmethod
-    def from_linear(cls, linear: torch.nn.Linear, mode: str = "auto", device="cuda") -> "CompressedLinear":
+    def from_linear(cls, linear: torch.nn.Linear, mode: str = "by_rows", device="cuda") -> "CompressedLinear":
         from .codec import encode_device
 
         w = linear.weight.detach()
@@ -123,7 +139,7 @@ class CompressedLinear(torch.nn.Module):
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         rows = x.numel() // self.in_features if self.in_features else 0
-        if self.mode == "exact" or (self.mode == "auto" and rows > FUSED_MAX_ROWS):
+        if self.mode == "exact" or (self.mode == "by_rows" and rows > FUSED_MAX_ROWS):
             w = self.weight_bf16()
             return F.linear(x, w if x.dtype == torch.bfloat16 else w.to(x.dtype), self.bias)
         lead = x.shape[:-1]
@@ -171,7 +187,7 @@ class CompressedEmbedding(torch.nn.Module):
             rows = rows * self.embed_scale.to(rows.dtype)
         return rows
 
-    def as_linear(self, mode: str = "auto") -> CompressedLinear:
+    def as_linear(self, mode: str = "by_rows") -> CompressedLinear:
         """The tied output projection over the same streams (the LM head)."""
         return CompressedLinear(self.matrix, None, mode)
 
@@ -218,7 +234,7 @@ def group_projections(model: torch.nn.Module) -> int:
     return made
 
 
-def compress_model(model: torch.nn.Module, mode: str = "auto", device="cuda", embeddings: bool = True,
+def compress_model(model: torch.nn.Module, mode: str = "by_rows", device="cuda", embeddings: bool = True,
                    group: bool = True) -> torch.nn.Module:
     """Replaces every BF16 ``nn.Linear`` (and, with ``embeddings``, every BF16
     ``nn.Embedding``) of ``model`` in place. Layers that share one weight
@@ -250,7 +266,7 @@ def compress_model(model: torch.nn.Module, mode: str = "auto", device="cuda", em
     return model
 
 
-def load_packed(packed_dir: str | pathlib.Path, model: torch.nn.Module, mode: str = "auto", device="cuda",
+def load_packed(packed_dir: str | pathlib.Path, model: torch.nn.Module, mode: str = "by_rows", device="cuda",
                 group: bool = True) -> torch.nn.Module:
     """Fills ``model`` from a packed directory: each ``nn.Linear`` /
     ``nn.Embedding`` whose ``<name>.weight`` is an SE12 entry becomes a

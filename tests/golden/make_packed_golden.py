@@ -82,4 +82,6 @@ def main(reference_src: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference/src")
+    if len(sys.argv) != 2:
+        sys.exit(f"usage: python {pathlib.Path(__file__).name} <path to the reference's src directory (holds lws/)>")
+    main(sys.argv[1])

@@ -1,4 +1,4 @@
-"""Tensor-parallel sharding (SURVEY multi-GPU row, configs 2-4): shards cut
+"""Tensor-parallel sharding (the multi-GPU configs 2-4): shards cut
 from the packed streams decode to exactly the matching slice of the
 original matrix, and the sharded layer's collectives (gloo ranks on CPU
 here; NCCL on GPUs) reassemble the unsharded product.

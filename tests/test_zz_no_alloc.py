@@ -49,13 +49,30 @@ def rel_err(y: torch.Tensor, ref: torch.Tensor) -> float:
     return float(((y.double() - ref.double()).abs() / ref.double().abs().clamp_min(1.0)).max())
 
 
-@pytest.mark.parametrize("rows,cols,batch", [(2304, 2304, 1), (2304, 2304, 4), (1000, 700, 3), (4608, 9216, 16)])
-def test_noalloc_matches_workspace_entry_point_on_two_calls(rows, cols, batch):
+# (rows, cols, batch, stream-K?): the stream-K cases split tile rows between
+# CTAs, so their partial rows and per-CTA flags go through the fixed scratch
+# (written by the contributors, read and cleared by the finisher); the row
+# mode cases never touch it.
+CASES = [
+    (2304, 2304, 1, False),
+    (2304, 2304, 4, False),
+    (1000, 700, 3, False),
+    (4608, 9216, 16, False),
+    (256, 9216, 1, True),     # 144 CTAs, x resident
+    (1024, 16384, 4, True),   # 296 CTAs (two per SM), x staged
+    (256, 9216, 16, True),    # two batch blocks through the partial rows
+]
+
+
+@pytest.mark.parametrize("rows,cols,batch,stream_k", CASES)
+def test_noalloc_matches_workspace_entry_point_on_two_calls(rows, cols, batch, stream_k):
     from se12_b200 import _lib
     from se12_b200.codec import encode_device
     from se12_b200.device import device_status
 
     m = encode_device(synthetic_bf16(rows, cols, seed=rows + cols))
+    if torch.cuda.get_device_properties(0).multi_processor_count == 148:
+        assert m.launch_config(batch)["row_mode"] == (0 if stream_k else 1)
     ldx = (cols + 7) // 8 * 8
     for call in range(2):
         g = torch.Generator(device="cuda").manual_seed(1000 * call + batch)
