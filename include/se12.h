@@ -230,6 +230,65 @@ int se12_gemv_allreduce(const se12_matrix* m, const uint16_t* x_dev, int batch, 
 int se12_gemv_noalloc(const se12_matrix* m, const uint16_t* x_dev, int batch, int ldx, float* y_dev, int ldy,
                       void* stream);
 
+/*
+ * Chains: a sequence of GEMVs run in order by ONE persistent launch, for
+ * example every projection of a decode step (q/k/v, o, gate/up, down of each
+ * layer, then the LM head). Op j reads its x only after op j - 1 has been
+ * completed by every CTA (so x of op j may be y of op j - 1, or computed from
+ * it between launches), while the weights of op j already stream in: the
+ * per-launch fill, drain and hand-over cost of one launch per GEMV is paid
+ * once per chain. Results are the same GEMVs as se12_gemv's (fp32
+ * accumulation, fp32 y; within 1e-3 of the fp64 product), deterministic for
+ * a given chain. This is the stacked mode of the reference's
+ * microbenchmark design (.spec/features/fused-decode-gemv/design.md:155-165:
+ * the same projections of every layer back to back), taken into one kernel;
+ * each op replaces one Se12MatVecKernel.multiply / lws_gemv_se12 call
+ * (src/lws/adapters/cuda/gemv.py:196-226, kernels/gemv_se12.cu:50-64).
+ *
+ * Use: se12_chain_create -> se12_chain_add_* per GEMV, in order ->
+ * se12_chain_descriptor_bytes / se12_chain_workspace_bytes -> allocate both
+ * (descriptors 64-byte aligned, workspace 256-byte aligned) ->
+ * se12_chain_upload (copies the descriptors, zeroes the workspace) ->
+ * se12_chain_run on a stream, any number of times (graph-capturable: it only
+ * launches). Launches of one chain must be ordered on one stream. The chain
+ * keeps the pointers it was given: matrices, records, x and y must stay
+ * allocated while it runs. A chain's GEMVs all have the chain's batch; one
+ * whose x (batch x cols BF16) does not fit shared memory is split by column
+ * blocks into ops that accumulate into y. After se12_device_status reports a
+ * timed-out wait, se12_chain_reset zeroes the workspace before the next run.
+ */
+typedef struct se12_chain se12_chain;
+
+/* Per-tile records a chain reads (escape positions with their exponents,
+ * fallback ranks): 64 bytes per tile, filled once per matrix by
+ * se12_matrix_prepare_records after se12_matrix_prepare. No reference
+ * counterpart (derived like the reference's host tables, gemv.py:47-77). */
+size_t se12_tile_records_bytes(int rows, int cols);
+int se12_matrix_prepare_records(const se12_matrix* m, uint32_t* records_dev, void* stream);
+
+/* dense = 1: a chain of dense BF16 GEMVs (the comparison baseline, the
+ * chain form of bf16_gemv / lws_gemv_raw_bf16, gemv_raw_bf16.cu:18-56). */
+int se12_chain_create(int batch, int dense, se12_chain** out);
+int se12_chain_add_gemv(se12_chain* c, const se12_matrix* m, const uint32_t* records_dev, const uint16_t* x_dev,
+                        int ldx, float* y_dev, int ldy);
+/* The GEMV of a column shard, its rows all-reduced over the peer group (as
+ * se12_gemv_allreduce). Every rank's chain must hold the same ops in the same
+ * order; all such ops of a chain use one peer group. */
+int se12_chain_add_gemv_allreduce(se12_chain* c, const se12_matrix* m, const uint32_t* records_dev,
+                                  const uint16_t* x_dev, int ldx, float* y_dev, int ldy, const se12_peer_group* peers);
+int se12_chain_add_dense(se12_chain* c, const uint16_t* w_dev, int rows, int cols, int ldw, const uint16_t* x_dev,
+                         int ldx, float* y_dev, int ldy);
+int se12_chain_ops(const se12_chain* c);
+size_t se12_chain_descriptor_bytes(const se12_chain* c);
+size_t se12_chain_workspace_bytes(const se12_chain* c);
+int se12_chain_upload(se12_chain* c, void* descriptors_dev, void* workspace_dev, size_t workspace_bytes, void* stream);
+int se12_chain_run(const se12_chain* c, void* stream);
+int se12_chain_reset(const se12_chain* c, void* stream);
+/* The launch se12_chain_run makes: CTAs, consumer warps per CTA, dynamic
+ * shared memory, ops (after column splits). */
+int se12_chain_info(const se12_chain* c, int* grid, int* consumers, int* smem_bytes, int* ops);
+void se12_chain_destroy(se12_chain* c);
+
 /* Exact BF16 bits of the whole matrix, row-major [rows, ldo] (ldo >= cols).
  * Replaces CudaSe12WeightDecoder.decode / decode_to_device and the kernel
  * lws_se12_decode (src/lws/adapters/cuda/se12_decoder.py:54-76,

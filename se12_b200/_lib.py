@@ -92,6 +92,22 @@ SIGNATURES = {
     "se12_encode_tiles": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
     "se12_encode_bitmap": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p]),
     "se12_encode_raw": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p]),
+    "se12_tile_records_bytes": (c_size_t, [c_int, c_int]),
+    "se12_matrix_prepare_records": (c_int, [c_void_p, c_void_p, c_void_p]),
+    "se12_chain_create": (c_int, [c_int, c_int, ctypes.POINTER(c_void_p)]),
+    "se12_chain_add_gemv": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_int]),
+    "se12_chain_add_gemv_allreduce": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_int,
+                                              ctypes.POINTER(Se12PeerGroupStruct)]),
+    "se12_chain_add_dense": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_int, c_void_p, c_int]),
+    "se12_chain_ops": (c_int, [c_void_p]),
+    "se12_chain_descriptor_bytes": (c_size_t, [c_void_p]),
+    "se12_chain_workspace_bytes": (c_size_t, [c_void_p]),
+    "se12_chain_upload": (c_int, [c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
+    "se12_chain_run": (c_int, [c_void_p, c_void_p]),
+    "se12_chain_reset": (c_int, [c_void_p, c_void_p]),
+    "se12_chain_info": (c_int, [c_void_p, ctypes.POINTER(c_int), ctypes.POINTER(c_int), ctypes.POINTER(c_int),
+                                ctypes.POINTER(c_int)]),
+    "se12_chain_destroy": (None, [c_void_p]),
     "se12_device_status": (c_int, [ctypes.POINTER(c_uint), c_int]),
     "se12_status_string": (c_char_p, [c_int]),
     "se12_last_error": (c_char_p, []),

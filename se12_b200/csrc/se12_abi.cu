@@ -5,6 +5,7 @@
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <vector>
 
 #include <cudaTypedefs.h>
 
@@ -755,6 +756,339 @@ int se12_device_status(unsigned* status, int clear) {
   if (!status) return fail(SE12_ERR_INVALID_ARGUMENT, "null argument");
   cudaError_t err = se12::read_device_status(status, clear != 0);
   if (err != cudaSuccess) return cuda_fail(err, "read device status");
+  return SE12_OK;
+}
+
+}  // extern "C"
+
+// ------------------------------------------------------------------ chains
+// A chain: GEMVs run in order by one persistent launch (se12_chain.cu).
+// Host side: the ops (with their TMA descriptors) in a vector; upload copies
+// them to a caller buffer on the device and zeroes the caller's workspace.
+struct se12_chain {
+  std::vector<se12::ChainOp> ops;
+  int batch = 1;
+  bool dense = false;
+  int device = 0;
+  int sm_count = 0;
+  int consumers = 0;
+  int x_bytes = 0;
+  int x_stride_max = 0;
+  int n_ar = 0;
+  se12::PeerArgs peers{};
+  void* desc_dev = nullptr;
+  void* ws_dev = nullptr;
+  bool uploaded = false;
+};
+
+namespace {
+
+constexpr size_t kChainSmemLimit = 227 * 1024;
+constexpr int kChainMinConsumers = 12;
+
+// x budget: what is left of shared memory with kChainMinConsumers warps.
+size_t chain_x_budget(bool dense) {
+  return kChainSmemLimit - se12::chain_smem_bytes(dense, kChainMinConsumers, 0);
+}
+
+// Consumer warps that fit beside an x buffer of x_bytes.
+int chain_consumers(bool dense, int x_bytes) {
+  int c = se12::kChainMaxWarps;
+  while (c > 1 && se12::chain_smem_bytes(dense, c, x_bytes) > kChainSmemLimit) --c;
+  return c;
+}
+
+int chain_x_stride(int width_tiles) { return width_tiles * 512 + 64; }
+
+// Tile columns per op so that batch rows of x fit the budget.
+int chain_split_width(bool dense, int batch, int tile_cols) {
+  const size_t budget = chain_x_budget(dense);
+  int w = tile_cols;
+  while (w > 1 && static_cast<size_t>(batch) * chain_x_stride(w) > budget) w = (w + 1) / 2;
+  return w;
+}
+
+struct ChainLayout {
+  size_t done, gen, rowcnt, partials, total;
+};
+
+ChainLayout chain_layout(int n_ops, long long workers) {
+  ChainLayout l{};
+  auto up = [](size_t v) { return (v + 255) / 256 * 256; };
+  l.done = 0;
+  l.gen = up(static_cast<size_t>(n_ops) * 4);
+  l.rowcnt = l.gen + 256;
+  l.partials = up(l.rowcnt + static_cast<size_t>(n_ops) * workers * 4);
+  l.total = up(l.partials + static_cast<size_t>(workers) * 2 * 256 * 4);
+  return l;
+}
+
+int chain_check_open(se12_chain* c) {
+  if (!c) return fail(SE12_ERR_INVALID_ARGUMENT, "null chain");
+  if (c->uploaded) return fail(SE12_ERR_INVALID_ARGUMENT, "the chain was uploaded: no more ops can be added");
+  if (static_cast<int>(c->ops.size()) >= se12::kChainMaxOps)
+    return fail(SE12_ERR_INVALID_ARGUMENT, "a chain holds at most " + std::to_string(se12::kChainMaxOps) + " ops");
+  return SE12_OK;
+}
+
+// Appends the op(s) of one GEMV: one per column block of x that fits the
+// shared-memory budget; every block after the first accumulates into y.
+int chain_append(se12_chain* c, se12::ChainOp base, int tile_cols, int cols) {
+  const int width = chain_split_width(c->dense, c->batch, tile_cols);
+  const int tile_rows_n = base.tiles;  // caller passes tile rows here
+  for (int k0 = 0; k0 < tile_cols; k0 += width) {
+    se12::ChainOp op = base;
+    op.k0 = k0;
+    op.k1 = std::min(tile_cols, k0 + width);
+    op.tiles = tile_rows_n * (op.k1 - op.k0);
+    op.x_cols = std::min(cols, op.k1 * SE12_TILE_COLS) - k0 * SE12_TILE_COLS;
+    op.accumulate = k0 > 0 ? 1 : 0;
+    c->x_stride_max = std::max(c->x_stride_max, chain_x_stride(op.k1 - op.k0));
+    c->ops.push_back(op);
+  }
+  return SE12_OK;
+}
+
+int chain_check_io(se12_chain* c, int rows, int cols, const uint16_t* x, int ldx, const float* y, int ldy) {
+  return check_gemv_io(rows, cols, x, c->batch, ldx, y, ldy);
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t se12_tile_records_bytes(int rows, int cols) {
+  if (rows <= 0 || cols <= 0) return 0;
+  return static_cast<size_t>(tiles_of(rows, cols)) * SE12_ESCAPE_BUDGET * sizeof(uint32_t);
+}
+
+int se12_matrix_prepare_records(const se12_matrix* m, uint32_t* records, void* stream) {
+  if (!m || !records) return fail(SE12_ERR_INVALID_ARGUMENT, "null argument");
+  if (!aligned16(records)) return fail(SE12_ERR_MISALIGNED, "records must be 16-byte aligned");
+  cudaError_t err = se12::launch_prepare_records(m->view, records, static_cast<cudaStream_t>(stream));
+  if (err != cudaSuccess) return cuda_fail(err, "se12_matrix_prepare_records launch");
+  return SE12_OK;
+}
+
+int se12_chain_create(int batch, int dense, se12_chain** out) {
+  if (!out) return fail(SE12_ERR_INVALID_ARGUMENT, "null argument");
+  *out = nullptr;
+  if (batch < 1 || batch > SE12_MAX_BATCH)
+    return fail(SE12_ERR_INVALID_ARGUMENT, "batch must be in 1.." + std::to_string(SE12_MAX_BATCH));
+  int device = 0, sm_count = 0;
+  int st = current_device_info(&device, &sm_count);
+  if (st != SE12_OK) return st;
+  se12_chain* c = new se12_chain();
+  c->batch = batch;
+  c->dense = dense != 0;
+  c->device = device;
+  c->sm_count = sm_count;
+  c->peers.world = 1;
+  *out = c;
+  return SE12_OK;
+}
+
+void se12_chain_destroy(se12_chain* c) { delete c; }
+
+static int chain_add_se12(se12_chain* c, const se12_matrix* m, const uint32_t* records, const uint16_t* x, int ldx,
+                          float* y, int ldy, int ar_index) {
+  int st = chain_check_open(c);
+  if (st != SE12_OK) return st;
+  if (c->dense) return fail(SE12_ERR_INVALID_ARGUMENT, "a dense chain takes dense GEMVs only");
+  if (!m || !records) return fail(SE12_ERR_INVALID_ARGUMENT, "null matrix or records");
+  if (m->device != c->device) return fail(SE12_ERR_INVALID_ARGUMENT, "matrix and chain are on different devices");
+  if (!aligned16(records)) return fail(SE12_ERR_MISALIGNED, "records must be 16-byte aligned");
+  st = chain_check_io(c, m->view.rows, m->view.cols, x, ldx, y, ldy);
+  if (st != SE12_OK) return st;
+  const se12::MatrixView& v = m->view;
+  se12::ChainOp op{};
+  // one-tile boxes of the sm and ec streams
+  const cuuint64_t rows16 = static_cast<cuuint64_t>(v.tiles) * SE12_TILE_ROWS;
+  const cuuint64_t sm_dims[3] = {128, 2, rows16};
+  const cuuint64_t sm_strides[2] = {128, 256};
+  const cuuint32_t sm_box[3] = {128, 2, SE12_TILE_ROWS};
+  st = encode_map(&op.sm_map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, v.sm, sm_dims, sm_strides, sm_box);
+  if (st != SE12_OK) return st;
+  const cuuint64_t ec_dims[2] = {128, rows16};
+  const cuuint64_t ec_strides[1] = {128};
+  const cuuint32_t ec_box[2] = {128, SE12_TILE_ROWS};
+  st = encode_map(&op.ec_map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, v.ec, ec_dims, ec_strides, ec_box);
+  if (st != SE12_OK) return st;
+  op.records = records;
+  op.fallback_raw = v.fallback_raw;
+  op.x = x;
+  op.y = y;
+  op.ldx = ldx;
+  op.ldy = ldy;
+  op.rows = v.rows;
+  op.cols = v.cols;
+  op.tile_cols = v.tile_cols;
+  op.tiles = v.tile_rows;  // tile rows: chain_append multiplies by the block width
+  op.ar_index = ar_index;
+  op.segments = v.segments;
+  for (int s = 0; s < se12::kMaxSegments; ++s) {
+    op.seg_end[s] = v.seg_end[s];
+    uint32_t w[4] = {0u, 0u, 0u, 0u};
+    for (int code = 0; code < 16; ++code) w[code >> 2] |= se12::table_byte(v.codebooks[s], code) << (8 * (code & 3));
+    for (int q = 0; q < 4; ++q) op.tab[s][q] = w[q];
+  }
+  return chain_append(c, op, v.tile_cols, v.cols);
+}
+
+int se12_chain_add_gemv(se12_chain* c, const se12_matrix* m, const uint32_t* records, const uint16_t* x, int ldx,
+                        float* y, int ldy) {
+  return chain_add_se12(c, m, records, x, ldx, y, ldy, -1);
+}
+
+int se12_chain_add_gemv_allreduce(se12_chain* c, const se12_matrix* m, const uint32_t* records, const uint16_t* x,
+                                  int ldx, float* y, int ldy, const se12_peer_group* g) {
+  int st = chain_check_open(c);
+  if (st != SE12_OK) return st;
+  if (!g) return fail(SE12_ERR_INVALID_ARGUMENT, "null peer group");
+  if (g->world < 2 || g->world > SE12_MAX_PEERS || g->rank < 0 || g->rank >= g->world)
+    return fail(SE12_ERR_INVALID_ARGUMENT, "peer group needs 2.." + std::to_string(SE12_MAX_PEERS) +
+                                               " ranks and 0 <= rank < world");
+  if (!m) return fail(SE12_ERR_INVALID_ARGUMENT, "null matrix");
+  if (m->view.rows > g->rows_cap)
+    return fail(SE12_ERR_INVALID_ARGUMENT, "matrix has " + std::to_string(m->view.rows) +
+                                               " rows, the peer buffers hold " + std::to_string(g->rows_cap));
+  if (chain_split_width(false, c->batch, m->view.tile_cols) < m->view.tile_cols)
+    return fail(SE12_ERR_INVALID_ARGUMENT, "an all-reduced GEMV must fit one op: x of this batch and width is "
+                                           "too large for shared memory");
+  for (int r = 0; r < g->world; ++r)
+    if (!g->recv[r] || !aligned16(g->recv[r])) return fail(SE12_ERR_MISALIGNED, "null or misaligned peer buffer");
+  if (c->n_ar > 0) {
+    if (c->peers.world != g->world || c->peers.rank != g->rank || c->peers.rows_cap != g->rows_cap)
+      return fail(SE12_ERR_INVALID_ARGUMENT, "all all-reduced ops of a chain use one peer group");
+    for (int r = 0; r < g->world; ++r)
+      if (c->peers.recv[r] != static_cast<unsigned long long*>(g->recv[r]))
+        return fail(SE12_ERR_INVALID_ARGUMENT, "all all-reduced ops of a chain use one peer group");
+  } else {
+    c->peers.world = g->world;
+    c->peers.rank = g->rank;
+    c->peers.rows_cap = g->rows_cap;
+    for (int r = 0; r < g->world; ++r) c->peers.recv[r] = static_cast<unsigned long long*>(g->recv[r]);
+    c->peers.epoch = g->epoch;
+  }
+  st = chain_add_se12(c, m, records, x, ldx, y, ldy, c->n_ar);
+  if (st == SE12_OK) ++c->n_ar;
+  return st;
+}
+
+int se12_chain_add_dense(se12_chain* c, const uint16_t* w, int rows, int cols, int ldw, const uint16_t* x, int ldx,
+                         float* y, int ldy) {
+  int st = chain_check_open(c);
+  if (st != SE12_OK) return st;
+  if (!c->dense) return fail(SE12_ERR_INVALID_ARGUMENT, "an SE12 chain takes SE12 GEMVs only");
+  if (!w) return fail(SE12_ERR_INVALID_ARGUMENT, "null weights");
+  if (rows <= 0 || cols <= 0 || ldw < cols) return fail(SE12_ERR_INVALID_ARGUMENT, "bad weight shape");
+  if (!aligned16(w) || (ldw % 8) != 0) return fail(SE12_ERR_MISALIGNED, "W must be 16-byte aligned, ldw % 8 == 0");
+  st = chain_check_io(c, rows, cols, x, ldx, y, ldy);
+  if (st != SE12_OK) return st;
+  se12::ChainOp op{};
+  int raw_3d = 0;
+  st = encode_raw_map(&op.sm_map, w, rows, cols, ldw, &raw_3d);
+  if (st != SE12_OK) return st;
+  op.raw_3d = raw_3d;
+  op.x = x;
+  op.y = y;
+  op.ldx = ldx;
+  op.ldy = ldy;
+  op.rows = rows;
+  op.cols = cols;
+  op.tile_cols = (cols + SE12_TILE_COLS - 1) / SE12_TILE_COLS;
+  op.tiles = (rows + SE12_TILE_ROWS - 1) / SE12_TILE_ROWS;
+  op.ar_index = -1;
+  op.segments = 1;
+  for (int s = 0; s < se12::kMaxSegments; ++s) op.seg_end[s] = INT32_MAX;
+  return chain_append(c, op, op.tile_cols, cols);
+}
+
+int se12_chain_ops(const se12_chain* c) { return c ? static_cast<int>(c->ops.size()) : 0; }
+
+size_t se12_chain_descriptor_bytes(const se12_chain* c) {
+  return c ? c->ops.size() * sizeof(se12::ChainOp) : 0;
+}
+
+static void chain_finalize(se12_chain* c) {
+  c->x_bytes = c->batch * c->x_stride_max;
+  c->consumers = chain_consumers(c->dense, c->x_bytes);
+}
+
+size_t se12_chain_workspace_bytes(const se12_chain* c) {
+  if (!c || c->ops.empty()) return 0;
+  se12_chain tmp = *c;
+  chain_finalize(&tmp);
+  return chain_layout(static_cast<int>(c->ops.size()), static_cast<long long>(c->sm_count) * tmp.consumers).total;
+}
+
+int se12_chain_upload(se12_chain* c, void* descriptors, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!c) return fail(SE12_ERR_INVALID_ARGUMENT, "null chain");
+  if (c->ops.empty()) return fail(SE12_ERR_INVALID_ARGUMENT, "empty chain");
+  if (!descriptors || (reinterpret_cast<uintptr_t>(descriptors) & 63u))
+    return fail(SE12_ERR_MISALIGNED, "the descriptor buffer must be 64-byte aligned");
+  chain_finalize(c);
+  const ChainLayout l = chain_layout(static_cast<int>(c->ops.size()), static_cast<long long>(c->sm_count) * c->consumers);
+  if (!workspace || workspace_bytes < l.total || (reinterpret_cast<uintptr_t>(workspace) & 255u))
+    return fail(SE12_ERR_WORKSPACE_TOO_SMALL, "chain workspace needs " + std::to_string(l.total) +
+                                                  " bytes, 256-byte aligned");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t err = cudaMemcpyAsync(descriptors, c->ops.data(), c->ops.size() * sizeof(se12::ChainOp),
+                                    cudaMemcpyHostToDevice, s);
+  if (err != cudaSuccess) return cuda_fail(err, "chain descriptor copy");
+  err = cudaMemsetAsync(workspace, 0, l.total, s);
+  if (err != cudaSuccess) return cuda_fail(err, "chain workspace clear");
+  c->desc_dev = descriptors;
+  c->ws_dev = workspace;
+  c->uploaded = true;
+  return SE12_OK;
+}
+
+int se12_chain_reset(const se12_chain* c, void* stream) {
+  if (!c || !c->uploaded) return fail(SE12_ERR_INVALID_ARGUMENT, "chain not uploaded");
+  const ChainLayout l = chain_layout(static_cast<int>(c->ops.size()), static_cast<long long>(c->sm_count) * c->consumers);
+  cudaError_t err = cudaMemsetAsync(c->ws_dev, 0, l.total, static_cast<cudaStream_t>(stream));
+  if (err != cudaSuccess) return cuda_fail(err, "chain workspace clear");
+  return SE12_OK;
+}
+
+int se12_chain_info(const se12_chain* c, int* grid, int* consumers, int* smem_bytes, int* ops) {
+  if (!c || !grid || !consumers || !smem_bytes || !ops) return fail(SE12_ERR_INVALID_ARGUMENT, "null argument");
+  se12_chain tmp = *c;
+  chain_finalize(&tmp);
+  *grid = tmp.sm_count;
+  *consumers = tmp.consumers;
+  *smem_bytes = static_cast<int>(se12::chain_smem_bytes(tmp.dense, tmp.consumers, tmp.x_bytes));
+  *ops = static_cast<int>(tmp.ops.size());
+  return SE12_OK;
+}
+
+int se12_chain_run(const se12_chain* c, void* stream) {
+  if (!c || !c->uploaded) return fail(SE12_ERR_INVALID_ARGUMENT, "chain not uploaded");
+  int device = -1;
+  cudaError_t err = cudaGetDevice(&device);
+  if (err != cudaSuccess) return cuda_fail(err, "cudaGetDevice");
+  if (device != c->device) return fail(SE12_ERR_INVALID_ARGUMENT, "the current device is not the chain's device");
+  const int n = static_cast<int>(c->ops.size());
+  const long long workers = static_cast<long long>(c->sm_count) * c->consumers;
+  const ChainLayout l = chain_layout(n, workers);
+  char* ws = static_cast<char*>(c->ws_dev);
+  se12::ChainParams p{};
+  p.ops = static_cast<const se12::ChainOp*>(c->desc_dev);
+  p.n_ops = n;
+  p.batch = c->batch;
+  p.consumers = c->consumers;
+  p.x_stride = c->x_stride_max;
+  p.x_bytes = c->x_bytes;
+  p.n_ar = c->n_ar;
+  p.done = reinterpret_cast<unsigned*>(ws + l.done);
+  p.gen = reinterpret_cast<unsigned*>(ws + l.gen);
+  p.rowcnt = reinterpret_cast<unsigned*>(ws + l.rowcnt);
+  p.partials = reinterpret_cast<float*>(ws + l.partials);
+  p.peers = c->peers;
+  const size_t smem = se12::chain_smem_bytes(c->dense, c->consumers, c->x_bytes);
+  err = se12::launch_chain(c->dense, p, c->sm_count, smem, static_cast<cudaStream_t>(stream));
+  if (err != cudaSuccess) return cuda_fail(err, "se12_chain_run launch");
   return SE12_OK;
 }
 

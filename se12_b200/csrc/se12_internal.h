@@ -145,7 +145,58 @@ inline size_t gemv_smem_bytes(bool raw, bool full_tiles, bool x_resident, int st
   return bytes;
 }
 
+// ------------------------------------------------------------------ chains
+// A chain is a sequence of GEMVs run by one persistent launch (se12_chain.cu):
+// op j reads its x only once every CTA has finished op j - 1.
+constexpr int kChainSlots = 2;            // TMA slots per consumer warp
+constexpr int kChainMaxWarps = 15;        // consumer warps per CTA (+ the control warp: 4 warps per SM sub-partition, 128 registers)
+constexpr uint32_t kChainSlotSe12 = 6144; // sm (4096 B) + ec (2048 B) of one tile
+constexpr uint32_t kChainSlotRaw = 8192;  // one dense BF16 tile
+constexpr int kChainMaxOps = 4096;
+
+// One op of a chain, in device memory (the TMA descriptors must be 64-byte
+// aligned and stay unchanged while a launch runs).
+struct alignas(64) ChainOp {
+  CUtensorMap sm_map;            // SE12: sm [16T rows][2][128 B], box one tile; dense: W, box one tile
+  CUtensorMap ec_map;            // SE12: ec [16T rows][128 B], box one tile
+  const uint32_t* records;       // SE12: [T][16] tile records (se12_matrix_prepare_records)
+  const uint16_t* fallback_raw;  // SE12: [F][4096] raw bits of fallback tiles
+  const uint16_t* x;             // [batch][ldx] bf16
+  float* y;                      // [batch][ldy] fp32
+  int ldx, ldy;
+  int rows, cols;                // the matrix
+  int tile_cols;                 // its tile columns
+  int k0, k1;                    // tile-column range this op multiplies (a column split of the matrix)
+  int tiles;                     // tile rows x (k1 - k0)
+  int x_cols;                    // columns of x this op reads: min(cols, 256 k1) - 256 k0
+  int accumulate;                // 1: y += result (an earlier op wrote the other columns' sum)
+  int ar_index;                  // >= 0: rows all-reduced over the peer group (the chain's ar_index-th such op)
+  int raw_3d;                    // dense: one 3-D box per tile (cols % 64 == 0) or four 2-D boxes
+  int segments;
+  int seg_end[kMaxSegments];     // exclusive end tile row per segment (INT32_MAX past the last)
+  uint32_t tab[kMaxSegments][4]; // decode table per segment (table_byte of codes 0..15, four per word)
+};
+
+struct ChainParams {
+  const ChainOp* ops;
+  int n_ops;
+  int batch;
+  int consumers;        // consumer warps per CTA (the CTA has one more: the control warp)
+  int x_stride;         // bytes per batch row of x in shared memory (= 64 mod 128)
+  int x_bytes;          // bytes of the x buffer
+  int n_ar;             // ops with an all-reduce
+  unsigned* done;       // [n_ops] CTAs that finished op j, over all launches
+  unsigned* gen;        // [2]: launches completed, CTAs that left the current launch
+  float* partials;      // [grid * consumers][2][16 * 16] partial rows
+  unsigned* rowcnt;     // [n_ops][grid * consumers] arrivals on a shared row (zero between launches)
+  PeerArgs peers;
+};
+
+size_t chain_smem_bytes(bool raw, int consumers, int x_bytes);
+
 // Kernel launchers (defined in the .cu files).
+cudaError_t launch_chain(bool raw, const ChainParams& p, int grid, size_t smem, cudaStream_t stream);
+cudaError_t launch_prepare_records(const MatrixView& m, uint32_t* records, cudaStream_t stream);
 cudaError_t launch_gemv(bool raw, const CUtensorMap& map0, const CUtensorMap& map1, const GemvArgs& a, int nblocks,
                         size_t smem, cudaStream_t stream, bool pdl);
 cudaError_t launch_prepare(const MatrixView& m, uint16_t* escape_pos, int32_t* fallback_index, cudaStream_t stream);

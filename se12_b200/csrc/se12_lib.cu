@@ -2,4 +2,5 @@
 // status word g_status, so they are compiled together.
 #include "se12_codec.cu"
 #include "se12_gemv.cu"
+#include "se12_chain.cu"
 #include "se12_abi.cu"

@@ -213,6 +213,19 @@ class DeviceSe12Matrix:
         return self._handle
 
     @property
+    def records(self) -> torch.Tensor:
+        """Per-tile records the chain kernel reads (64 bytes per tile: the
+        escaped weights' positions with their exponents, fallback ranks),
+        built on the device on first use."""
+        if getattr(self, "_records", None) is None:
+            rec = torch.empty(self.tiles * ESCAPE_BUDGET, dtype=torch.int32, device=self.device)
+            with torch.cuda.device(self.device):
+                _lib.call("se12_matrix_prepare_records", self._handle, ctypes.c_void_p(rec.data_ptr()),
+                          ctypes.c_void_p(stream_handle(self.device)))
+            self._records = rec
+        return self._records
+
+    @property
     def byte_size(self) -> int:
         """Algorithmic SE12 bytes: five streams + 15 codebook bytes."""
         # a segmented matrix counts each segment's own bitmap and codebook,

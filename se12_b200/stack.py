@@ -27,25 +27,55 @@ class GemvOp:
 
 
 class GemvStack:
-    def __init__(self, device: torch.device | str = "cuda"):
+    """With ``chain=True`` the sequence runs as one persistent launch
+    (``se12_b200.chain.Se12Chain``: op j reads x once op j - 1 is done, the
+    next op's weights stream in meanwhile) instead of one launch per GEMV;
+    every op then needs the same batch, and SE12 and dense ops do not mix."""
+
+    def __init__(self, device: torch.device | str = "cuda", chain: bool = False):
         self.device = torch.device(device)
         self.ops: list = []
         self.graph: torch.cuda.CUDAGraph | None = None
         self.stream = torch.cuda.Stream(self.device)
+        self.use_chain = bool(chain)
+        self.chain = None
 
     def add(self, matrix: DeviceSe12Matrix, x: torch.Tensor, y: torch.Tensor) -> None:
         self.ops.append(GemvOp(matrix, x, y))
         self.graph = None
+        self.chain = None
 
     def add_dense(self, weights: torch.Tensor, x: torch.Tensor, y: torch.Tensor) -> None:
         self.ops.append(GemvOp(None, x, y, weights))
         self.graph = None
+        self.chain = None
 
     @property
     def launches(self) -> int:
-        return len(self.ops)
+        return 1 if self.use_chain else len(self.ops)
+
+    def _build_chain(self):
+        from .chain import Se12Chain
+
+        dense = self.ops[0].matrix is None
+        batch = self.ops[0].x.shape[0]
+        chain = Se12Chain(batch, self.device, dense=dense)
+        for op in self.ops:
+            if (op.matrix is None) != dense or op.x.shape[0] != batch:
+                raise ValueError("a chain needs one batch size and one kind of GEMV")
+            if dense:
+                chain.add_dense(op.weights, op.x, op.y)
+            else:
+                chain.add(op.matrix, op.x, op.y)
+        chain.upload()
+        self.chain = chain
 
     def _launch_all(self) -> None:
+        if self.use_chain:
+            if self.chain is None:
+                self._build_chain()
+            self.chain.run()
+            return
         for op in self.ops:
             if op.matrix is not None:
                 gemv_call(op.matrix, op.x, op.y)
