@@ -74,9 +74,9 @@ def parse_args():
                         "memory every token; SE12 and BF16 on the same pipeline")
     p.add_argument("--eager", action="store_true",
                    help="issue each step's launches one by one instead of replaying a CUDA graph (profiler runs)")
-    p.add_argument("--no-chain", action="store_true",
-                   help="one launch per GEMV (programmatic dependent launch) instead of the whole step as one "
-                        "persistent chain launch")
+    p.add_argument("--chain", action="store_true",
+                   help="the whole step as one persistent chain launch instead of one launch per GEMV "
+                        "(programmatic dependent launch)")
     p.add_argument("--no-group", action="store_true",
                    help="one GEMV per projection instead of q/k/v and gate/up as one segmented matrix each")
     p.add_argument("--tp", action="store_true",
@@ -426,7 +426,7 @@ def run_ours(args) -> None:
 
     def stack_for(b, use_dense=False, cublas=False):
         xs = inputs_for(b)
-        st = GemvStack(device, chain=not args.no_chain)
+        st = GemvStack(device, chain=args.chain)
         outs = []
         for (name, m, kind), w in zip(mats, dense):
             y = torch.empty(b, m.rows, dtype=torch.float32, device=device)

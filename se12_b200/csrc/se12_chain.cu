@@ -510,11 +510,15 @@ __global__ void __launch_bounds__((kChainMaxWarps + 1) * 32, 1) chain_kernel(con
               __syncwarp();
               const int u_first = run_owner(static_cast<long long>(row) * W, T, GC);
               const int u_last = run_owner(static_cast<long long>(row + 1) * W - 1, T, GC);
+              // the counter adds up tiles, not workers: when the op has fewer
+              // tiles than the grid has warps, workers with empty runs lie
+              // between the row's holders and never arrive
               unsigned* rc = p.rowcnt + static_cast<size_t>(j) * GC + u_first;
+              const unsigned held = static_cast<unsigned>(i + 1 - seg_first);
               unsigned old = 0;
-              if (lane == 0) old = atom_add_acq_rel_gpu_u32(rc, 1u);
+              if (lane == 0) old = atom_add_acq_rel_gpu_u32(rc, held);
               old = __shfl_sync(0xFFFFFFFFu, old, 0);
-              emit = (old == static_cast<unsigned>(u_last - u_first));
+              emit = (old + held == static_cast<unsigned>(W));
               if (emit) {
                 __threadfence();
 #pragma unroll
@@ -522,7 +526,9 @@ __global__ void __launch_bounds__((kChainMaxWarps + 1) * 32, 1) chain_kernel(con
 #pragma unroll
                   for (int q = 0; q < 4; ++q) v[nb][q] = 0.f;
                 for (int w = u_first; w <= u_last; ++w) {
-                  const int wrow = run_start(T, w, GC) / W;
+                  const int ws = run_start(T, w, GC);
+                  if (ws == run_start(T, w + 1, GC)) continue;  // empty run: no partial
+                  const int wrow = ws / W;
                   const float* src = p.partials + (static_cast<size_t>(w) * 2 + (wrow == row ? 0 : 1)) * 256;
 #pragma unroll
                   for (int nb = 0; nb < NB; ++nb) {

@@ -174,8 +174,9 @@ struct alignas(64) ChainOp {
   int raw_3d;                    // dense: one 3-D box per tile (cols % 64 == 0) or four 2-D boxes
   int segments;
   int seg_end[kMaxSegments];     // exclusive end tile row per segment (INT32_MAX past the last)
-  uint32_t tab[kMaxSegments][4]; // decode table per segment (table_byte of codes 0..15, four per word)
+  alignas(16) uint32_t tab[kMaxSegments][4]; // decode table per segment (table_byte of codes 0..15, four per word); read as uint4
 };
+static_assert(offsetof(ChainOp, tab) % 16 == 0, "the kernel loads a segment's table with one 16-byte load");
 
 struct ChainParams {
   const ChainOp* ops;
