@@ -79,6 +79,10 @@ def parse_args():
                         "(programmatic dependent launch)")
     p.add_argument("--no-group", action="store_true",
                    help="one GEMV per projection instead of q/k/v and gate/up as one segmented matrix each")
+    p.add_argument("--no-tp", action="store_true",
+                   help="skip the tensor-parallel leg (the --tp-config step sharded over the torchrun ranks, reported "
+                        "as the line's tp object)")
+    p.add_argument("--tp-config", default="gemma2-27b", help="model of the tensor-parallel leg")
     p.add_argument("--tp", action="store_true",
                    help="tensor-parallel decode step over the torchrun ranks (default config gemma2-27b)")
     return p.parse_args()
@@ -394,7 +398,7 @@ def run_ours(args) -> None:
 
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=120), device_id=torch.device("cuda", local))
+        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=300), device_id=torch.device("cuda", local))
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
 
@@ -622,20 +626,273 @@ def run_ours(args) -> None:
             "other_batches": extra,
             "dense": dense_info,
         }
+    # ----------------------------------------------------------- tensor-parallel leg
+    if not args.no_tp:
+        del stack, xs, outs, e2e_stack, e2e_xs, e2e_outs, mats, dense, host_in, host_out, logits
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+        tp = tp_leg(args, torch, world, rank, local, device)
+        if rank == 0:
+            line["tp"] = tp
+    if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()
 
 
+def tp_leg(args, torch, world, rank, local, device):
+    """The tensor-parallel decode step of --tp-config over all ranks (one rank:
+    the whole model on one GPU), and at N > 1 the same model on rank 0's GPU
+    alone, for the strong-scaling efficiency T1 / (N * TN)."""
+    from se12_b200.shapes import CONFIGS
+
+    shapes = CONFIGS[args.tp_config]
+    sampler = ClockSampler(local)
+    res = tp_measure(args, torch, shapes, world, rank, local, device, sampler=sampler)
+    res["clocks"] = sampler.summary()
+    if world > 1:
+        import torch.distributed as dist
+
+        one = None
+        if rank == 0:
+            one = tp_measure(args, torch, shapes, 1, 0, local, device, check=False)
+        dist.barrier()
+        if rank == 0:
+            res["one_gpu_ms_per_step"] = one["ms_per_step"]
+            res["strong_efficiency"] = one["ms_per_step"] / (world * res["ms_per_step"])
+            res["speedup_vs_one_gpu"] = one["ms_per_step"] / res["ms_per_step"]
+    else:
+        res["one_gpu_ms_per_step"] = res["ms_per_step"]
+        res["strong_efficiency"] = 1.0
+        res["speedup_vs_one_gpu"] = 1.0
+    res["scaling"] = "strong: the same model at every N, Megatron-sharded over the N ranks"
+    return res
+
+
+class TpOp:
+    """One GEMV of a tensor-parallel decode step on this rank: its matrix
+    (the rank's shards of ``names``, one segmented matrix when several), x, y
+    and the collective after it; ``seeds`` regenerate the shards' weights."""
+
+    def __init__(self, names, layer, plan, m, x, y, coll, seeds, dims):
+        self.names, self.layer, self.plan, self.m, self.x, self.y = names, layer, plan, m, x, y
+        self.coll, self.seeds, self.dims = coll, seeds, dims
+
+
+def tp_specs(shapes, group=True):
+    """GEMVs of one layer: tuples of projection names (row-sharded q/k/v and
+    gate/up each as one segmented matrix of their shards when ``group``)."""
+    groups, members = dict(shapes.GROUPS), {m: g for g, ms in shapes.GROUPS for m in ms}
+    specs, done = [], set()
+    for name, _, _, _ in shapes.layer_matrices():
+        if name in done:
+            continue
+        names = groups[members[name]] if (name in members and group) else (name,)
+        specs.append(names)
+        done.update(names)
+    return specs
+
+
+def tp_shard_weights(torch, plan, rows, cols, seed, world, rank, device):
+    """BF16 weights of shard ``rank`` of ``world`` (seeded per shard)."""
+    from se12_b200.sharding import col_range, row_range
+
+    if plan == "rows":
+        r0, r1 = row_range(rows, world, rank)
+        return synthetic_bf16(torch, r1 - r0, cols, seed * 64 + rank, device)
+    c0, c1 = col_range(cols, world, rank)
+    return synthetic_bf16(torch, rows, c1 - c0, seed * 64 + rank, device)
+
+
+def tp_build(torch, shapes, layers, batch, world, rank, device, group=True, lm_head=True):
+    """This rank's part of the Megatron split of every GEMV of a decode step:
+    q/k/v/gate/up by output rows, o/down by input columns (all-reduce after),
+    the LM head by rows (all-gather after). Returns (ops, local bytes)."""
+    from se12_b200.codec import encode_device
+    from se12_b200.device import DeviceSe12Matrix
+    from se12_b200.sharding import megatron_plan
+
+    dims = {name: (rows, cols) for name, rows, cols, _ in shapes.layer_matrices()}
+    order = {name: j for j, (name, _, _, _) in enumerate(shapes.layer_matrices())}
+    gen = torch.Generator(device=device)
+    gen.manual_seed(1)
+    x_full = torch.randn(batch, shapes.hidden, generator=gen, device=device).to(torch.bfloat16)
+    seqs = [(layer, names) for layer in range(layers) for names in tp_specs(shapes, group)]
+    if lm_head:
+        seqs.append((None, ("lm_head",)))
+    ops, local_bytes = [], 0
+    for layer, names in seqs:
+        parts, seeds, ds = [], [], []
+        plan = megatron_plan(names[0])
+        for name in names:
+            rows, cols = dims[name] if layer is not None else shapes.lm_head()[1:3]
+            seed = 1000 * layer + order[name] if layer is not None else 999_999
+            parts.append(encode_device(tp_shard_weights(torch, plan, rows, cols, seed, world, rank, device)))
+            seeds.append(seed)
+            ds.append((rows, cols))
+        m = DeviceSe12Matrix.concatenate(parts) if len(parts) > 1 else parts[0]
+        del parts
+        x = x_full if plan == "rows" else torch.randn(batch, m.cols, generator=gen, device=device).to(torch.bfloat16)
+        y = torch.empty(batch, m.rows, dtype=torch.float32, device=device)
+        coll = "all_reduce" if plan == "cols" else ("all_gather" if names[0] == "lm_head" else None)
+        ops.append(TpOp(names, layer, plan, m, x, y, coll, seeds, ds))
+        local_bytes += m.byte_size + batch * m.cols * 2 + batch * m.rows * 4
+    torch.cuda.synchronize()
+    return ops, local_bytes
+
+
+def tp_time(torch, ops, world, device, steps, warmup, fused_peers=None, logits=None, sampler=None):
+    """Captures the step (GEMVs and collectives) in one CUDA graph, replays
+    it ``warmup`` times, then times ``steps`` replays with CUDA events.
+    Returns (max-over-ranks ms per step, graph)."""
+    import torch.distributed as dist
+
+    from se12_b200.device import gemv_call
+
+    def step():
+        for op in ops:
+            if fused_peers is not None and op.coll == "all_reduce":
+                fused_peers.gemv_allreduce(op.m, op.x, op.y)
+                continue
+            gemv_call(op.m, op.x, op.y)
+            if world > 1 and op.coll == "all_reduce":
+                dist.all_reduce(op.y)
+            elif world > 1 and op.coll == "all_gather":
+                dist.all_gather_into_tensor(logits, op.y)
+
+    stream = torch.cuda.Stream(device)
+    stream.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(stream):
+        step()
+    stream.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step()
+    for _ in range(warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with (sampler if sampler is not None else _Null()):
+        e0.record()  # replay() launches on the current stream
+        for _ in range(steps):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+    t = torch.tensor([e0.elapsed_time(e1)], device=device, dtype=torch.float64)
+    if world > 1:
+        dist.barrier()
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item()) / steps, graph
+
+
+def tp_check(torch, ops, world, rank, device, logits=None, sample_rows=1024):
+    """Checks the outputs the last step left against float64 products of the
+    same BF16 weights (regenerated from the shard seeds), for the first
+    layer's GEMVs and the LM head. Row shards: this rank's rows; column
+    shards: the all-reduced rows (the sum over every rank's shard and x);
+    LM head: a row sample of every rank's part of the all-gathered logits.
+    Returns max |y - y64| / max(|y64|, 1) over the checked outputs and ranks."""
+    import torch.distributed as dist
+
+    def err(y, y64):
+        return float(((y.double() - y64).abs() / y64.abs().clamp_min(1.0)).max())
+
+    worst = 0.0
+    first = [op for op in ops if op.layer == 0] + [op for op in ops if op.names[0] == "lm_head"]
+    for op in first:
+        if op.plan == "cols":
+            xs = [None] * world
+            if world > 1:
+                dist.all_gather_object(xs, op.x.cpu())
+            else:
+                xs = [op.x.cpu()]
+            (rows, cols), seed = op.dims[0], op.seeds[0]
+            y64 = torch.zeros(op.x.shape[0], rows, dtype=torch.float64, device=device)
+            for r in range(world):
+                w = tp_shard_weights(torch, "cols", rows, cols, seed, world, r, device)
+                y64 += xs[r].to(device).double() @ w.double().T
+                del w
+            worst = max(worst, err(op.y, y64))
+        elif op.names[0] == "lm_head":
+            (rows, cols), seed = op.dims[0], op.seeds[0]
+            parts = range(world) if (world > 1 and logits is not None) else [rank]
+            for r in parts:
+                w = tp_shard_weights(torch, "rows", rows, cols, seed, world, r, device)
+                g = torch.Generator(device="cpu").manual_seed(17 + r)
+                ids = torch.randint(0, w.shape[0], (min(sample_rows, w.shape[0]),), generator=g).to(device)
+                y64 = op.x.double() @ w[ids].double().T
+                got = (logits[r] if (world > 1 and logits is not None) else op.y)[:, ids]
+                worst = max(worst, err(got, y64))
+                del w
+        else:
+            y64 = []
+            for (rows, cols), seed in zip(op.dims, op.seeds):
+                w = tp_shard_weights(torch, "rows", rows, cols, seed, world, rank, device)
+                y64.append(op.x.double() @ w.double().T)
+                del w
+            worst = max(worst, err(op.y, torch.cat(y64, dim=1)))
+    t = torch.tensor([worst], device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def tp_measure(args, torch, shapes, world, rank, local, device, sampler=None, check=True):
+    """Builds, times and (optionally) checks the tensor-parallel decode step
+    of ``shapes`` on ``world`` ranks (world 1: the whole model on this GPU).
+    The process group, if any, is already initialised."""
+    import torch.distributed as dist
+
+    from se12_b200.device import device_status
+
+    layers = args.layers if args.layers is not None else shapes.layers
+    batch = args.batch
+    t0 = time.perf_counter()
+    ops, local_bytes = tp_build(torch, shapes, layers, batch, world, rank, device, group=not args.no_group,
+                                lm_head=not args.no_lm_head)
+    setup_s = time.perf_counter() - t0
+    lm_rows = ops[-1].y.shape[1] if not args.no_lm_head else 0
+    logits = torch.empty(world, batch, lm_rows, dtype=torch.float32, device=device) if (lm_rows and world > 1) else None
+    fused = world > 1 and args.tp_allreduce == "fused"
+    peers = None
+    if fused:
+        from se12_b200.peers import PeerGroup
+
+        peers = PeerGroup(rows_cap=max(op.m.rows for op in ops if op.coll == "all_reduce"), device=device)
+    ms, graph = tp_time(torch, ops, world, device, args.steps, args.warmup, fused_peers=peers, logits=logits, sampler=sampler)
+    del graph
+    status = device_status()
+    if status:
+        raise RuntimeError(f"device status word is {status}: a kernel reported an error")
+    max_err = tp_check(torch, ops, world, rank, device, logits=logits) if check else None
+    total = torch.tensor([float(local_bytes)], device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(total)
+    if peers is not None:
+        peers.close()
+    weights = layers * shapes.weights_per_layer + (0 if args.no_lm_head else shapes.vocab * shapes.hidden)
+    res = {
+        "config": shapes.name, "layers": layers, "batch": batch, "n_gpus": world, "weights": weights,
+        "gemvs_per_step": len(ops), "bytes_per_step": float(total.item()), "ms_per_step": ms,
+        "gbs": float(total.item()) / (ms * 1e-3) / 1e9, "tok_s": batch / (ms * 1e-3),
+        "allreduce": ("fused into the GEMV over peer memory" if fused else "NCCL") if world > 1 else None,
+        "max_rel_err_vs_fp64": max_err, "setup_seconds": setup_s,
+    }
+    del ops, logits
+    torch.cuda.empty_cache()
+    return res
+
+
 def run_tp(args) -> None:
-    """Tensor-parallel decode step (baseline configs 2-4): every rank holds
-    its Megatron shards of every matrix -- q/k/v/gate/up by output rows, o
-    and down by input columns followed by an NCCL all-reduce of the fp32
-    partial sums, the LM head by rows followed by an all-gather of the
-    logits -- and replays one CUDA graph of the step's GEMVs and
-    collectives. value = the full model's SE12 bytes (all ranks' shards) per
-    step / the slowest rank's step time: strong scaling at a fixed model."""
+    """Tensor-parallel decode step alone (baseline configs 2-4; default
+    gemma2-27b): every rank holds its Megatron shards of every matrix and
+    replays one CUDA graph of the step's GEMVs and collectives. value = the
+    full model's SE12 bytes (all ranks' shards) per step / the slowest rank's
+    step time: strong scaling at a fixed model."""
     import datetime
 
     import torch
@@ -646,154 +903,37 @@ def run_tp(args) -> None:
     torch.cuda.set_device(device)
     if world > 1:
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
     from se12_b200 import _build
-    from se12_b200.codec import encode_device
-    from se12_b200.device import device_status, gemv_call
     from se12_b200.shapes import CONFIGS
-    from se12_b200.sharding import col_range, megatron_plan, row_range
 
     if rank == 0:
         _build.build()
     if world > 1:
         dist.barrier()
     shapes = CONFIGS[args.config if args.config != "gemma2-2b" else "gemma2-27b"]
-    layers = args.layers if args.layers is not None else shapes.layers
-    batch = args.batch
-    from se12_b200.device import DeviceSe12Matrix
-
-    # (names, kind) per GEMV of a layer: row-sharded projections that read the
-    # same input (q/k/v, gate/up) are one segmented matrix of their shards
-    groups, members = dict(shapes.GROUPS), {m: g for g, ms in shapes.GROUPS for m in ms}
-    specs, done = [], set()
-    for name, _, _, _ in shapes.layer_matrices():
-        if name in done:
-            continue
-        names = groups[members[name]] if (name in members and not args.no_group) else (name,)
-        specs.append(names)
-        done.update(names)
-    dims = {name: (rows, cols) for name, rows, cols, _ in shapes.layer_matrices()}
-    t_setup = time.perf_counter()
-    gen = torch.Generator(device=device)
-    gen.manual_seed(1)
-    x_full = torch.randn(batch, shapes.hidden, generator=gen, device=device).to(torch.bfloat16)
-    ops = []  # (matrix, x, y, collective) in step order
-    local_bytes = 0
-    plan_of = {}
-
-    def shard(name, rows, cols, seed):
-        plan = megatron_plan(name)
-        if plan == "rows":
-            r0, r1 = row_range(rows, world, rank)
-            return encode_device(synthetic_bf16(torch, r1 - r0, cols, seed * 64 + rank, device)), plan
-        c0, c1 = col_range(cols, world, rank)
-        return encode_device(synthetic_bf16(torch, rows, c1 - c0, seed * 64 + rank, device)), plan
-
-    seqs = [(layer, names) for layer in range(layers) for names in specs]
-    if not args.no_lm_head:
-        seqs.append((None, ("lm_head",)))
-    order = {name: j for j, (name, _, _, _) in enumerate(shapes.layer_matrices())}
-    for layer, names in seqs:
-        parts = []
-        for name in names:
-            rows, cols = dims[name] if layer is not None else shapes.lm_head()[1:3]
-            seed = 1000 * layer + order[name] if layer is not None else 999_999
-            m, plan = shard(name, rows, cols, seed)
-            parts.append(m)
-        m = DeviceSe12Matrix.concatenate(parts) if len(parts) > 1 else parts[0]
-        del parts
-        if plan == "rows":
-            x = x_full
-        else:
-            x = torch.randn(batch, m.cols, generator=gen, device=device).to(torch.bfloat16)
-        y = torch.empty(batch, m.rows, dtype=torch.float32, device=device)
-        coll = "all_reduce" if plan == "cols" else ("all_gather" if names[0] == "lm_head" else None)
-        ops.append((m, x, y, coll))
-        local_bytes += m.byte_size + batch * m.cols * 2 + batch * m.rows * 4
-    torch.cuda.synchronize()
-    setup_s = time.perf_counter() - t_setup
-    lm_rows = ops[-1][2].shape[1] if not args.no_lm_head else 0
-    logits = torch.empty(world, batch, lm_rows, dtype=torch.float32, device=device) if lm_rows else None
-    fused = world > 1 and args.tp_allreduce == "fused"
-    peers = None
-    if fused:
-        from se12_b200.peers import PeerGroup
-
-        peers = PeerGroup(rows_cap=max(m.rows for m, _, _, coll in ops if coll == "all_reduce"), device=device)
-
-    def step():
-        for m, x, y, coll in ops:
-            if fused and coll == "all_reduce":
-                peers.gemv_allreduce(m, x, y)
-                continue
-            gemv_call(m, x, y)
-            if world > 1 and coll == "all_reduce":
-                dist.all_reduce(y)
-            elif world > 1 and coll == "all_gather":
-                dist.all_gather_into_tensor(logits, y)
-
-    stream = torch.cuda.Stream(device)
-    stream.wait_stream(torch.cuda.current_stream(device))
-    with torch.cuda.stream(stream):
-        step()
-    stream.synchronize()
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph, stream=stream):
-        step()
-    for _ in range(args.warmup):
-        graph.replay()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
     sampler = ClockSampler(local)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with sampler:
-        e0.record()  # replay() launches on the current stream
-        for _ in range(args.steps):
-            graph.replay()
-        e1.record()
-        torch.cuda.synchronize()
-    elapsed = e0.elapsed_time(e1)
-    total_bytes = torch.tensor([float(local_bytes)], device=device, dtype=torch.float64)
-    t = torch.tensor([elapsed], device=device, dtype=torch.float64)
-    if world > 1:
-        dist.barrier()
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        dist.all_reduce(total_bytes)
-    ms = float(t.item()) / args.steps
-    status = device_status()
-    if status:
-        raise RuntimeError(f"device status word is {status}: a kernel reported an error")
+    res = tp_measure(args, torch, shapes, world, rank, local, device, sampler=sampler)
     if rank == 0:
-        value = float(total_bytes.item()) / (ms * 1e-3) / 1e9
-        weights = layers * shapes.weights_per_layer + (0 if args.no_lm_head else shapes.vocab * shapes.hidden)
+        fused = res["allreduce"] is not None and res["allreduce"].startswith("fused")
         line = {
-            "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic",
-            "config": {"workload": f"{shapes.name} tensor-parallel decode-step GEMV set: {layers} layers x 7 + lm_head, "
-                       f"batch {batch}", "batch": batch, "weights": weights, "gemvs_per_step": len(ops),
-                       "grouping": "none" if args.no_group else "row shards of q/k/v and of gate/up as one segmented matrix each",
-                       "bytes_per_step": float(total_bytes.item()),
+            "metric": METRIC, "value": res["gbs"], "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": res["ms_per_step"], "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": f"{shapes.name} tensor-parallel decode-step GEMV set: {res['layers']} layers + lm_head, "
+                       f"batch {res['batch']}", "batch": res["batch"], "weights": res["weights"],
+                       "gemvs_per_step": res["gemvs_per_step"], "bytes_per_step": res["bytes_per_step"],
                        "parallelism": f"tp{world}: q/k/v/gate/up by rows, o/down by columns + "
                        + ("all-reduce fused into the GEMV (peer memory)" if fused else "NCCL all-reduce")
-                       + ", lm_head by rows + NCCL all-gather; one CUDA graph per step", "setup_seconds": setup_s},
-            "tok_s": batch / (ms * 1e-3),
-            "per_gpu_gbs": value / world,
-            "nccl_collectives_per_step": ((0 if fused else 2 * layers) + (0 if args.no_lm_head else 1)) if world > 1 else 0,
-            "fused_allreduces_per_step": 2 * layers if fused else 0,
-            "allreduce": ("fused into the GEMV over peer memory" if fused else "NCCL") if world > 1 else None,
-            "clocks": sampler.summary(),
+                       + ", lm_head by rows + NCCL all-gather; one CUDA graph per step",
+                       "setup_seconds": res["setup_seconds"]},
+            "tok_s": res["tok_s"], "per_gpu_gbs": res["gbs"] / world, "allreduce": res["allreduce"],
+            "max_rel_err_vs_fp64": res["max_rel_err_vs_fp64"], "clocks": sampler.summary(),
         }
         print(json.dumps(line), flush=True)
-    del graph
-    if peers is not None:
-        peers.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
-
 
 def run_offload(args) -> None:
     """Weight offload (the reference's weight-offload feature, spec.md

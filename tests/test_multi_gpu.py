@@ -1,6 +1,8 @@
-"""Tensor-parallel SE12 layers on real GPUs over NCCL (two ranks, one GPU
-each): row shards + all-gather and column shards + all-reduce reproduce the
-fp64 oracle within the GEMV tolerance. Skipped with fewer than two GPUs.
+"""Tensor-parallel SE12 layers on real GPUs (2, 4 and 8 ranks, one GPU
+each): row shards + NCCL all-gather, column shards + NCCL all-reduce, and
+column shards whose all-reduce is fused into the GEMV reproduce the fp64
+oracle within the GEMV tolerance. A world size is skipped when fewer GPUs
+are visible.
 """
 
 from __future__ import annotations
@@ -56,13 +58,22 @@ def _rank_main(rank, world, port, result_path):
         dist.destroy_process_group()
 
 
-@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_row_and_column_sharded_layers_over_nccl(tmp_path):
+WORLDS = (2, 4, 8)
+
+
+def _need(world):
+    if not torch.cuda.is_available() or torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+
+
+@pytest.mark.parametrize("world", WORLDS)
+def test_row_and_column_sharded_layers_over_nccl(tmp_path, world):
     import torch.multiprocessing as mp
 
+    _need(world)
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
-    mp.spawn(_rank_main, args=(2, _free_port(), str(tmp_path / "errs")), nprocs=2, join=True)
-    for r in range(2):
+    mp.spawn(_rank_main, args=(world, _free_port(), str(tmp_path / "errs")), nprocs=world, join=True)
+    for r in range(world):
         errs = torch.load(tmp_path / f"errs.{r}")
         assert max(errs) <= TOLERANCE, errs
 
@@ -133,16 +144,17 @@ def _allreduce_main(rank, world, port, result_path):
         dist.destroy_process_group()
 
 
-@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_fused_gemv_allreduce_over_peer_memory(tmp_path):
+@pytest.mark.parametrize("world", WORLDS)
+def test_fused_gemv_allreduce_over_peer_memory(tmp_path, world):
     """Column shards whose GEMV and all-reduce are one kernel (peer memory,
     no NCCL on the data path): within 1e-3 of the fp64 oracle, the same bits
-    on both ranks, over calls in a row and from a replayed CUDA graph."""
+    on every rank, over calls in a row and from a replayed CUDA graph."""
     import torch.multiprocessing as mp
 
+    _need(world)
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
-    mp.spawn(_allreduce_main, args=(2, _free_port(), str(tmp_path / "ar")), nprocs=2, join=True)
-    for r in range(2):
+    mp.spawn(_allreduce_main, args=(world, _free_port(), str(tmp_path / "ar")), nprocs=world, join=True)
+    for r in range(world):
         res = torch.load(tmp_path / f"ar.{r}")
         assert res["status"] == 0, res
         assert max(res["errs"]) <= TOLERANCE, res["errs"]
