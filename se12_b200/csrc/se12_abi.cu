@@ -767,6 +767,7 @@ int se12_device_status(unsigned* status, int clear) {
 // them to a caller buffer on the device and zeroes the caller's workspace.
 struct se12_chain {
   std::vector<se12::ChainOp> ops;
+  std::vector<int> starts;  // [ops][sm_count + 1] CTA tile ranges (made at upload)
   int batch = 1;
   bool dense = false;
   int device = 0;
@@ -787,14 +788,14 @@ constexpr size_t kChainSmemLimit = 227 * 1024;
 constexpr int kChainMinConsumers = 12;
 
 // x budget: what is left of shared memory with kChainMinConsumers warps.
-size_t chain_x_budget(bool dense) {
-  return kChainSmemLimit - se12::chain_smem_bytes(dense, kChainMinConsumers, 0);
+size_t chain_x_budget(bool dense, int batch) {
+  return kChainSmemLimit - se12::chain_smem_bytes(dense, kChainMinConsumers, 0, batch);
 }
 
 // Consumer warps that fit beside an x buffer of x_bytes.
-int chain_consumers(bool dense, int x_bytes) {
+int chain_consumers(bool dense, int x_bytes, int batch) {
   int c = se12::kChainMaxWarps;
-  while (c > 1 && se12::chain_smem_bytes(dense, c, x_bytes) > kChainSmemLimit) --c;
+  while (c > 1 && se12::chain_smem_bytes(dense, c, x_bytes, batch) > kChainSmemLimit) --c;
   return c;
 }
 
@@ -802,7 +803,7 @@ int chain_x_stride(int width_tiles) { return width_tiles * 512 + 64; }
 
 // Tile columns per op so that batch rows of x fit the budget.
 int chain_split_width(bool dense, int batch, int tile_cols) {
-  const size_t budget = chain_x_budget(dense);
+  const size_t budget = chain_x_budget(dense, batch);
   int w = tile_cols;
   while (w > 1 && static_cast<size_t>(batch) * chain_x_stride(w) > budget) w = (w + 1) / 2;
   return w;
@@ -812,15 +813,28 @@ struct ChainLayout {
   size_t done, gen, rowcnt, partials, total;
 };
 
-ChainLayout chain_layout(int n_ops, long long workers) {
+// Workspace: done[n_ops] | gen[2] | rowcnt[n_ops][grid][2] | partials[grid][2][256]
+ChainLayout chain_layout(int n_ops, int grid) {
   ChainLayout l{};
   auto up = [](size_t v) { return (v + 255) / 256 * 256; };
   l.done = 0;
   l.gen = up(static_cast<size_t>(n_ops) * 4);
   l.rowcnt = l.gen + 256;
-  l.partials = up(l.rowcnt + static_cast<size_t>(n_ops) * workers * 4);
-  l.total = up(l.partials + static_cast<size_t>(workers) * 2 * 256 * 4);
+  l.partials = up(l.rowcnt + static_cast<size_t>(n_ops) * grid * 2 * 4);
+  l.total = up(l.partials + static_cast<size_t>(grid) * 2 * 256 * 4);
   return l;
+}
+
+// The tile range of every CTA for one op (grid + 1 boundaries): whole tile
+// rows per CTA when that costs no more than an even split of the tiles (the
+// longest warp part in tiles, plus 2 for the cross-CTA sum a row split
+// needs). Rows then never cross CTAs and are summed in shared memory.
+void chain_starts(const se12::ChainOp& op, int grid, int consumers, int* st) {
+  const long long W = op.k1 - op.k0, T = op.tiles, R = T / W, G = grid, C = consumers;
+  const long long cost_rows = (((R + G - 1) / G) * W + C - 1) / C;
+  const long long cost_split = ((T + G - 1) / G + C - 1) / C + 2;
+  const bool by_rows = cost_rows <= cost_split;
+  for (long long c = 0; c <= G; ++c) st[c] = static_cast<int>(by_rows ? (R * c / G) * W : T * c / G);
 }
 
 int chain_check_open(se12_chain* c) {
@@ -1006,20 +1020,21 @@ int se12_chain_add_dense(se12_chain* c, const uint16_t* w, int rows, int cols, i
 
 int se12_chain_ops(const se12_chain* c) { return c ? static_cast<int>(c->ops.size()) : 0; }
 
+// Descriptors: the ops, then every op's CTA boundaries (int32 [n_ops][grid + 1]).
 size_t se12_chain_descriptor_bytes(const se12_chain* c) {
-  return c ? c->ops.size() * sizeof(se12::ChainOp) : 0;
+  return c ? c->ops.size() * (sizeof(se12::ChainOp) + static_cast<size_t>(c->sm_count + 1) * sizeof(int)) : 0;
 }
 
 static void chain_finalize(se12_chain* c) {
   c->x_bytes = c->batch * c->x_stride_max;
-  c->consumers = chain_consumers(c->dense, c->x_bytes);
+  c->consumers = chain_consumers(c->dense, c->x_bytes, c->batch);
 }
 
 size_t se12_chain_workspace_bytes(const se12_chain* c) {
   if (!c || c->ops.empty()) return 0;
   se12_chain tmp = *c;
   chain_finalize(&tmp);
-  return chain_layout(static_cast<int>(c->ops.size()), static_cast<long long>(c->sm_count) * tmp.consumers).total;
+  return chain_layout(static_cast<int>(c->ops.size()), c->sm_count).total;
 }
 
 int se12_chain_upload(se12_chain* c, void* descriptors, void* workspace, size_t workspace_bytes, void* stream) {
@@ -1028,13 +1043,19 @@ int se12_chain_upload(se12_chain* c, void* descriptors, void* workspace, size_t 
   if (!descriptors || (reinterpret_cast<uintptr_t>(descriptors) & 63u))
     return fail(SE12_ERR_MISALIGNED, "the descriptor buffer must be 64-byte aligned");
   chain_finalize(c);
-  const ChainLayout l = chain_layout(static_cast<int>(c->ops.size()), static_cast<long long>(c->sm_count) * c->consumers);
+  const ChainLayout l = chain_layout(static_cast<int>(c->ops.size()), c->sm_count);
   if (!workspace || workspace_bytes < l.total || (reinterpret_cast<uintptr_t>(workspace) & 255u))
     return fail(SE12_ERR_WORKSPACE_TOO_SMALL, "chain workspace needs " + std::to_string(l.total) +
                                                   " bytes, 256-byte aligned");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  cudaError_t err = cudaMemcpyAsync(descriptors, c->ops.data(), c->ops.size() * sizeof(se12::ChainOp),
-                                    cudaMemcpyHostToDevice, s);
+  const size_t ops_bytes = c->ops.size() * sizeof(se12::ChainOp);
+  c->starts.assign(c->ops.size() * static_cast<size_t>(c->sm_count + 1), 0);
+  for (size_t j = 0; j < c->ops.size(); ++j)
+    chain_starts(c->ops[j], c->sm_count, c->consumers, c->starts.data() + j * static_cast<size_t>(c->sm_count + 1));
+  cudaError_t err = cudaMemcpyAsync(descriptors, c->ops.data(), ops_bytes, cudaMemcpyHostToDevice, s);
+  if (err != cudaSuccess) return cuda_fail(err, "chain descriptor copy");
+  err = cudaMemcpyAsync(static_cast<char*>(descriptors) + ops_bytes, c->starts.data(), c->starts.size() * sizeof(int),
+                        cudaMemcpyHostToDevice, s);
   if (err != cudaSuccess) return cuda_fail(err, "chain descriptor copy");
   err = cudaMemsetAsync(workspace, 0, l.total, s);
   if (err != cudaSuccess) return cuda_fail(err, "chain workspace clear");
@@ -1046,7 +1067,7 @@ int se12_chain_upload(se12_chain* c, void* descriptors, void* workspace, size_t 
 
 int se12_chain_reset(const se12_chain* c, void* stream) {
   if (!c || !c->uploaded) return fail(SE12_ERR_INVALID_ARGUMENT, "chain not uploaded");
-  const ChainLayout l = chain_layout(static_cast<int>(c->ops.size()), static_cast<long long>(c->sm_count) * c->consumers);
+  const ChainLayout l = chain_layout(static_cast<int>(c->ops.size()), c->sm_count);
   cudaError_t err = cudaMemsetAsync(c->ws_dev, 0, l.total, static_cast<cudaStream_t>(stream));
   if (err != cudaSuccess) return cuda_fail(err, "chain workspace clear");
   return SE12_OK;
@@ -1058,7 +1079,7 @@ int se12_chain_info(const se12_chain* c, int* grid, int* consumers, int* smem_by
   chain_finalize(&tmp);
   *grid = tmp.sm_count;
   *consumers = tmp.consumers;
-  *smem_bytes = static_cast<int>(se12::chain_smem_bytes(tmp.dense, tmp.consumers, tmp.x_bytes));
+  *smem_bytes = static_cast<int>(se12::chain_smem_bytes(tmp.dense, tmp.consumers, tmp.x_bytes, tmp.batch));
   *ops = static_cast<int>(tmp.ops.size());
   return SE12_OK;
 }
@@ -1070,11 +1091,11 @@ int se12_chain_run(const se12_chain* c, void* stream) {
   if (err != cudaSuccess) return cuda_fail(err, "cudaGetDevice");
   if (device != c->device) return fail(SE12_ERR_INVALID_ARGUMENT, "the current device is not the chain's device");
   const int n = static_cast<int>(c->ops.size());
-  const long long workers = static_cast<long long>(c->sm_count) * c->consumers;
-  const ChainLayout l = chain_layout(n, workers);
+  const ChainLayout l = chain_layout(n, c->sm_count);
   char* ws = static_cast<char*>(c->ws_dev);
   se12::ChainParams p{};
   p.ops = static_cast<const se12::ChainOp*>(c->desc_dev);
+  p.starts = reinterpret_cast<const int*>(static_cast<const char*>(c->desc_dev) + c->ops.size() * sizeof(se12::ChainOp));
   p.n_ops = n;
   p.batch = c->batch;
   p.consumers = c->consumers;
@@ -1086,7 +1107,7 @@ int se12_chain_run(const se12_chain* c, void* stream) {
   p.rowcnt = reinterpret_cast<unsigned*>(ws + l.rowcnt);
   p.partials = reinterpret_cast<float*>(ws + l.partials);
   p.peers = c->peers;
-  const size_t smem = se12::chain_smem_bytes(c->dense, c->consumers, c->x_bytes);
+  const size_t smem = se12::chain_smem_bytes(c->dense, c->consumers, c->x_bytes, c->batch);
   err = se12::launch_chain(c->dense, p, c->sm_count, smem, static_cast<cudaStream_t>(stream));
   if (err != cudaSuccess) return cuda_fail(err, "se12_chain_run launch");
   return SE12_OK;

@@ -10,13 +10,16 @@
 // stream of the next GEMV is already in flight.
 //
 // Work split. Each GEMV's tiles (16 x 256 weights, tile-row-major order) are
-// cut into equal contiguous runs, one per consumer warp of the whole grid
-// (stream-K over grid x C warps). A warp accumulates its tiles row by row in
-// mma.sync accumulators. A tile row held entirely by one warp is written to
-// y by that warp. A row shared by several warps is published by each as a
-// partial (global memory); the warp that arrives last on the row's counter
-// sums all partials in worker order -- deterministic, no floating-point
-// atomics, and nobody spins -- and writes y.
+// cut into one contiguous range per CTA (a host table), whole tile rows per
+// CTA unless an even split of the tiles is clearly shorter; each CTA's range
+// is cut evenly over its consumer warps. A warp accumulates its tiles row by
+// row in mma.sync accumulators. A tile row held entirely by one warp is
+// written to y by that warp. A row shared by several warps of the CTA is
+// stored by each as a share in shared memory; the warp that arrives last on
+// the row's counter (tiles summed so far) adds the shares in warp order --
+// deterministic, no floating-point atomics, nobody waits -- and writes y.
+// Only when the split cuts a row between CTAs do the CTAs' sums of that row
+// go through global memory, added by the last CTA to arrive in CTA order.
 //
 // Pipeline. Every consumer warp owns kChainSlots slots of shared memory and
 // issues its own TMA loads into them (one lane): the sm and ec bytes of one
@@ -162,14 +165,24 @@ __device__ __forceinline__ unsigned atom_add_acq_rel_gpu_u32(unsigned* p, unsign
 
 __device__ __forceinline__ void fence_proxy_async_all() { asm volatile("fence.proxy.async;" ::: "memory"); }
 
-// First op-linear tile of worker u (of W workers) for an op of T tiles.
-__device__ __forceinline__ int run_start(long long T, long long u, long long W) {
-  return static_cast<int>(T * u / W);
-}
+// A CTA's range of n tiles is split over its C consumer warps: warp w holds
+// local tiles [n w / C, n (w + 1) / C).
+__device__ __forceinline__ int part_start(int n, int w, int C) { return n * w / C; }
 
-// Worker whose run holds op-linear tile i.
-__device__ __forceinline__ int run_owner(long long i, long long T, long long W) {
-  return static_cast<int>(((i + 1) * W - 1) / T);
+// Warp whose part holds local tile t (t < n).
+__device__ __forceinline__ int part_owner(int t, int n, int C) { return ((t + 1) * C - 1) / n; }
+
+// CTA whose range holds op tile i: the largest c with starts[c] <= i (an
+// empty range never qualifies as the largest, its successor starts at the
+// same tile).
+__device__ __forceinline__ int cta_owner(const int* st, int G, int i) {
+  int lo = 0, hi = G - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (__ldg(st + mid) <= i) lo = mid;
+    else hi = mid - 1;
+  }
+  return lo;
 }
 
 // ---------------------------------------------------------------- kernel
@@ -178,19 +191,25 @@ template <int NB, bool RAW>
 __global__ void __launch_bounds__((kChainMaxWarps + 1) * 32, 1) chain_kernel(const __grid_constant__ ChainParams p) {
   constexpr int D = kChainSlots;
   constexpr uint32_t SLOT = RAW ? kChainSlotRaw : kChainSlotSe12;
+  constexpr int PB = 16 * 8 * NB;  // floats of one partial row block: [8 NB batch columns][16 rows]
   extern __shared__ __align__(1024) uint8_t smem[];
   const uint32_t pad = (1024u - (smem_addr(smem) & 1023u)) & 1023u;
   const int C = p.consumers;
   const int B = p.batch;
   const int nops = p.n_ops;
+  const int G = gridDim.x;
+  const int cta = blockIdx.x;
   const uint32_t o_slots = pad;
   const uint32_t o_rec = o_slots + static_cast<uint32_t>(C * D) * SLOT;
   const uint32_t o_x = o_rec + (RAW ? 0u : static_cast<uint32_t>(C * D) * 64u);
-  const uint32_t o_bar = (o_x + static_cast<uint32_t>(p.x_bytes) + 7u) & ~7u;
+  const uint32_t o_part = (o_x + static_cast<uint32_t>(p.x_bytes) + 15u) & ~15u;
+  const uint32_t o_bar = o_part + static_cast<uint32_t>(C * 2 * PB) * 4u;
+  float* const part_s = reinterpret_cast<float*>(smem + o_part);    // [C][2][PB] warps' shares of shared rows
   uint64_t* const full = reinterpret_cast<uint64_t*>(smem + o_bar);  // [C * D] slot loaded
   uint64_t* const xbar = full + C * D;                               // x copy landed (control warp)
   uint64_t* const xready = xbar + 1;                                  // x of the current op ready
   unsigned* const opcnt = reinterpret_cast<unsigned*>(xready + 1);    // [2] consumer warps done with op j (j & 1)
+  unsigned* const rowcnt_s = opcnt + 2;                               // [C][2] tiles summed of a row shared by warps
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (tid == 0) {
@@ -198,6 +217,7 @@ __global__ void __launch_bounds__((kChainMaxWarps + 1) * 32, 1) chain_kernel(con
     mbar_init(xbar, 1);
     mbar_init(xready, 1);
     opcnt[0] = opcnt[1] = 0u;
+    for (int i = 0; i < 2 * C; ++i) rowcnt_s[i] = 0u;
     fence_barrier_init();
   }
   __syncthreads();
@@ -248,8 +268,6 @@ __global__ void __launch_bounds__((kChainMaxWarps + 1) * 32, 1) chain_kernel(con
     }
   } else if (warp < C) {
     // ------------------------------------------------------------ consumer warps
-    const long long u = static_cast<long long>(blockIdx.x) * C + warp;  // worker id
-    const long long GC = static_cast<long long>(gridDim.x) * C;
     const int g = lane >> 2, t = lane & 3;
     const uint32_t my_slots = o_slots + static_cast<uint32_t>(warp * D) * SLOT;
     const uint32_t my_recs = o_rec + static_cast<uint32_t>(warp * D) * 64u;
@@ -277,13 +295,18 @@ __global__ void __launch_bounds__((kChainMaxWarps + 1) * 32, 1) chain_kernel(con
 
     // ---- issue side: this warp's tile sequence across ops, kept D tiles
     // ahead of consumption
+    // this warp's part of op j: tiles [a, b) of the CTA's range
+    auto part_of = [&](int j, int& a, int& b) {
+      const int* st = p.starts + static_cast<size_t>(j) * (G + 1);
+      const int s = __ldg(st + cta), n = __ldg(st + cta + 1) - s;
+      a = s + part_start(n, warp, C);
+      b = s + part_start(n, warp + 1, C);
+    };
     int iop = 0, ii = 0, iend = 0;
     auto seek = [&](int from) {
       iop = from;
       while (iop < nops) {
-        const long long T = p.ops[iop].tiles;
-        ii = run_start(T, u, GC);
-        iend = run_start(T, u + 1, GC);
+        part_of(iop, ii, iend);
         if (ii < iend) return;
         ++iop;
       }
@@ -333,8 +356,9 @@ __global__ void __launch_bounds__((kChainMaxWarps + 1) * 32, 1) chain_kernel(con
 
     for (int j = 0; j < nops; ++j) {
       const ChainOp* op = p.ops + j;
-      const long long T = op->tiles;
-      const int a = run_start(T, u, GC), b = run_start(T, u + 1, GC);
+      const int* const st = p.starts + static_cast<size_t>(j) * (G + 1);
+      const int cs = __ldg(st + cta), n = __ldg(st + cta + 1) - cs;  // this CTA's tiles [cs, cs + n)
+      const int a = cs + part_start(n, warp, C), b = cs + part_start(n, warp + 1, C);
       if (ok) ok = __all_sync(0xFFFFFFFFu, mbar_wait(xready, static_cast<uint32_t>(j) & 1u));
       if (a < b && ok) {
         const int k0 = op->k0;
@@ -359,6 +383,7 @@ __global__ void __launch_bounds__((kChainMaxWarps + 1) * 32, 1) chain_kernel(con
           const int s = static_cast<int>(consumed % D);
           const uint32_t par = (consumed / D) & 1u;
           if (ok) ok = __all_sync(0xFFFFFFFFu, mbar_wait(&my_full[s], par));
+          const bool landed = ok;  // the slot's copy arrived (and counts as consumed below)
           if (ok) {
             const uint32_t sb = my_slots + s * SLOT;
             const uint32_t xt = x_lane + static_cast<uint32_t>(kt_local) * 512u;
@@ -478,7 +503,7 @@ __global__ void __launch_bounds__((kChainMaxWarps + 1) * 32, 1) chain_kernel(con
           // slot s is read: refill it with the next tile of this warp's sequence
           __syncwarp();
           fence_proxy_async_shared();
-          ++consumed;
+          if (landed) ++consumed;
           if (ok) issue_next();
 
           // ---- row end: the tile row ends here, or this warp's run does
@@ -491,55 +516,104 @@ __global__ void __launch_bounds__((kChainMaxWarps + 1) * 32, 1) chain_kernel(con
                 v[nb][q] = acc[0][nb][q] + acc[1][nb][q];
                 acc[0][nb][q] = acc[1][nb][q] = 0.f;
               }
-            const bool whole = (seg_first - row * W == 0) && (kt_local == W - 1);
+            const int row_lo = row * W, row_hi = row_lo + W;
+            const bool whole = (seg_first == row_lo) && (i + 1 == row_hi);
             bool emit = ok;
             if (!whole && ok) {
-              // shared row: publish this warp's partial, count it; the last
-              // of the row's workers to arrive sums them in worker order
-              const int which = (row == a / W) ? 0 : 1;
-              float* part = p.partials + (static_cast<size_t>(u) * 2 + which) * 256;
+              // A row shared by warps: each stores its share in shared
+              // memory and adds its tile count to the row's counter; the last
+              // to arrive sums the shares in warp order (deterministic, no
+              // float atomics, nobody waits).
+              const int which = (row == a / W) ? 0 : 1;  // this warp's first row or its last
+              float* mine = part_s + (warp * 2 + which) * PB;
 #pragma unroll
               for (int nb = 0; nb < NB; ++nb) {
                 const int b0 = nb * 8 + 2 * t;
-                part[b0 * 16 + g] = v[nb][0];
-                part[(b0 + 1) * 16 + g] = v[nb][1];
-                part[b0 * 16 + g + 8] = v[nb][2];
-                part[(b0 + 1) * 16 + g + 8] = v[nb][3];
+                mine[b0 * 16 + g] = v[nb][0];
+                mine[(b0 + 1) * 16 + g] = v[nb][1];
+                mine[b0 * 16 + g + 8] = v[nb][2];
+                mine[(b0 + 1) * 16 + g + 8] = v[nb][3];
               }
-              __threadfence();
-              __syncwarp();
-              const int u_first = run_owner(static_cast<long long>(row) * W, T, GC);
-              const int u_last = run_owner(static_cast<long long>(row + 1) * W - 1, T, GC);
-              // the counter adds up tiles, not workers: when the op has fewer
-              // tiles than the grid has warps, workers with empty runs lie
-              // between the row's holders and never arrive
-              unsigned* rc = p.rowcnt + static_cast<size_t>(j) * GC + u_first;
+              const int lo = max(row_lo, cs), hi = min(row_hi, cs + n);  // the row's tiles in this CTA
+              const int wf = part_owner(lo - cs, n, C);                   // the first warp holding one
+              // the row is wf's first or last row: (wf, 0) or (wf, 1) names it
+              const int kf = ((cs + part_start(n, wf, C)) / W == row) ? 0 : 1;
               const unsigned held = static_cast<unsigned>(i + 1 - seg_first);
+              __syncwarp();
               unsigned old = 0;
-              if (lane == 0) old = atom_add_acq_rel_gpu_u32(rc, held);
+              if (lane == 0) {
+                __threadfence_block();
+                old = atomicAdd(&rowcnt_s[wf * 2 + kf], held);
+                __threadfence_block();
+              }
               old = __shfl_sync(0xFFFFFFFFu, old, 0);
-              emit = (old + held == static_cast<unsigned>(W));
+              emit = (old + held == static_cast<unsigned>(hi - lo));
               if (emit) {
-                __threadfence();
 #pragma unroll
                 for (int nb = 0; nb < NB; ++nb)
 #pragma unroll
                   for (int q = 0; q < 4; ++q) v[nb][q] = 0.f;
-                for (int w = u_first; w <= u_last; ++w) {
-                  const int ws = run_start(T, w, GC);
-                  if (ws == run_start(T, w + 1, GC)) continue;  // empty run: no partial
-                  const int wrow = ws / W;
-                  const float* src = p.partials + (static_cast<size_t>(w) * 2 + (wrow == row ? 0 : 1)) * 256;
+                const int wl = part_owner(hi - 1 - cs, n, C);
+                for (int w = wf; w <= wl; ++w) {
+                  const int ws = cs + part_start(n, w, C);
+                  if (ws == cs + part_start(n, w + 1, C)) continue;  // empty part
+                  const float* src = part_s + (w * 2 + ((ws / W == row) ? 0 : 1)) * PB;
 #pragma unroll
                   for (int nb = 0; nb < NB; ++nb) {
                     const int b0 = nb * 8 + 2 * t;
-                    v[nb][0] += __ldcg(src + b0 * 16 + g);
-                    v[nb][1] += __ldcg(src + (b0 + 1) * 16 + g);
-                    v[nb][2] += __ldcg(src + b0 * 16 + g + 8);
-                    v[nb][3] += __ldcg(src + (b0 + 1) * 16 + g + 8);
+                    v[nb][0] += src[b0 * 16 + g];
+                    v[nb][1] += src[(b0 + 1) * 16 + g];
+                    v[nb][2] += src[b0 * 16 + g + 8];
+                    v[nb][3] += src[(b0 + 1) * 16 + g + 8];
                   }
                 }
-                if (lane == 0) *rc = 0u;  // ready for the next launch
+                if (lane == 0) rowcnt_s[wf * 2 + kf] = 0u;  // ready for the next op
+                if (lo != row_lo || hi != row_hi) {
+                  // the row continues in other CTAs (a stream-K split of the
+                  // op): publish this CTA's sum; the last CTA to arrive adds
+                  // the CTAs' sums in CTA order
+                  float* gp = p.partials + (static_cast<size_t>(cta) * 2 + ((row == cs / W) ? 0 : 1)) * 256;
+#pragma unroll
+                  for (int nb = 0; nb < NB; ++nb) {
+                    const int b0 = nb * 8 + 2 * t;
+                    gp[b0 * 16 + g] = v[nb][0];
+                    gp[(b0 + 1) * 16 + g] = v[nb][1];
+                    gp[b0 * 16 + g + 8] = v[nb][2];
+                    gp[(b0 + 1) * 16 + g + 8] = v[nb][3];
+                  }
+                  __threadfence();
+                  __syncwarp();
+                  const int cf = cta_owner(st, G, row_lo);
+                  const int kc = (__ldg(st + cf) / W == row) ? 0 : 1;
+                  unsigned* rc = p.rowcnt + (static_cast<size_t>(j) * G + cf) * 2 + kc;
+                  const unsigned mine_tiles = static_cast<unsigned>(hi - lo);
+                  unsigned oldg = 0;
+                  if (lane == 0) oldg = atom_add_acq_rel_gpu_u32(rc, mine_tiles);
+                  oldg = __shfl_sync(0xFFFFFFFFu, oldg, 0);
+                  emit = (oldg + mine_tiles == static_cast<unsigned>(W));
+                  if (emit) {
+                    __threadfence();
+#pragma unroll
+                    for (int nb = 0; nb < NB; ++nb)
+#pragma unroll
+                      for (int q = 0; q < 4; ++q) v[nb][q] = 0.f;
+                    const int cl = cta_owner(st, G, row_hi - 1);
+                    for (int c = cf; c <= cl; ++c) {
+                      const int c0 = __ldg(st + c);
+                      if (c0 == __ldg(st + c + 1)) continue;  // empty range
+                      const float* src = p.partials + (static_cast<size_t>(c) * 2 + ((c0 / W == row) ? 0 : 1)) * 256;
+#pragma unroll
+                      for (int nb = 0; nb < NB; ++nb) {
+                        const int b0 = nb * 8 + 2 * t;
+                        v[nb][0] += __ldcg(src + b0 * 16 + g);
+                        v[nb][1] += __ldcg(src + (b0 + 1) * 16 + g);
+                        v[nb][2] += __ldcg(src + b0 * 16 + g + 8);
+                        v[nb][3] += __ldcg(src + (b0 + 1) * 16 + g + 8);
+                      }
+                    }
+                    if (lane == 0) *rc = 0u;  // ready for the next launch
+                  }
+                }
               }
             }
             if (emit) {
@@ -632,6 +706,11 @@ __global__ void __launch_bounds__((kChainMaxWarps + 1) * 32, 1) chain_kernel(con
       }
       __syncwarp();
     }
+    // A warp that gave up (a timed-out wait) stopped issuing; its loads still
+    // in flight land in this CTA's shared memory, so it waits for them
+    // (bounded) before the CTA may exit. On the normal path none are left.
+    for (; consumed < issued; ++consumed)
+      mbar_wait(&my_full[consumed % D], (consumed / D) & 1u);
   }
 
   // ---- exit: the last CTA bumps the generation for the next launch
@@ -647,12 +726,15 @@ __global__ void __launch_bounds__((kChainMaxWarps + 1) * 32, 1) chain_kernel(con
   }
 }
 
-size_t chain_smem_bytes(bool raw, int consumers, int x_bytes) {
+size_t chain_smem_bytes(bool raw, int consumers, int x_bytes, int batch) {
+  const size_t nb = batch <= 8 ? 1 : 2;
   size_t b = 1024;  // alignment slack
   b += static_cast<size_t>(consumers) * kChainSlots * (raw ? kChainSlotRaw : kChainSlotSe12);
   if (!raw) b += static_cast<size_t>(consumers) * kChainSlots * 64;
-  b += (static_cast<size_t>(x_bytes) + 7) & ~static_cast<size_t>(7);
-  b += static_cast<size_t>(consumers) * kChainSlots * 8 + 16 + 8;  // barriers, op counters
+  b += (static_cast<size_t>(x_bytes) + 15) & ~static_cast<size_t>(15);
+  b += static_cast<size_t>(consumers) * 2 * 16 * 8 * nb * 4;               // warps' shares of shared rows
+  b += static_cast<size_t>(consumers) * kChainSlots * 8 + 16 + 8;          // barriers, op counters
+  b += static_cast<size_t>(consumers) * 2 * 4;                             // row counters
   return b;
 }
 

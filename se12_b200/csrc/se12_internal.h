@@ -180,6 +180,7 @@ static_assert(offsetof(ChainOp, tab) % 16 == 0, "the kernel loads a segment's ta
 
 struct ChainParams {
   const ChainOp* ops;
+  const int* starts;    // [n_ops][grid + 1]: op j's tiles [starts[c], starts[c + 1]) belong to CTA c
   int n_ops;
   int batch;
   int consumers;        // consumer warps per CTA (the CTA has one more: the control warp)
@@ -188,12 +189,12 @@ struct ChainParams {
   int n_ar;             // ops with an all-reduce
   unsigned* done;       // [n_ops] CTAs that finished op j, over all launches
   unsigned* gen;        // [2]: launches completed, CTAs that left the current launch
-  float* partials;      // [grid * consumers][2][16 * 16] partial rows
-  unsigned* rowcnt;     // [n_ops][grid * consumers] arrivals on a shared row (zero between launches)
+  float* partials;      // [grid][2][16 * 16] a CTA's sums of the rows it shares with other CTAs
+  unsigned* rowcnt;     // [n_ops][grid][2] tiles summed of a row shared by CTAs (zero between launches)
   PeerArgs peers;
 };
 
-size_t chain_smem_bytes(bool raw, int consumers, int x_bytes);
+size_t chain_smem_bytes(bool raw, int consumers, int x_bytes, int batch);
 
 // Kernel launchers (defined in the .cu files).
 cudaError_t launch_chain(bool raw, const ChainParams& p, int grid, size_t smem, cudaStream_t stream);

@@ -3,7 +3,7 @@ through the C ABI, against the fp64 oracle.
 
 Every op's y must satisfy max |y - y64| / max(|y64|, 1) <= 1e-3 (the GEMV
 tolerance of the single-call tests), for chains that mix shapes which reach
-every code path of the chain kernel: rows shared by many warps and CTAs,
+every code path of the chain kernel: rows shared by the warps of a CTA and rows split between CTAs,
 rows held by one warp, padded rows and columns (K % 256 != 0, K % 8 != 0),
 segmented matrices (one codebook per segment), escape-heavy and fallback
 tiles, a codebook whose padding weight is +inf, column-split ops (x too
@@ -64,7 +64,8 @@ CHAIN = [
     ("synthetic", 33, 300),      # padded rows and columns, K % 8 != 0
     ("outliers", 160, 2560),     # fallback tiles
     ("synthetic", 2304, 9216),   # down-like: rows split between CTAs
-    ("synthetic", 16, 65536),    # one tile row shared by every warp of the grid
+    ("synthetic", 16, 65536),    # one tile row split between CTAs (an even split of the tiles)
+    ("escapes", 48, 32768),      # three tile rows, each split between several CTAs
     ("concentrated", 160, 2560),
     ("synthetic", 1, 1),
     ("synthetic", 9216, 2304),   # gate-like: rows held by one warp
