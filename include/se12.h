@@ -331,8 +331,22 @@ int se12_encode_raw(const uint16_t* w_dev, int rows, int cols, int ldw, const in
                     int16_t* raw_dev, void* stream);
 
 /* Device status word (bit 0: a bounded wait timed out, bit 1: bad argument
- * seen by a kernel). Reading it synchronises with the device. */
+ * seen by a kernel). Reading it synchronises with the device. While bit 0 is
+ * set, the waits on other CTAs' and other GPUs' progress give up at once
+ * instead of waiting out their limit (a lost peer ends the kernel after one
+ * limit): clear it (clear = 1) and zero the workspaces the failed calls used
+ * (se12_workspace_clear, se12_chain_reset) before the next calls. No
+ * counterpart in the reference, whose kernels never wait on other blocks. */
 int se12_device_status(unsigned* status_out, int clear);
+
+/* Limit of those waits on the current device, in ns (default 2 s). A short
+ * limit makes a wait on a peer that will not write run out quickly (for
+ * failure-detection tests); a correct wait completes in microseconds. A
+ * synchronous copy to the device. */
+#define SE12_MIN_WAIT_LIMIT_NS 100000ull
+#define SE12_MAX_WAIT_LIMIT_NS 60000000000ull
+int se12_set_wait_limit_ns(unsigned long long ns);
+int se12_wait_limit_ns(unsigned long long* ns_out);
 
 const char* se12_status_string(int status);
 const char* se12_last_error(void);

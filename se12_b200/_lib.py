@@ -109,6 +109,8 @@ SIGNATURES = {
                                 ctypes.POINTER(c_int)]),
     "se12_chain_destroy": (None, [c_void_p]),
     "se12_device_status": (c_int, [ctypes.POINTER(c_uint), c_int]),
+    "se12_set_wait_limit_ns": (c_int, [ctypes.c_ulonglong]),
+    "se12_wait_limit_ns": (c_int, [ctypes.POINTER(ctypes.c_ulonglong)]),
     "se12_status_string": (c_char_p, [c_int]),
     "se12_last_error": (c_char_p, []),
     "se12_abi_version": (c_int, []),

@@ -759,6 +759,22 @@ int se12_device_status(unsigned* status, int clear) {
   return SE12_OK;
 }
 
+int se12_set_wait_limit_ns(unsigned long long ns) {
+  if (ns < SE12_MIN_WAIT_LIMIT_NS || ns > SE12_MAX_WAIT_LIMIT_NS)
+    return fail(SE12_ERR_INVALID_ARGUMENT, "wait limit must be in " + std::to_string(SE12_MIN_WAIT_LIMIT_NS) + ".." +
+                                               std::to_string(SE12_MAX_WAIT_LIMIT_NS) + " ns");
+  cudaError_t err = se12::set_wait_limit(ns);
+  if (err != cudaSuccess) return cuda_fail(err, "set wait limit");
+  return SE12_OK;
+}
+
+int se12_wait_limit_ns(unsigned long long* ns) {
+  if (!ns) return fail(SE12_ERR_INVALID_ARGUMENT, "null argument");
+  cudaError_t err = se12::get_wait_limit(ns);
+  if (err != cudaSuccess) return cuda_fail(err, "read wait limit");
+  return SE12_OK;
+}
+
 }  // extern "C"
 
 // ------------------------------------------------------------------ chains

@@ -43,8 +43,9 @@
 // A dense BF16 variant (RAW) runs the same chain over plain BF16 matrices:
 // the comparison baseline.
 //
-// Every wait is bounded (2 s); on timeout the kernel raises the status word
-// and the affected warp stops.
+// Every wait is bounded (2 s, or the limit the host set for waits on other
+// CTAs and GPUs); on timeout the kernel raises the status word and the
+// affected warp stops, after waiting for its own loads in flight.
 #include "se12_device.cuh"
 #include "se12_internal.h"
 
@@ -149,7 +150,7 @@ __device__ __forceinline__ bool wait_counter(const unsigned* p, unsigned target)
   const unsigned long long start = global_ns();
   while (!counter_reached(p, target)) {
     __nanosleep(32);
-    if (global_ns() - start > kWaitLimitNs) {
+    if (peer_wait_expired(start)) {
       raise_status(kStatusWaitTimeout);
       return false;
     }

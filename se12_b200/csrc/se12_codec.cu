@@ -497,4 +497,8 @@ cudaError_t read_device_status(unsigned* out, bool clear) {
   return err;
 }
 
+cudaError_t set_wait_limit(unsigned long long ns) { return cudaMemcpyToSymbol(g_wait_limit_ns, &ns, sizeof(ns)); }
+
+cudaError_t get_wait_limit(unsigned long long* ns) { return cudaMemcpyFromSymbol(ns, g_wait_limit_ns, sizeof(*ns)); }
+
 }  // namespace se12

@@ -46,6 +46,21 @@ __device__ __forceinline__ unsigned long long global_ns() {
 
 __device__ __forceinline__ void raise_status(unsigned bits) { atomicOr(&g_status, bits); }
 
+// Limit of the waits on other CTAs' and other GPUs' progress (flags,
+// counters, epoch-tagged words), in ns: kWaitLimitNs unless the host set
+// another (se12_set_wait_limit_ns), e.g. a short one to make a test's wait
+// on a peer that never writes run out quickly.
+__device__ unsigned long long g_wait_limit_ns = kWaitLimitNs;
+
+// Such a wait gives up when its limit has passed, or at once when some wait
+// already timed out and the host has not cleared the status word: one lost
+// peer then ends a kernel after one limit, not one limit per waiting value.
+// (Waits for this CTA's own copies, the mbarrier waits, always wait them out.)
+__device__ __forceinline__ bool peer_wait_expired(unsigned long long start) {
+  if (*reinterpret_cast<volatile unsigned*>(&g_status) & kStatusWaitTimeout) return true;
+  return global_ns() - start > *reinterpret_cast<volatile unsigned long long*>(&g_wait_limit_ns);
+}
+
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
@@ -148,13 +163,13 @@ __device__ __forceinline__ int ld_acquire_gpu(const int* flag) {
 }
 
 // Waits until *flag is non-zero (acquiring what its writer released).
-// Returns false (and raises kStatusWaitTimeout) after kWaitLimitNs.
+// Returns false (and raises kStatusWaitTimeout) once peer_wait_expired.
 __device__ __forceinline__ bool wait_flag_gpu(const int* flag) {
   if (ld_acquire_gpu(flag)) return true;
   const unsigned long long start = global_ns();
   while (!ld_acquire_gpu(flag)) {
     __nanosleep(64);
-    if (global_ns() - start > kWaitLimitNs) {
+    if (peer_wait_expired(start)) {
       raise_status(kStatusWaitTimeout);
       return false;
     }
@@ -175,7 +190,7 @@ __device__ __forceinline__ int ld_acquire_sys(const int* p) {
 }
 
 // Waits until *flag has reached epoch e (flags only grow; compared modulo
-// 2^32). Returns false (and raises kStatusWaitTimeout) after kWaitLimitNs.
+// 2^32). Returns false (and raises kStatusWaitTimeout) once peer_wait_expired.
 __device__ __forceinline__ bool wait_epoch_sys(const int* flag, int e) {
   auto reached = [flag, e]() {
     return static_cast<int>(static_cast<unsigned>(ld_acquire_sys(flag)) - static_cast<unsigned>(e)) >= 0;
@@ -184,7 +199,7 @@ __device__ __forceinline__ bool wait_epoch_sys(const int* flag, int e) {
   const unsigned long long start = global_ns();
   while (!reached()) {
     __nanosleep(32);
-    if (global_ns() - start > kWaitLimitNs) {
+    if (peer_wait_expired(start)) {
       raise_status(kStatusWaitTimeout);
       return false;
     }
@@ -205,14 +220,14 @@ __device__ __forceinline__ unsigned long long ld_word_sys(const unsigned long lo
 }
 
 // Waits until *p holds epoch e in its high half; returns its low half in
-// *value. False (and kStatusWaitTimeout raised) after kWaitLimitNs.
+// *value. False (and kStatusWaitTimeout raised) once peer_wait_expired.
 __device__ __forceinline__ bool wait_word_sys(const unsigned long long* p, unsigned e, unsigned* value) {
   unsigned long long w = ld_word_sys(p);
   if (static_cast<unsigned>(w >> 32) != e) {
     const unsigned long long start = global_ns();
     do {
       __nanosleep(20);
-      if (global_ns() - start > kWaitLimitNs) {
+      if (peer_wait_expired(start)) {
         raise_status(kStatusWaitTimeout);
         return false;
       }

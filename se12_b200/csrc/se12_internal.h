@@ -195,6 +195,8 @@ struct ChainParams {
 };
 
 size_t chain_smem_bytes(bool raw, int consumers, int x_bytes, int batch);
+cudaError_t set_wait_limit(unsigned long long ns);
+cudaError_t get_wait_limit(unsigned long long* ns);
 
 // Kernel launchers (defined in the .cu files).
 cudaError_t launch_chain(bool raw, const ChainParams& p, int grid, size_t smem, cudaStream_t stream);

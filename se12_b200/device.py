@@ -355,6 +355,18 @@ def bf16_gemv(weights: torch.Tensor, x: torch.Tensor, out: torch.Tensor | None =
 STATUS_WAIT_TIMEOUT = 1
 
 
+def set_wait_limit_ns(ns: int) -> None:
+    """Limit of the kernels' waits on other CTAs and GPUs on the current
+    device (default 2 s; a short one makes a lost peer's wait run out fast)."""
+    _lib.call("se12_set_wait_limit_ns", ctypes.c_ulonglong(int(ns)))
+
+
+def wait_limit_ns() -> int:
+    v = ctypes.c_ulonglong(0)
+    _lib.call("se12_wait_limit_ns", ctypes.byref(v))
+    return v.value
+
+
 def device_status(clear: bool = True) -> int:
     """Device status word of the library (non-zero after a kernel-side error).
 

@@ -159,3 +159,64 @@ def test_fused_gemv_allreduce_over_peer_memory(tmp_path, world):
         assert res["status"] == 0, res
         assert max(res["errs"]) <= TOLERANCE, res["errs"]
         assert all(res["same"]), res["same"]
+
+
+def _lost_peer_main(rank, world, port, result_path):
+    import datetime
+    import time
+
+    import torch.distributed as dist
+
+    from se12_b200.device import STATUS_WAIT_TIMEOUT, device_status, set_wait_limit_ns
+    from se12_b200.format import make_tensor
+    from se12_b200.peers import PeerGroup
+    from se12_b200.sharding import shard_matrix
+
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", rank))
+    out = {}
+    try:
+        rows, cols = 1040, 4608
+        bits, _, _ = cases.synthetic_weights(rows, cols, seed=8)
+        s = oracle.encode(np.asarray(bits, dtype=np.uint16), rows, cols)
+        t = make_tensor(s.rows, s.cols, s.codebook, s.sm, s.ec, s.esc, s.fallback_bitmap, s.fallback_raw)
+        peers = PeerGroup(rows_cap=rows)
+        layer = shard_matrix(t, "cols", world, rank, device=f"cuda:{rank}", peers=peers)
+        xb = oracle.bf16_round(np.random.default_rng(1).normal(size=(1, cols)).astype(np.float32))
+        x = torch.from_numpy(xb.view(np.int16)).view(torch.bfloat16).cuda()
+        y64 = oracle.gemv_fp64(bits, rows, cols, oracle.bits_to_float32(xb))
+        good = oracle.max_relative_error(layer(x).cpu().numpy(), y64)  # every rank calls: fine
+        torch.cuda.synchronize()
+        dist.barrier()
+        set_wait_limit_ns(100_000_000)
+        elapsed = None
+        if rank == 0:  # rank 1 skips this call: rank 0 waits for rows that never come
+            t0 = time.perf_counter()
+            layer(x)
+            torch.cuda.synchronize()
+            elapsed = time.perf_counter() - t0
+        status = device_status(clear=True)
+        set_wait_limit_ns(2_000_000_000)
+        dist.barrier()  # host-side: rank 1 learns here that the step failed; no kernel of it is in flight
+        peers.close()   # the group's epochs now differ: it is torn down, not reused
+        out = {"good": good, "timed_out": bool(status & STATUS_WAIT_TIMEOUT), "status": status, "elapsed": elapsed}
+    finally:
+        torch.save(out, f"{result_path}.{rank}")
+        dist.destroy_process_group()
+
+
+def test_lost_peer_makes_the_fused_allreduce_time_out(tmp_path):
+    """Rank 1 skips one fused GEMV + all-reduce call: rank 0's wait for its
+    rows runs out (100 ms limit), the kernel returns with the timed-out bit,
+    rank 1 sees nothing wrong on the device, and the group is torn down."""
+    import torch.multiprocessing as mp
+
+    _need(2)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    mp.spawn(_lost_peer_main, args=(2, _free_port(), str(tmp_path / "lost")), nprocs=2, join=True)
+    r0, r1 = (torch.load(tmp_path / f"lost.{r}") for r in range(2))
+    assert r0["good"] <= TOLERANCE and r1["good"] <= TOLERANCE
+    assert r0["timed_out"], r0
+    assert r0["elapsed"] < 10.0, r0
+    assert r1["status"] == 0, r1
