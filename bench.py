@@ -79,6 +79,7 @@ def parse_args():
                         "(programmatic dependent launch)")
     p.add_argument("--no-group", action="store_true",
                    help="one GEMV per projection instead of q/k/v and gate/up as one segmented matrix each")
+    p.add_argument("--no-per-gemv", action="store_true", help="skip the per-GEMV-class times")
     p.add_argument("--no-tp", action="store_true",
                    help="skip the tensor-parallel leg (the --tp-config step sharded over the torchrun ranks, reported "
                         "as the line's tp object)")
@@ -389,6 +390,34 @@ class _Null:
         return False
 
 
+def per_gemv_times(torch, args, mats, xs, batch, device, peak):
+    """Live time of each GEMV class of the step (all its matrices stacked in
+    one graph, as in the step), its fraction of the copy roofline, and the
+    B200 performance model's prediction (se12_b200.roofline.B200_DEFAULT)."""
+    from se12_b200.roofline import B200_DEFAULT, tiles_of
+    from se12_b200.stack import GemvStack
+
+    classes = {}
+    for name, m, kind in mats:
+        classes.setdefault(name.rsplit(".", 1)[-1], []).append((m, kind))
+    out = {}
+    for cls, entries in classes.items():
+        st = GemvStack(device, chain=args.chain)
+        for m, kind in entries:
+            st.add(m, xs[kind], torch.empty(batch, m.rows, dtype=torch.float32, device=device))
+        n = max(3, args.steps // 4)
+        ms = time_stack(torch, st, n, 3, device, eager=args.eager) / n
+        del st
+        m0 = entries[0][0]
+        us = ms * 1e3 / len(entries)
+        byts = m0.byte_size + batch * m0.cols * 2 + batch * m0.rows * 4
+        tiles = tiles_of(m0.rows, m0.cols)
+        out[cls] = {"gemvs": len(entries), "rows": m0.rows, "cols": m0.cols, "tiles": tiles, "bytes": byts,
+                    "us_per_gemv": us, "frac_of_measured_hbm": byts / (us * 1e-6) / 1e9 / peak,
+                    "model_us": B200_DEFAULT.gemv_us(m0.byte_size, tiles) if batch == 1 else None}
+    return out
+
+
 def run_ours(args) -> None:
     import torch
 
@@ -468,6 +497,9 @@ def run_ours(args) -> None:
     peaks = measured_peaks()
     peak = float(peaks["hbm_gbs"])
     achieved = bytes_per_step / (ms_per_step * 1e-3) / 1e9
+
+    # ----------------------------------------------------------- per GEMV class
+    per_gemv = per_gemv_times(torch, args, mats, inputs_for(batch), batch, device, peak) if not args.no_per_gemv else None
 
     extra = {}
     # ----------------------------------------------------------- other batch sizes
@@ -625,6 +657,7 @@ def run_ours(args) -> None:
             "clocks": sampler.summary(),
             "other_batches": extra,
             "dense": dense_info,
+            "per_gemv": per_gemv,
         }
     # ----------------------------------------------------------- tensor-parallel leg
     if not args.no_tp:
