@@ -303,12 +303,23 @@ __global__ void __launch_bounds__((kChainMaxWarps + 1) * 32, 1) chain_kernel(con
       a = s + part_start(n, warp, C);
       b = s + part_start(n, warp + 1, C);
     };
+    // the issue side's op fields live in registers, loaded once per op
     int iop = 0, ii = 0, iend = 0;
+    int is_k0 = 0, is_w = 1, is_tc = 1, is_r3 = 0;
+    const uint32_t* is_rec = nullptr;
     auto seek = [&](int from) {
       iop = from;
       while (iop < nops) {
         part_of(iop, ii, iend);
-        if (ii < iend) return;
+        if (ii < iend) {
+          const ChainOp* op = p.ops + iop;
+          is_k0 = op->k0;
+          is_w = op->k1 - is_k0;
+          is_tc = op->tile_cols;
+          is_r3 = op->raw_3d;
+          is_rec = op->records;
+          return;
+        }
         ++iop;
       }
     };
@@ -317,16 +328,15 @@ __global__ void __launch_bounds__((kChainMaxWarps + 1) * 32, 1) chain_kernel(con
     auto issue_next = [&]() {
       if (iop >= nops) return;
       if (lane == 0) {
-        const ChainOp* op = p.ops + iop;
-        const int W = op->k1 - op->k0;
-        const int tr = ii / W;
-        const int kt = op->k0 + (ii - tr * W);
+        const ChainOp* op = p.ops + iop;  // tensor maps: read by the copy engine, not here
+        const int tr = ii / is_w;
+        const int kt = is_k0 + (ii - tr * is_w);
         const int s = static_cast<int>(issued % D);
         uint8_t* dst = smem + my_slots + s * SLOT;
         uint64_t* bar = &my_full[s];
         if (RAW) {
           mbar_arrive_expect_tx(bar, 8192u);
-          if (op->raw_3d) {
+          if (is_r3) {
             tma_load_3d(dst, &op->sm_map, 0, kt * 4, tr * kTileRows, bar, pol_w);
           } else {
 #pragma unroll
@@ -334,11 +344,11 @@ __global__ void __launch_bounds__((kChainMaxWarps + 1) * 32, 1) chain_kernel(con
               tma_load_2d(dst + c * 2048, &op->sm_map, kt * kTileCols + c * 64, tr * kTileRows, bar, pol_w);
           }
         } else {
-          const int tile = tr * op->tile_cols + kt;
+          const int tile = tr * is_tc + kt;
           mbar_arrive_expect_tx(bar, 4096u + 2048u + 64u);
           tma_load_3d(dst, &op->sm_map, 0, 0, tile * kTileRows, bar, pol_w);
           tma_load_2d(dst + 4096, &op->ec_map, 0, tile * kTileRows, bar, pol_w);
-          bulk_load(smem + my_recs + s * 64, op->records + static_cast<size_t>(tile) * kEscapeBudget, 64u, bar, pol_w);
+          bulk_load(smem + my_recs + s * 64, is_rec + static_cast<size_t>(tile) * kEscapeBudget, 64u, bar, pol_w);
         }
       }
       __syncwarp();
@@ -360,20 +370,37 @@ __global__ void __launch_bounds__((kChainMaxWarps + 1) * 32, 1) chain_kernel(con
       const int* const st = p.starts + static_cast<size_t>(j) * (G + 1);
       const int cs = __ldg(st + cta), n = __ldg(st + cta + 1) - cs;  // this CTA's tiles [cs, cs + n)
       const int a = cs + part_start(n, warp, C), b = cs + part_start(n, warp + 1, C);
+      // the op's fields (and the decode table of this warp's first tile),
+      // loaded before its x is ready: their latency hides under that wait
+      const int k0 = op->k0;
+      const int W = op->k1 - k0;
+      const int N = op->rows;
+      const int K = op->cols;
+      float* const y = op->y;
+      const int ldy = op->ldy;
+      const uint16_t* const fbraw = op->fallback_raw;
+      const int accumulate = op->accumulate;
+      const int ar_index = op->ar_index;
+      const bool r3 = RAW && op->raw_3d != 0;
+      int seg_end[kMaxSegments];
+#pragma unroll
+      for (int q = 0; q < kMaxSegments; ++q) seg_end[q] = op->seg_end[q];
+      uint32_t tab[4] = {0u, 0u, 0u, 0u};
+      int cur_seg = -1;
+      if (!RAW && a < b) {
+        const int tr0 = a / W;
+        int sg = 0;
+#pragma unroll
+        for (int q = 0; q < kMaxSegments - 1; ++q) sg += (tr0 >= seg_end[q]);
+        const uint4 v = *reinterpret_cast<const uint4*>(op->tab[sg]);
+        tab[0] = v.x;
+        tab[1] = v.y;
+        tab[2] = v.z;
+        tab[3] = v.w;
+        cur_seg = sg;
+      }
       if (ok) ok = __all_sync(0xFFFFFFFFu, mbar_wait(xready, static_cast<uint32_t>(j) & 1u));
       if (a < b && ok) {
-        const int k0 = op->k0;
-        const int W = op->k1 - k0;
-        const int N = op->rows;
-        const int K = op->cols;
-        float* const y = op->y;
-        const int ldy = op->ldy;
-        const uint16_t* const fbraw = op->fallback_raw;
-        int seg_end[kMaxSegments];
-#pragma unroll
-        for (int s = 0; s < kMaxSegments; ++s) seg_end[s] = op->seg_end[s];
-        uint32_t tab[4] = {0u, 0u, 0u, 0u};
-        int cur_seg = -1;
 
         int row = a / W;       // current tile row (of the op)
         int seg_first = a;     // op-linear index of this warp's first tile in `row`
@@ -389,7 +416,6 @@ __global__ void __launch_bounds__((kChainMaxWarps + 1) * 32, 1) chain_kernel(con
             const uint32_t sb = my_slots + s * SLOT;
             const uint32_t xt = x_lane + static_cast<uint32_t>(kt_local) * 512u;
             if (RAW) {
-              const bool r3 = op->raw_3d != 0;
 #pragma unroll
               for (int k = 0; k < 8; ++k) {
                 const uint32_t m1 = k >> 1, unit = 4u * (k & 1) + t;
@@ -618,7 +644,7 @@ __global__ void __launch_bounds__((kChainMaxWarps + 1) * 32, 1) chain_kernel(con
               }
             }
             if (emit) {
-              if (op->accumulate) {
+              if (accumulate) {
                 // the previous op wrote these rows' other columns
 #pragma unroll
                 for (int nb = 0; nb < NB; ++nb)
@@ -629,12 +655,12 @@ __global__ void __launch_bounds__((kChainMaxWarps + 1) * 32, 1) chain_kernel(con
                     if (bb < B && grow < N) v[nb][q] += __ldcg(y + static_cast<size_t>(bb) * ldy + grow);
                   }
               }
-              if (op->ar_index >= 0) {
+              if (ar_index >= 0) {
                 // all-reduce of the row over the peer group: every value with
                 // the op's epoch in one 64-bit word into every rank's receive
                 // buffer, then all ranks' words summed in rank order
                 const PeerArgs& P = p.peers;
-                const unsigned epoch = ar_base + static_cast<unsigned>(op->ar_index) + 1u;
+                const unsigned epoch = ar_base + static_cast<unsigned>(ar_index) + 1u;
                 const size_t slot = static_cast<size_t>(16) * P.rows_cap;
                 const size_t base = static_cast<size_t>((epoch & 1u) * P.world) * slot;
                 const unsigned long long tag = static_cast<unsigned long long>(epoch) << 32;
