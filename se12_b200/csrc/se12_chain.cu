@@ -166,6 +166,33 @@ __device__ __forceinline__ unsigned atom_add_acq_rel_gpu_u32(unsigned* p, unsign
 
 __device__ __forceinline__ void fence_proxy_async_all() { asm volatile("fence.proxy.async;" ::: "memory"); }
 
+// Waits for an mbarrier phase by polling without suspending the warp: the
+// consumers waiting for an op's x have nothing else to do, and a suspended
+// warp wakes up later than a polling one. Bounded like mbar_wait.
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+__device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity) {
+  if (mbar_test(bar, parity)) return true;
+  const unsigned long long start = global_ns();
+  while (!mbar_test(bar, parity)) {
+    if (global_ns() - start > kWaitLimitNs) {
+      raise_status(kStatusWaitTimeout);
+      return false;
+    }
+  }
+  return true;
+}
+
 // A CTA's range of n tiles is split over its C consumer warps: warp w holds
 // local tiles [n w / C, n (w + 1) / C).
 __device__ __forceinline__ int part_start(int n, int w, int C) { return n * w / C; }
@@ -209,15 +236,13 @@ __global__ void __launch_bounds__((kChainMaxWarps + 1) * 32, 1) chain_kernel(con
   uint64_t* const full = reinterpret_cast<uint64_t*>(smem + o_bar);  // [C * D] slot loaded
   uint64_t* const xbar = full + C * D;                               // x copy landed (control warp)
   uint64_t* const xready = xbar + 1;                                  // x of the current op ready
-  unsigned* const opcnt = reinterpret_cast<unsigned*>(xready + 1);    // [2] consumer warps done with op j (j & 1)
-  unsigned* const rowcnt_s = opcnt + 2;                               // [C][2] tiles summed of a row shared by warps
+  unsigned* const rowcnt_s = reinterpret_cast<unsigned*>(xready + 1);  // [C][2] tiles summed of a row shared by warps
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (tid == 0) {
     for (int i = 0; i < C * D; ++i) mbar_init(&full[i], 1);
     mbar_init(xbar, 1);
     mbar_init(xready, 1);
-    opcnt[0] = opcnt[1] = 0u;
     for (int i = 0; i < 2 * C; ++i) rowcnt_s[i] = 0u;
     fence_barrier_init();
   }
@@ -399,7 +424,7 @@ __global__ void __launch_bounds__((kChainMaxWarps + 1) * 32, 1) chain_kernel(con
         tab[3] = v.w;
         cur_seg = sg;
       }
-      if (ok) ok = __all_sync(0xFFFFFFFFu, mbar_wait(xready, static_cast<uint32_t>(j) & 1u));
+      if (ok) ok = __all_sync(0xFFFFFFFFu, mbar_wait_spin(xready, static_cast<uint32_t>(j) & 1u));
       if (a < b && ok) {
 
         int row = a / W;       // current tile row (of the op)
@@ -719,19 +744,14 @@ __global__ void __launch_bounds__((kChainMaxWarps + 1) * 32, 1) chain_kernel(con
           }
         }
       }
-      // ---- this warp is done with op j; the CTA's last warp to finish
-      // publishes the CTA's completion of op j
-      __syncwarp();
-      if (lane == 0) {
+      // ---- every consumer warp of the CTA is done with op j (every one
+      // reaches this barrier: all their waits are bounded); one thread then
+      // publishes the CTA's completion, its fence covering the warps' writes
+      named_barrier(1, C * 32);
+      if (warp == 0 && lane == 0) {
         __threadfence();
-        const unsigned before = static_cast<unsigned>(atomic_add_acq_rel_cta(reinterpret_cast<int*>(&opcnt[j & 1]), 1));
-        if (before == static_cast<unsigned>(C - 1)) {
-          opcnt[j & 1] = 0u;
-          __threadfence();
-          atomicAdd(p.done + j, 1u);
-        }
+        atomicAdd(p.done + j, 1u);
       }
-      __syncwarp();
     }
     // A warp that gave up (a timed-out wait) stopped issuing; its loads still
     // in flight land in this CTA's shared memory, so it waits for them
