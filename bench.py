@@ -84,6 +84,9 @@ def parse_args():
                    help="skip the tensor-parallel leg (the --tp-config step sharded over the torchrun ranks, reported "
                         "as the line's tp object)")
     p.add_argument("--tp-config", default="gemma2-27b", help="model of the tensor-parallel leg")
+    p.add_argument("--sweep", action="store_true",
+                   help="escape-stress sweep (baseline config 4): one 8192 x 28672 matrix over weight scales and "
+                        "outlier rates; bits/weight, fallback tiles and GEMV GB/s per point")
     p.add_argument("--tp", action="store_true",
                    help="tensor-parallel decode step over the torchrun ranks (default config gemma2-27b)")
     return p.parse_args()
@@ -1108,10 +1111,82 @@ def run_offload(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+SWEEP_SIGMAS = (0.005, 0.02, 0.1)
+SWEEP_OUTLIERS = ((0.0, 64.0), (1e-4, 64.0), (1e-3, 64.0), (3e-3, 64.0), (1e-2, 64.0), (1e-3, 1024.0), (1e-2, 1024.0))
+
+
+def run_sweep(args) -> None:
+    """Escape-stress sweep (baseline config 4): one 8192 x 28672 matrix of
+    N(0, sigma) BF16 weights with a fraction of entries scaled up (outliers),
+    packed to SE12 on the GPU; per point: bits/weight, the share of fallback
+    tiles (more than 16 escapes: stored raw, src/lws/domain/se12/codec.py:
+    131-133), the fused GEMV's live time (batch 1, one graph of 8 GEMVs over
+    8 distinct copies of the point's matrix, so every GEMV streams from HBM)
+    and its GB/s, and a float64 check of 2048 sampled rows."""
+    import torch
+
+    from se12_b200 import _build
+    from se12_b200.codec import encode_device
+    from se12_b200.stack import GemvStack
+
+    _build.build()
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    rows, cols = 8192, 28672
+    peak = float(measured_peaks()["hbm_gbs"])
+    points = []
+    for sigma in SWEEP_SIGMAS:
+        for rate, scale in SWEEP_OUTLIERS:
+            mats, dense0 = [], None
+            for c in range(8):
+                w = synthetic_bf16(torch, rows, cols, 77 + c, device, sigma=sigma, outlier_rate=rate, outlier_scale=scale)
+                mats.append(encode_device(w))
+                if c == 0:
+                    dense0 = w
+                else:
+                    del w
+            x = torch.randn(1, cols, device=device).to(torch.bfloat16)
+            st = GemvStack(device)
+            ys = [torch.empty(1, rows, dtype=torch.float32, device=device) for _ in mats]
+            for m, y in zip(mats, ys):
+                st.add(m, x, y)
+            ms = time_stack(torch, st, max(3, args.steps // 4), max(3, args.warmup), device) / len(mats)
+            ids = torch.randint(0, rows, (2048,), generator=torch.Generator().manual_seed(3)).to(device)
+            y64 = x.double() @ dense0[ids].double().T
+            err = float(((ys[0][:, ids].double() - y64).abs() / y64.abs().clamp_min(1.0)).max())
+            m0 = mats[0]
+            nbytes = m0.byte_size + cols * 2 + rows * 4
+            points.append({
+                "sigma": sigma, "outlier_rate": rate, "outlier_scale": scale,
+                "bits_per_weight": 8 * m0.byte_size / (rows * cols),
+                "fallback_tile_fraction": m0.fallback_tiles / m0.tiles,
+                "us_per_gemv": ms * 1e3, "gbs": nbytes / (ms * 1e-3) / 1e9,
+                "bf16_equiv_gbs": (2 * rows * cols + cols * 2 + rows * 4) / (ms * 1e-3) / 1e9,
+                "frac_of_measured_hbm": nbytes / (ms * 1e-3) / 1e9 / peak,
+                "max_rel_err_vs_fp64": err,
+            })
+            print(json.dumps(points[-1]), file=sys.stderr, flush=True)
+            del st, mats, ys, dense0
+            torch.cuda.empty_cache()
+    base = next(pt for pt in points if pt["sigma"] == 0.02 and pt["outlier_rate"] == 1e-4)
+    line = {
+        "metric": METRIC, "value": base["gbs"], "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": base["us_per_gemv"] * 1e-3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"escape-stress sweep: one {rows} x {cols} matrix, batch 1; value = the sigma 0.02, "
+                   "0.01 % x64 point", "sigmas": list(SWEEP_SIGMAS),
+                   "outliers": [list(o) for o in SWEEP_OUTLIERS]},
+        "sweep": points,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse_args()
     if args.impl == "reference":
         run_reference(args)
+    elif args.sweep:
+        run_sweep(args)
     elif args.tp:
         run_tp(args)
     elif args.offload_gb is not None:
