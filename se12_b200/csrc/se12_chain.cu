@@ -440,6 +440,8 @@ __global__ void __launch_bounds__((kChainMaxWarps + 1) * 32, 1) chain_kernel(con
           if (ok) {
             const uint32_t sb = my_slots + s * SLOT;
             const uint32_t xt = x_lane + static_cast<uint32_t>(kt_local) * 512u;
+            float part[2][NB][4];  // the tile's MMAs sum here first (two-level accumulation, see add_acc)
+            zero_acc(part);
             if (RAW) {
 #pragma unroll
               for (int k = 0; k < 8; ++k) {
@@ -457,8 +459,8 @@ __global__ void __launch_bounds__((kChainMaxWarps + 1) * 32, 1) chain_kernel(con
                 for (int nb = 0; nb < NB; ++nb) {
                   uint4 xv = make_uint4(0u, 0u, 0u, 0u);
                   if (nb * 8 + g < B) xv = lds<uint4>(smem, xt + nb * x_nb + 64u * k);
-                  mma_bf16_16816(acc[k & 1][nb], v0.x, v1.x, v0.y, v1.y, xv.x, xv.y);
-                  mma_bf16_16816(acc[k & 1][nb], v0.z, v1.z, v0.w, v1.w, xv.z, xv.w);
+                  mma_bf16_16816(part[k & 1][nb], v0.x, v1.x, v0.y, v1.y, xv.x, xv.y);
+                  mma_bf16_16816(part[k & 1][nb], v0.z, v1.z, v0.w, v1.w, xv.z, xv.w);
                 }
               }
             } else {
@@ -475,8 +477,8 @@ __global__ void __launch_bounds__((kChainMaxWarps + 1) * 32, 1) chain_kernel(con
                   for (int nb = 0; nb < NB; ++nb) {
                     uint4 xv = make_uint4(0u, 0u, 0u, 0u);
                     if (nb * 8 + g < B) xv = lds<uint4>(smem, xt + nb * x_nb + 64u * k);
-                    mma_bf16_16816(acc[k & 1][nb], v0.x, v1.x, v0.y, v1.y, xv.x, xv.y);
-                    mma_bf16_16816(acc[k & 1][nb], v0.z, v1.z, v0.w, v1.w, xv.z, xv.w);
+                    mma_bf16_16816(part[k & 1][nb], v0.x, v1.x, v0.y, v1.y, xv.x, xv.y);
+                    mma_bf16_16816(part[k & 1][nb], v0.z, v1.z, v0.w, v1.w, xv.z, xv.w);
                   }
                 }
               } else {
@@ -516,8 +518,8 @@ __global__ void __launch_bounds__((kChainMaxWarps + 1) * 32, 1) chain_kernel(con
                   for (int nb = 0; nb < NB; ++nb) {
                     uint4 xv = make_uint4(0u, 0u, 0u, 0u);
                     if (nb * 8 + g < B) xv = lds<uint4>(smem, xt + nb * x_nb + 64u * k);
-                    mma_bf16_16816(acc[k & 1][nb], f0[0], f1[0], f0[1], f1[1], xv.x, xv.y);
-                    mma_bf16_16816(acc[k & 1][nb], f0[2], f1[2], f0[3], f1[3], xv.z, xv.w);
+                    mma_bf16_16816(part[k & 1][nb], f0[0], f1[0], f0[1], f1[1], xv.x, xv.y);
+                    mma_bf16_16816(part[k & 1][nb], f0[2], f1[2], f0[3], f1[3], xv.z, xv.w);
                   }
                 }
                 // exact products of the escaped weights (decoded with
@@ -551,6 +553,7 @@ __global__ void __launch_bounds__((kChainMaxWarps + 1) * 32, 1) chain_kernel(con
                 }
               }
             }
+            add_acc(acc, part);  // this tile's MMA sums into the running fp32 sums
           }
           // slot s is read: refill it with the next tile of this warp's sequence
           __syncwarp();

@@ -139,6 +139,31 @@ __device__ __forceinline__ T lds_at(const uint8_t* smem, uint32_t offset) {
   return *reinterpret_cast<const T*>(smem + offset);
 }
 
+// Two-level accumulation: the MMAs of one half-tile (128 columns) sum into
+// fresh accumulators, which are then added to the running sums with plain
+// fp32 adds. A tensor-core accumulator carried across a whole tile row adds
+// every product into an ever larger partial sum; with large weights (the
+// escape-stress points: 1 % of the weights x1024) and long rows that lost
+// up to 2e-3 of the output against fp64, where summing per half-tile keeps
+// the error at the level of a plain fp32 dot product.
+template <int NB>
+__device__ __forceinline__ void zero_acc(float (&a)[2][NB][4]) {
+#pragma unroll
+  for (int h = 0; h < 2; ++h)
+#pragma unroll
+    for (int nb = 0; nb < NB; ++nb) a[h][nb][0] = a[h][nb][1] = a[h][nb][2] = a[h][nb][3] = 0.f;
+}
+
+template <int NB>
+__device__ __forceinline__ void add_acc(float (&acc)[2][NB][4], const float (&part)[2][NB][4]) {
+#pragma unroll
+  for (int h = 0; h < 2; ++h)
+#pragma unroll
+    for (int nb = 0; nb < NB; ++nb)
+#pragma unroll
+      for (int q = 0; q < 4; ++q) acc[h][nb][q] += part[h][nb][q];
+}
+
 template <int NB, bool RAW, bool XRES, bool FULL, bool AR, bool WIDE>
 __global__ void __launch_bounds__(gemv_threads(WIDE), WIDE ? 1 : 2) gemv_kernel(const __grid_constant__ CUtensorMap map0,
                                                                                 const __grid_constant__ CUtensorMap map1,
@@ -703,6 +728,8 @@ __global__ void __launch_bounds__(gemv_threads(WIDE), WIDE ? 1 : 2) gemv_kernel(
   // s) into acc.
   auto mma_tile = [&](int s, int kt, int h) {
     const uint32_t xt = (XRES ? x_thread + kt * (kTileCols * 2) : x_thread + s * xstage) + 256 * h;
+    float part[2][NB][4];
+    zero_acc(part);
 #pragma unroll
     for (int nb = 0; nb < NB; ++nb) {
       const bool have = nb * 8 + g < B;
@@ -710,10 +737,11 @@ __global__ void __launch_bounds__(gemv_threads(WIDE), WIDE ? 1 : 2) gemv_kernel(
       for (int k = 0; k < 4; ++k) {
         uint4 xv = make_uint4(0, 0, 0, 0);
         if (have) xv = lds_at<uint4>(sm8, xt + nb * x_nb_step + 64 * k);
-        mma_bf16_16816(acc[k & 1][nb], frag0[k][0], frag1[k][0], frag0[k][1], frag1[k][1], xv.x, xv.y);
-        mma_bf16_16816(acc[k & 1][nb], frag0[k][2], frag1[k][2], frag0[k][3], frag1[k][3], xv.z, xv.w);
+        mma_bf16_16816(part[k & 1][nb], frag0[k][0], frag1[k][0], frag0[k][1], frag1[k][1], xv.x, xv.y);
+        mma_bf16_16816(part[k & 1][nb], frag0[k][2], frag1[k][2], frag0[k][3], frag1[k][3], xv.z, xv.w);
       }
     }
+    add_acc(acc, part);
   };
 
   // Decodes half hw + h of this warp's tile of stage s and multiplies it
@@ -726,6 +754,8 @@ __global__ void __launch_bounds__(gemv_threads(WIDE), WIDE ? 1 : 2) gemv_kernel(
     const uint32_t wb = wst + w_base + (h ? 144u - ((static_cast<uint32_t>(lane) & 2u) << 4) : 0u);
     const uint32_t eb = wst + e_base + (h ? 64u - ((static_cast<uint32_t>(lane) & 16u) << 3) : 0u);
     const uint32_t xt = (XRES ? x_thread + kt * (kTileCols * 2) : x_thread + s * xstage) + 256 * h;
+    float part[2][NB][4];
+    zero_acc(part);
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
       const uint32_t wo = wb + ((32u * k) ^ w_xor);
@@ -737,10 +767,11 @@ __global__ void __launch_bounds__(gemv_threads(WIDE), WIDE ? 1 : 2) gemv_kernel(
       for (int nb = 0; nb < NB; ++nb) {
         uint4 xv = make_uint4(0, 0, 0, 0);
         if (nb * 8 + g < B) xv = lds_at<uint4>(sm8, xt + nb * x_nb_step + 64 * k);
-        mma_bf16_16816(acc[k & 1][nb], f0[0], f1[0], f0[1], f1[1], xv.x, xv.y);
-        mma_bf16_16816(acc[k & 1][nb], f0[2], f1[2], f0[3], f1[3], xv.z, xv.w);
+        mma_bf16_16816(part[k & 1][nb], f0[0], f1[0], f0[1], f1[1], xv.x, xv.y);
+        mma_bf16_16816(part[k & 1][nb], f0[2], f1[2], f0[3], f1[3], xv.z, xv.w);
       }
     }
+    add_acc(acc, part);
   };
 
   // Adds the exact products of the warp's escaped weights: in the MMA they
