@@ -1150,7 +1150,8 @@ def run_sweep(args) -> None:
             ys = [torch.empty(1, rows, dtype=torch.float32, device=device) for _ in mats]
             for m, y in zip(mats, ys):
                 st.add(m, x, y)
-            ms = time_stack(torch, st, max(3, args.steps // 4), max(3, args.warmup), device) / len(mats)
+            n_steps = max(3, args.steps // 4)
+            ms = time_stack(torch, st, n_steps, max(3, args.warmup), device) / n_steps / len(mats)
             ids = torch.randint(0, rows, (2048,), generator=torch.Generator().manual_seed(3)).to(device)
             y64 = x.double() @ dense0[ids].double().T
             err = float(((ys[0][:, ids].double() - y64).abs() / y64.abs().clamp_min(1.0)).max())
