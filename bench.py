@@ -258,6 +258,72 @@ def reference_band_streams(shapes, rows_per_matrix: int, band_rows: int = 64, se
     return out
 
 
+def ref_gpu_kernel_step(args, shapes) -> dict:
+    """The reference's own fused kernel (lws_gemv_se12, compiled unchanged
+    for sm_100a into oracle/_ref) over the same decode step: every matrix as
+    its own SE12 tensor (183 GEMVs: the kernel takes one codebook per
+    launch), fp32 x as the reference feeds it, its default launch heuristic,
+    all launches in one CUDA graph. Same algorithmic bytes as our line."""
+    import torch
+
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import ref_gpu
+
+    if not torch.cuda.is_available():
+        return {"unavailable": "no GPU"}
+    if not ref_gpu.available():
+        return {"unavailable": "oracle/_ref/libref_kernels.so was not built (no reference tree where build() ran)"}
+    from se12_b200 import _build
+    _build.build()
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    layers = args.layers if args.layers is not None else shapes.layers
+    mats, _ = build_stack(torch, shapes, args.batch, device, layers, True, keep_dense=False, group=False)
+    sms = torch.cuda.get_device_properties(device).multi_processor_count
+    gen = torch.Generator(device=device)
+    gen.manual_seed(1)
+    xs = {kind: torch.randn(args.batch, shapes.input_width(kind), generator=gen, device=device).to(torch.bfloat16)
+          for kind in ("hidden", "attn", "mlp")}
+    x32 = {k: v.float().contiguous() for k, v in xs.items()}
+    refs = [(ref_gpu.RefSe12Gemv(m, sms), x32[kind], torch.empty(args.batch, m.rows, device=device)) for _, m, kind in mats]
+    stream = torch.cuda.Stream(device)
+    stream.wait_stream(torch.cuda.current_stream(device))
+    handle = stream.cuda_stream
+
+    def step():
+        for r, x, y in refs:
+            r.launch(x, y, handle)
+
+    with torch.cuda.stream(stream):
+        step()
+    stream.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step()
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    n = max(3, min(args.steps, 20))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(n):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / n
+    # its output against this package's kernel on the first and last GEMV
+    err = 0.0
+    for (name, m, kind), (r, x, y) in (list(zip(mats, refs))[0], list(zip(mats, refs))[-1]):
+        ours = m.gemv(xs[kind]).double()
+        err = max(err, float(((y.double() - ours).abs() / ours.abs().clamp_min(1.0)).max()))
+    nbytes = sum(m.byte_size + args.batch * m.cols * 2 + args.batch * m.rows * 4 for _, m, _ in mats)
+    del graph, refs
+    return {"kernel": "lws_gemv_se12 (the reference's, src/lws/adapters/cuda/kernels/gemv_se12.cu, compiled unchanged "
+                      "for sm_100a)", "launch": "the reference's default heuristic, one warp per (row, batch)",
+            "gemvs_per_step": len(mats), "ms_per_step": ms, "gbs": nbytes / (ms * 1e-3) / 1e9, "steps": n,
+            "max_rel_diff_vs_ours": err}
+
+
 def run_reference(args) -> None:
     world, rank, _ = dist_info()
     if rank != 0:
@@ -268,6 +334,10 @@ def run_reference(args) -> None:
     # Each step decodes and multiplies a 256-row band of every matrix of one
     # decoder layer (about 7.5 M weights, ~0.1-0.3 s on the host), so that
     # --steps K --warmup W ends within a few minutes for the driver's K.
+    try:
+        ref_gpu_info = ref_gpu_kernel_step(args, shapes)
+    except Exception as exc:  # the CPU arm stands on its own
+        ref_gpu_info = {"unavailable": f"{type(exc).__name__}: {exc}"[:300]}
     bands = reference_band_streams(shapes, 256)
     res = cpu_baseline_sample(shapes, args.batch, max(1, args.steps), max(0, args.warmup), host_streams=bands)
     line = {
@@ -288,6 +358,7 @@ def run_reference(args) -> None:
                    "7 matrices per step", "batch": args.batch},
         "cpu_baseline": {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")},
         "e2e": {"value": res["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "ref_gpu_kernel": ref_gpu_info,
     }
     print(json.dumps(line), flush=True)
 
