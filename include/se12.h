@@ -306,6 +306,20 @@ int se12_decode_rows(const se12_matrix* m, const int32_t* rows_dev, int nrows, u
  * the same pipeline and output contract as se12_gemv (ldw % 8 == 0, W
  * 16-byte aligned). Replaces RawBf16MatVecKernel.multiply and lws_gemv_raw_bf16
  * (src/lws/adapters/cuda/gemv.py:143-172, src/lws/adapters/cuda/kernels/gemv_raw_bf16.cu:18-25). */
+/* The launch bf16_gemv makes for a shape on a GPU with sm_count SMs (host
+ * only), the dense counterpart of se12_gemv_plan. */
+int bf16_gemv_plan(int rows, int cols, int batch, int sm_count, se12_launch_config* out);
+
+/* se12_gemv launched with the configuration bf16_gemv picks for the same
+ * shape (grid, stages, x placement, row mode or stream-K), so that both
+ * kernels reduce in the same order: the order-matched configuration of the
+ * reference's fused-GEMV spec (.spec/features/fused-decode-gemv/spec.md:89-94,
+ * AC-032). On a matrix whose escaped weights all have exponent 0 (zeros and
+ * subnormals) it returns the same bits as bf16_gemv on the decoded weights;
+ * an escape with a non-zero exponent is added outside the tensor-core sum
+ * and may round differently. Same arguments and workspace as se12_gemv. */
+int se12_gemv_order_matched(const se12_matrix* m, const uint16_t* x_dev, int batch, int ldx, float* y_dev, int ldy,
+                            void* workspace_dev, size_t workspace_bytes, void* stream);
 size_t bf16_gemv_workspace_bytes(int rows, int cols, int batch);
 int bf16_gemv(const uint16_t* w_dev, int rows, int cols, int ldw, const uint16_t* x_dev, int batch, int ldx,
               float* y_dev, int ldy, void* workspace_dev, size_t workspace_bytes, void* stream);

@@ -108,6 +108,8 @@ SIGNATURES = {
     "se12_chain_info": (c_int, [c_void_p, ctypes.POINTER(c_int), ctypes.POINTER(c_int), ctypes.POINTER(c_int),
                                 ctypes.POINTER(c_int)]),
     "se12_chain_destroy": (None, [c_void_p]),
+    "bf16_gemv_plan": (c_int, [c_int, c_int, c_int, c_int, ctypes.POINTER(Se12LaunchConfigStruct)]),
+    "se12_gemv_order_matched": (c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p, c_int, c_void_p, c_size_t, c_void_p]),
     "se12_device_status": (c_int, [ctypes.POINTER(c_uint), c_int]),
     "se12_set_wait_limit_ns": (c_int, [ctypes.c_ulonglong]),
     "se12_wait_limit_ns": (c_int, [ctypes.POINTER(ctypes.c_ulonglong)]),

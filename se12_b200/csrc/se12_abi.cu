@@ -462,6 +462,48 @@ int se12_gemv(const se12_matrix* m, const uint16_t* x, int batch, int ldx, float
   return SE12_OK;
 }
 
+int bf16_gemv_plan(int rows, int cols, int batch, int sm_count, se12_launch_config* out) {
+  if (!out || rows <= 0 || cols <= 0 || batch < 1 || batch > SE12_MAX_BATCH || sm_count <= 0)
+    return fail(SE12_ERR_INVALID_ARGUMENT, "bad shape, batch or SM count");
+  fill_launch_config(choose_config(true, tiles_of(rows, cols), cols, batch, sm_count), out);
+  return SE12_OK;
+}
+
+int se12_gemv_order_matched(const se12_matrix* m, const uint16_t* x, int batch, int ldx, float* y, int ldy,
+                            void* workspace, size_t workspace_bytes, void* stream) {
+  if (!m) return fail(SE12_ERR_INVALID_ARGUMENT, "null matrix");
+  int st = check_gemv_io(m->view.rows, m->view.cols, x, batch, ldx, y, ldy);
+  if (st != SE12_OK) return st;
+  // bf16_gemv's configuration for this shape (4-tile stages, never the wide
+  // layout), with the SE12 kernel's own shared-memory size for it
+  LaunchConfig c = choose_config(true, m->view.tiles, m->view.cols, batch, m->sm_count);
+  c.smem = se12::gemv_smem_bytes(false, false, c.x_resident != 0, c.stages, batch, m->view.cols, false);
+  if (c.smem > se12::kMaxSmemPerCta)
+    return fail(SE12_ERR_UNSUPPORTED_DEVICE, "the dense kernel's configuration does not fit the SE12 kernel");
+  const size_t need = workspace_bytes_for(m->view.tile_rows, m->sm_count);
+  if (!workspace || workspace_bytes < need)
+    return fail(SE12_ERR_WORKSPACE_TOO_SMALL, "workspace needs " + std::to_string(need) + " bytes");
+  se12::GemvArgs a{};
+  a.m = m->view;
+  a.x = x;
+  a.ldx = ldx;
+  a.batch = batch;
+  a.y = y;
+  a.ldy = ldy;
+  a.partials = static_cast<float*>(workspace);
+  a.counters = reinterpret_cast<int*>(static_cast<char*>(workspace) + partials_region_bytes(m->sm_count));
+  a.grid = c.grid;
+  a.stages = c.stages;
+  a.x_resident = c.x_resident;
+  a.row_mode = c.row_mode;
+  a.full_tiles = 0;
+  a.wide = 0;
+  cudaError_t err = se12::launch_gemv(false, m->sm_map, m->ec_map, a, c.nblocks, c.smem,
+                                      static_cast<cudaStream_t>(stream), true);
+  if (err != cudaSuccess) return cuda_fail(err, "se12_gemv_order_matched launch");
+  return SE12_OK;
+}
+
 int se12_ipc_handle(const void* dev_ptr, uint8_t* handle_out, uint64_t* offset_out) {
   if (!dev_ptr || !handle_out || !offset_out) return fail(SE12_ERR_INVALID_ARGUMENT, "null argument");
   auto range = address_range_query();

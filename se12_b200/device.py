@@ -235,9 +235,12 @@ class DeviceSe12Matrix:
                 + self.fallback_tiles * TILE_SIZE * 2 + CODEBOOK_SIZE * len(self.segments))
 
     # ------------------------------------------------------------------ compute
-    def gemv(self, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
-        """y[B, N] = x[B, K] . W^T in fp32 (x: BF16 or fp32, [K] or [B, K])."""
-        return gemv_call(self, x, out)
+    def gemv(self, x: torch.Tensor, out: torch.Tensor | None = None, order_matched: bool = False) -> torch.Tensor:
+        """y[B, N] = x[B, K] . W^T in fp32 (x: BF16 or fp32, [K] or [B, K]).
+        ``order_matched``: in bf16_gemv's launch configuration, so that the
+        result equals the dense kernel's bit for bit on matrices without
+        escapes of non-zero exponent (the reference spec's AC-032)."""
+        return gemv_call(self, x, out, order_matched=order_matched)
 
     def launch_config(self, batch: int = 1) -> dict:
         """The launch se12_gemv makes for this matrix at this batch size."""
@@ -293,8 +296,11 @@ def _split_fp32(x: torch.Tensor) -> list:
     return [hi, mid, lo]
 
 
-def gemv_call(m: DeviceSe12Matrix, x: torch.Tensor, out: torch.Tensor | None = None, raw_weights: torch.Tensor | None = None) -> torch.Tensor:
-    """Shared GEMV driver for the fused SE12 kernel and the dense baseline."""
+def gemv_call(m: DeviceSe12Matrix, x: torch.Tensor, out: torch.Tensor | None = None, raw_weights: torch.Tensor | None = None,
+              order_matched: bool = False) -> torch.Tensor:
+    """Shared GEMV driver for the fused SE12 kernel and the dense baseline
+    (``order_matched``: the SE12 kernel in the dense kernel's launch
+    configuration, se12_gemv_order_matched)."""
     rows, cols = (m.rows, m.cols) if m is not None else raw_weights.shape
     device = x.device
     squeeze = x.dim() == 1
@@ -303,7 +309,7 @@ def gemv_call(m: DeviceSe12Matrix, x: torch.Tensor, out: torch.Tensor | None = N
         raise ValueError(f"x has {x2.shape[-1]} columns, matrix has {cols}")
     if x2.dtype == torch.float32:
         parts = _split_fp32(x2)
-        ys = [gemv_call(m, p, None, raw_weights) for p in parts]
+        ys = [gemv_call(m, p, None, raw_weights, order_matched) for p in parts]
         y = (ys[0] + ys[1]) + ys[2]
         if out is not None:
             out.copy_(y)
@@ -326,7 +332,8 @@ def gemv_call(m: DeviceSe12Matrix, x: torch.Tensor, out: torch.Tensor | None = N
             if m is not None:
                 need = _lib.load().se12_gemv_workspace_bytes(m.handle, MAX_BATCH)
                 ws = WORKSPACES.get(device, stream, need)
-                _lib.call("se12_gemv", m.handle, ctypes.c_void_p(xb.data_ptr()), nb, xb.stride(0),
+                _lib.call("se12_gemv_order_matched" if order_matched else "se12_gemv", m.handle,
+                          ctypes.c_void_p(xb.data_ptr()), nb, xb.stride(0),
                           ctypes.c_void_p(yb.data_ptr()), yb.stride(0), ctypes.c_void_p(ws.data_ptr()), ws.numel(),
                           ctypes.c_void_p(stream))
             else:
