@@ -658,19 +658,12 @@ def run_ours(args) -> None:
         raise RuntimeError(f"device status word is {status}: a kernel reported an error")
 
     # ----------------------------------------------------------- CPU baseline (rank 0)
+    # the same measurement as the --impl reference arm: 256-row bands (64-row
+    # pieces) of one decoder layer's seven matrices per step, all host threads
     cpu = None
     if rank == 0 and not args.no_cpu:
-        sys.path.insert(0, str(ROOT / "oracle"))
-        import se12_oracle as oracle
-
-        host_streams = []
-        for (name, m, kind) in mats:  # the first layer's seven matrices (segments of a group included)
-            for t in m.segment_tensors():
-                if len(host_streams) < 7:
-                    host_streams.append((oracle.Streams(rows=t.rows, cols=t.cols, codebook=t.codebook, sm=t.sm, ec=t.ec,
-                                                        esc=t.esc, fallback_bitmap=t.fallback_bitmap,
-                                                        fallback_raw=t.fallback_raw), kind))
-        res = cpu_baseline_sample(shapes, batch, steps=2, warmup=1, host_streams=host_streams)
+        bands = reference_band_streams(shapes, 256)
+        res = cpu_baseline_sample(shapes, batch, steps=2, warmup=1, host_streams=bands)
         cpu = {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")}
 
     if rank == 0:
