@@ -779,18 +779,28 @@ __global__ void __launch_bounds__(gemv_threads(WIDE), WIDE ? 1 : 2) gemv_kernel(
   // escape e as position | exponent << 16, or 0 for an unused slot and for
   // an escape whose exponent is 0 (zeros and BF16 subnormals: exact
   // already).
+  // The lanes of row group g (rows g and g + 8) take the escapes of their
+  // rows, the groups side by side: iteration k gives every group its k-th
+  // escape, so a tile's escapes cost as many iterations as the fullest
+  // group holds, not one per escape.
   auto fix_escapes = [&](int s, int kt, uint32_t rec) {
     const uint32_t wst = o_w + s * kWeightBytes;
     // whole tiles: all of the tile's escapes; else those in this warp's half
     const bool mine = rec > 0xFFFFu && (kTilePerWarp || ((rec >> 7) & 1u) == static_cast<uint32_t>(hw));
-    unsigned pending = __ballot_sync(0xFFFFFFFFu, mine);
-    while (pending) {
-      const int e = __ffs(pending) - 1;
+    const unsigned any = __ballot_sync(0xFFFFFFFFu, mine);
+    if (!any) return;
+    const uint32_t grp = (rec >> 8) & 7u;  // row group of this lane's escape
+    const unsigned b1 = __ballot_sync(0xFFFFFFFFu, grp & 1u), b2 = __ballot_sync(0xFFFFFFFFu, grp & 2u),
+                   b4 = __ballot_sync(0xFFFFFFFFu, grp & 4u);
+    unsigned pending = any & ((g & 1) ? b1 : ~b1) & ((g & 2) ? b2 : ~b2) & ((g & 4) ? b4 : ~b4);
+    const unsigned rounds = __reduce_max_sync(0xFFFFFFFFu, static_cast<unsigned>(__popc(pending)));
+    for (unsigned k = 0; k < rounds; ++k) {
+      const int e = pending ? __ffs(pending) - 1 : 31;  // lane 31 holds no escape
       pending &= pending - 1;
       const uint32_t erec = __shfl_sync(0xFFFFFFFFu, rec, e);
       const uint32_t eex = erec >> 16;
       const uint32_t r = (erec >> 8) & 255u, c = erec & 255u;
-      if ((r & 7) == static_cast<uint32_t>(g)) {
+      if (erec > 0xFFFFu) {
         const uint32_t L = 2 * (16 * jw + r) + (c >> 7), bc = c & 127;  // 128-byte line of the sm byte
         const uint32_t smb = sm8[wst + L * 128 + (((bc >> 4) ^ (L & 7)) << 4) + (bc & 15)];
         const float wv = bf16_bits_to_float(bf16_bits(smb, eex));
