@@ -42,14 +42,14 @@ ROOT = pathlib.Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 METRIC = "SE12 decode+GEMV HBM GB/s (compressed bytes)"
-# DRAM bytes (read + write) per algorithmic byte of the fused GEMV, from one
-# ncu capture of this script's lm_head GEMV (--layers 0 --eager: 256000 x
-# 2304, batch 1, the wide layout): 897.52 MB of DRAM traffic for 888.09 MB of
-# SE12 streams + x + y; the difference is mostly the derived escape-position
-# table (32 B per tile) and the fallback index. The step's GEMVs stream the
-# same kinds of data in proportion, so the step's traffic is scaled from it
-# by algorithmic bytes.
-DRAM_BYTES_PER_ALGORITHMIC_BYTE = 897.52 / 888.09
+# DRAM bytes (read + write) per algorithmic byte of each GEMV class, from
+# one ncu capture of every class of the step (profiles/dram_traffic_
+# gemma2-2b_decode_step_b1.md: three counters per launch); the excess is the
+# derived escape-position and fallback-index tables. The step's traffic is
+# the sum over its launches of ratio x algorithmic bytes.
+DRAM_BYTES_PER_ALGORITHMIC_BYTE = {"qkv_proj": 1.0095, "o_proj": 1.0140, "gate_up_proj": 1.0057, "down_proj": 1.0079,
+                                   "lm_head": 1.0073}
+DRAM_RATIO_OTHER = 1.0140  # classes without a capture (ungrouped projections): the largest measured ratio
 NOMINAL_HBM_GBS = 8000.0
 
 
@@ -565,6 +565,8 @@ def run_ours(args) -> None:
         elapsed_ms = float(t.item())
     ms_per_step = elapsed_ms / args.steps
     bytes_per_step = step_bytes(batch)
+    traffic_per_step = sum(DRAM_BYTES_PER_ALGORITHMIC_BYTE.get(name.rsplit(".", 1)[-1], DRAM_RATIO_OTHER)
+                           * (m.byte_size + batch * m.cols * 2 + batch * m.rows * 4) for name, m, _ in mats)
     value = world * bytes_per_step / (ms_per_step * 1e-3) / 1e9
     launches = stack.launches
 
@@ -709,8 +711,9 @@ def run_ours(args) -> None:
                 "peak": peak,
                 "unit": "GB/s",
                 "frac": achieved / peak,
-                "traffic": bytes_per_step * DRAM_BYTES_PER_ALGORITHMIC_BYTE,
-                "traffic_unit": "bytes per step (all launches), scaled from the ncu capture of the lm_head GEMV",
+                "traffic": traffic_per_step,
+                "traffic_unit": "bytes per step (all launches): each launch's algorithmic bytes times its GEMV "
+                                "class's measured DRAM ratio (ncu, one launch per class)",
                 "kernel": f"se12::gemv_kernel<{1 if batch <= 8 else 2},SE12,...> (all {len(mats)} launches of the step, "
                 "8-tile-stage and wide-layout variants)",
                 "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)" if "source" not in peaks else "fallback",
