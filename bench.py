@@ -61,7 +61,7 @@ def parse_args():
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
     p.add_argument("--config", default="gemma2-2b")
     p.add_argument("--batch", type=int, default=1)
-    p.add_argument("--extra-batches", default="4,16", help="batch sizes timed as extra fields ('' to skip)")
+    p.add_argument("--extra-batches", default="2,4,8,16", help="batch sizes timed as extra fields ('' to skip)")
     p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     p.add_argument("--no-dense", action="store_true", help="skip the dense BF16 comparisons")
     p.add_argument("--layers", type=int, default=None, help="override the layer count (profiling small cases)")
@@ -83,7 +83,10 @@ def parse_args():
     p.add_argument("--no-tp", action="store_true",
                    help="skip the tensor-parallel leg (the --tp-config step sharded over the torchrun ranks, reported "
                         "as the line's tp object)")
-    p.add_argument("--tp-config", default="gemma2-27b", help="model of the tensor-parallel leg")
+    p.add_argument("--tp-config", default="gemma2-27b", help="model of the tensor-parallel leg (Megatron split)")
+    p.add_argument("--tp-rows-config", default="gemma2-9b",
+                   help="model of the row-sharded leg (every GEMV by output rows, NCCL all-gather of each output)")
+    p.add_argument("--tp-split", choices=("megatron", "rows"), default="megatron", help="--tp: how the step is sharded")
     p.add_argument("--sweep", action="store_true",
                    help="escape-stress sweep (baseline config 4): one 8192 x 28672 matrix over weight scales and "
                         "outlier rates; bits/weight, fallback tiles and GEMV GB/s per point")
@@ -735,8 +738,12 @@ def run_ours(args) -> None:
         torch.cuda.synchronize()
         torch.cuda.empty_cache()
         tp = tp_leg(args, torch, world, rank, local, device)
+        # baseline config 2: Gemma-2-9B, every GEMV row-sharded, each output
+        # all-gathered over NCCL (output-parallel)
+        tp_rows = tp_leg(args, torch, world, rank, local, device, config=args.tp_rows_config, split="rows")
         if rank == 0:
             line["tp"] = tp
+            line["tp_rows"] = tp_rows
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -744,22 +751,22 @@ def run_ours(args) -> None:
         torch.distributed.destroy_process_group()
 
 
-def tp_leg(args, torch, world, rank, local, device):
-    """The tensor-parallel decode step of --tp-config over all ranks (one rank:
-    the whole model on one GPU), and at N > 1 the same model on rank 0's GPU
-    alone, for the strong-scaling efficiency T1 / (N * TN)."""
+def tp_leg(args, torch, world, rank, local, device, config=None, split="megatron"):
+    """A tensor-parallel decode step over all ranks (one rank: the whole
+    model on one GPU), and at N > 1 the same model on rank 0's GPU alone,
+    for the strong-scaling efficiency T1 / (N * TN)."""
     from se12_b200.shapes import CONFIGS
 
-    shapes = CONFIGS[args.tp_config]
+    shapes = CONFIGS[config or args.tp_config]
     sampler = ClockSampler(local)
-    res = tp_measure(args, torch, shapes, world, rank, local, device, sampler=sampler)
+    res = tp_measure(args, torch, shapes, world, rank, local, device, sampler=sampler, split=split)
     res["clocks"] = sampler.summary()
     if world > 1:
         import torch.distributed as dist
 
         one = None
         if rank == 0:
-            one = tp_measure(args, torch, shapes, 1, 0, local, device, check=False)
+            one = tp_measure(args, torch, shapes, 1, 0, local, device, check=False, split=split)
         dist.barrier()
         if rank == 0:
             res["one_gpu_ms_per_step"] = one["ms_per_step"]
@@ -769,7 +776,7 @@ def tp_leg(args, torch, world, rank, local, device):
         res["one_gpu_ms_per_step"] = res["ms_per_step"]
         res["strong_efficiency"] = 1.0
         res["speedup_vs_one_gpu"] = 1.0
-    res["scaling"] = "strong: the same model at every N, Megatron-sharded over the N ranks"
+    res["scaling"] = f"strong: the same model at every N, {'Megatron-' if split == 'megatron' else 'row-'}sharded over the N ranks"
     return res
 
 
@@ -781,6 +788,7 @@ class TpOp:
     def __init__(self, names, layer, plan, m, x, y, coll, seeds, dims):
         self.names, self.layer, self.plan, self.m, self.x, self.y = names, layer, plan, m, x, y
         self.coll, self.seeds, self.dims = coll, seeds, dims
+        self.gathered = None  # [world, B, rows] for an all-gathered output (world > 1)
 
 
 def tp_specs(shapes, group=True):
@@ -808,10 +816,12 @@ def tp_shard_weights(torch, plan, rows, cols, seed, world, rank, device):
     return synthetic_bf16(torch, rows, c1 - c0, seed * 64 + rank, device)
 
 
-def tp_build(torch, shapes, layers, batch, world, rank, device, group=True, lm_head=True):
-    """This rank's part of the Megatron split of every GEMV of a decode step:
+def tp_build(torch, shapes, layers, batch, world, rank, device, group=True, lm_head=True, split="megatron"):
+    """This rank's part of every GEMV of a decode step. ``split="megatron"``:
     q/k/v/gate/up by output rows, o/down by input columns (all-reduce after),
-    the LM head by rows (all-gather after). Returns (ops, local bytes)."""
+    the LM head by rows (all-gather after). ``split="rows"``: every GEMV by
+    output rows, each output all-gathered (output-parallel). Returns (ops,
+    local bytes)."""
     from se12_b200.codec import encode_device
     from se12_b200.device import DeviceSe12Matrix
     from se12_b200.sharding import megatron_plan
@@ -827,7 +837,7 @@ def tp_build(torch, shapes, layers, batch, world, rank, device, group=True, lm_h
     ops, local_bytes = [], 0
     for layer, names in seqs:
         parts, seeds, ds = [], [], []
-        plan = megatron_plan(names[0])
+        plan = megatron_plan(names[0]) if split == "megatron" else "rows"
         for name in names:
             rows, cols = dims[name] if layer is not None else shapes.lm_head()[1:3]
             seed = 1000 * layer + order[name] if layer is not None else 999_999
@@ -838,14 +848,14 @@ def tp_build(torch, shapes, layers, batch, world, rank, device, group=True, lm_h
         del parts
         x = x_full if plan == "rows" else torch.randn(batch, m.cols, generator=gen, device=device).to(torch.bfloat16)
         y = torch.empty(batch, m.rows, dtype=torch.float32, device=device)
-        coll = "all_reduce" if plan == "cols" else ("all_gather" if names[0] == "lm_head" else None)
+        coll = "all_reduce" if plan == "cols" else ("all_gather" if (names[0] == "lm_head" or split == "rows") else None)
         ops.append(TpOp(names, layer, plan, m, x, y, coll, seeds, ds))
         local_bytes += m.byte_size + batch * m.cols * 2 + batch * m.rows * 4
     torch.cuda.synchronize()
     return ops, local_bytes
 
 
-def tp_time(torch, ops, world, device, steps, warmup, fused_peers=None, logits=None, sampler=None):
+def tp_time(torch, ops, world, device, steps, warmup, fused_peers=None, sampler=None):
     """Captures the step (GEMVs and collectives) in one CUDA graph, replays
     it ``warmup`` times, then times ``steps`` replays with CUDA events.
     Returns (max-over-ranks ms per step, graph)."""
@@ -862,7 +872,7 @@ def tp_time(torch, ops, world, device, steps, warmup, fused_peers=None, logits=N
             if world > 1 and op.coll == "all_reduce":
                 dist.all_reduce(op.y)
             elif world > 1 and op.coll == "all_gather":
-                dist.all_gather_into_tensor(logits, op.y)
+                dist.all_gather_into_tensor(op.gathered, op.y)
 
     stream = torch.cuda.Stream(device)
     stream.wait_stream(torch.cuda.current_stream(device))
@@ -892,12 +902,13 @@ def tp_time(torch, ops, world, device, steps, warmup, fused_peers=None, logits=N
     return float(t.item()) / steps, graph
 
 
-def tp_check(torch, ops, world, rank, device, logits=None, sample_rows=1024):
+def tp_check(torch, ops, world, rank, device, sample_rows=1024):
     """Checks the outputs the last step left against float64 products of the
     same BF16 weights (regenerated from the shard seeds), for the first
     layer's GEMVs and the LM head. Row shards: this rank's rows; column
     shards: the all-reduced rows (the sum over every rank's shard and x);
-    LM head: a row sample of every rank's part of the all-gathered logits.
+    all-gathered outputs (the LM head; every GEMV of a row-sharded split): a
+    row sample of every rank's part of the gathered output.
     Returns max |y - y64| / max(|y64|, 1) over the checked outputs and ranks."""
     import torch.distributed as dist
 
@@ -920,15 +931,17 @@ def tp_check(torch, ops, world, rank, device, logits=None, sample_rows=1024):
                 y64 += xs[r].to(device).double() @ w.double().T
                 del w
             worst = max(worst, err(op.y, y64))
-        elif op.names[0] == "lm_head":
-            (rows, cols), seed = op.dims[0], op.seeds[0]
-            parts = range(world) if (world > 1 and logits is not None) else [rank]
+        elif op.coll == "all_gather":
+            # every rank's part of the gathered output (a row sample of it),
+            # against that rank's shard weights (all members of a group)
+            parts = range(world) if op.gathered is not None else [rank]
             for r in parts:
-                w = tp_shard_weights(torch, "rows", rows, cols, seed, world, r, device)
+                w = torch.cat([tp_shard_weights(torch, "rows", rows, cols, seed, world, r, device)
+                               for (rows, cols), seed in zip(op.dims, op.seeds)])
                 g = torch.Generator(device="cpu").manual_seed(17 + r)
                 ids = torch.randint(0, w.shape[0], (min(sample_rows, w.shape[0]),), generator=g).to(device)
                 y64 = op.x.double() @ w[ids].double().T
-                got = (logits[r] if (world > 1 and logits is not None) else op.y)[:, ids]
+                got = (op.gathered[r] if op.gathered is not None else op.y)[:, ids]
                 worst = max(worst, err(got, y64))
                 del w
         else:
@@ -944,10 +957,11 @@ def tp_check(torch, ops, world, rank, device, logits=None, sample_rows=1024):
     return float(t.item())
 
 
-def tp_measure(args, torch, shapes, world, rank, local, device, sampler=None, check=True):
+def tp_measure(args, torch, shapes, world, rank, local, device, sampler=None, check=True, split="megatron"):
     """Builds, times and (optionally) checks the tensor-parallel decode step
-    of ``shapes`` on ``world`` ranks (world 1: the whole model on this GPU).
-    The process group, if any, is already initialised."""
+    of ``shapes`` on ``world`` ranks (world 1: the whole model on this GPU),
+    split as tp_build's ``split``. The process group, if any, is already
+    initialised."""
     import torch.distributed as dist
 
     from se12_b200.device import device_status
@@ -956,22 +970,24 @@ def tp_measure(args, torch, shapes, world, rank, local, device, sampler=None, ch
     batch = args.batch
     t0 = time.perf_counter()
     ops, local_bytes = tp_build(torch, shapes, layers, batch, world, rank, device, group=not args.no_group,
-                                lm_head=not args.no_lm_head)
+                                lm_head=not args.no_lm_head, split=split)
     setup_s = time.perf_counter() - t0
-    lm_rows = ops[-1].y.shape[1] if not args.no_lm_head else 0
-    logits = torch.empty(world, batch, lm_rows, dtype=torch.float32, device=device) if (lm_rows and world > 1) else None
-    fused = world > 1 and args.tp_allreduce == "fused"
+    if world > 1:
+        for op in ops:
+            if op.coll == "all_gather":
+                op.gathered = torch.empty(world, batch, op.y.shape[1], dtype=torch.float32, device=device)
+    fused = world > 1 and args.tp_allreduce == "fused" and any(op.coll == "all_reduce" for op in ops)
     peers = None
     if fused:
         from se12_b200.peers import PeerGroup
 
         peers = PeerGroup(rows_cap=max(op.m.rows for op in ops if op.coll == "all_reduce"), device=device)
-    ms, graph = tp_time(torch, ops, world, device, args.steps, args.warmup, fused_peers=peers, logits=logits, sampler=sampler)
+    ms, graph = tp_time(torch, ops, world, device, args.steps, args.warmup, fused_peers=peers, sampler=sampler)
     del graph
     status = device_status()
     if status:
         raise RuntimeError(f"device status word is {status}: a kernel reported an error")
-    max_err = tp_check(torch, ops, world, rank, device, logits=logits) if check else None
+    max_err = tp_check(torch, ops, world, rank, device) if check else None
     total = torch.tensor([float(local_bytes)], device=device, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(total)
@@ -982,10 +998,13 @@ def tp_measure(args, torch, shapes, world, rank, local, device, sampler=None, ch
         "config": shapes.name, "layers": layers, "batch": batch, "n_gpus": world, "weights": weights,
         "gemvs_per_step": len(ops), "bytes_per_step": float(total.item()), "ms_per_step": ms,
         "gbs": float(total.item()) / (ms * 1e-3) / 1e9, "tok_s": batch / (ms * 1e-3),
-        "allreduce": ("fused into the GEMV over peer memory" if fused else "NCCL") if world > 1 else None,
+        "split": split,
+        "allreduce": (("fused into the GEMV over peer memory" if fused else "NCCL")
+                      if any(op.coll == "all_reduce" for op in ops) else None) if world > 1 else None,
+        "allgathers_per_step": sum(op.coll == "all_gather" for op in ops) if world > 1 else 0,
         "max_rel_err_vs_fp64": max_err, "setup_seconds": setup_s,
     }
-    del ops, logits
+    del ops
     torch.cuda.empty_cache()
     return res
 
@@ -1016,7 +1035,7 @@ def run_tp(args) -> None:
         dist.barrier()
     shapes = CONFIGS[args.config if args.config != "gemma2-2b" else "gemma2-27b"]
     sampler = ClockSampler(local)
-    res = tp_measure(args, torch, shapes, world, rank, local, device, sampler=sampler)
+    res = tp_measure(args, torch, shapes, world, rank, local, device, sampler=sampler, split=args.tp_split)
     if rank == 0:
         fused = res["allreduce"] is not None and res["allreduce"].startswith("fused")
         line = {
@@ -1026,9 +1045,11 @@ def run_tp(args) -> None:
             "config": {"workload": f"{shapes.name} tensor-parallel decode-step GEMV set: {res['layers']} layers + lm_head, "
                        f"batch {res['batch']}", "batch": res["batch"], "weights": res["weights"],
                        "gemvs_per_step": res["gemvs_per_step"], "bytes_per_step": res["bytes_per_step"],
-                       "parallelism": f"tp{world}: q/k/v/gate/up by rows, o/down by columns + "
-                       + ("all-reduce fused into the GEMV (peer memory)" if fused else "NCCL all-reduce")
-                       + ", lm_head by rows + NCCL all-gather; one CUDA graph per step",
+                       "parallelism": (f"tp{world}: q/k/v/gate/up by rows, o/down by columns + "
+                                       + ("all-reduce fused into the GEMV (peer memory)" if fused else "NCCL all-reduce")
+                                       + ", lm_head by rows + NCCL all-gather; one CUDA graph per step")
+                       if args.tp_split == "megatron" else
+                       f"tp{world}: every GEMV by output rows + NCCL all-gather of each output; one CUDA graph per step",
                        "setup_seconds": res["setup_seconds"]},
             "tok_s": res["tok_s"], "per_gpu_gbs": res["gbs"] / world, "allreduce": res["allreduce"],
             "max_rel_err_vs_fp64": res["max_rel_err_vs_fp64"], "clocks": sampler.summary(),
