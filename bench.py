@@ -846,7 +846,10 @@ def tp_build(torch, shapes, layers, batch, world, rank, device, group=True, lm_h
             ds.append((rows, cols))
         m = DeviceSe12Matrix.concatenate(parts) if len(parts) > 1 else parts[0]
         del parts
-        x = x_full if plan == "rows" else torch.randn(batch, m.cols, generator=gen, device=device).to(torch.bfloat16)
+        # row shards read the whole input: the hidden state (q/k/v, gate/up,
+        # LM head) or, in the row-sharded split, o's and down's own inputs
+        x = (x_full if (plan == "rows" and m.cols == shapes.hidden)
+             else torch.randn(batch, m.cols, generator=gen, device=device).to(torch.bfloat16))
         y = torch.empty(batch, m.rows, dtype=torch.float32, device=device)
         coll = "all_reduce" if plan == "cols" else ("all_gather" if (names[0] == "lm_head" or split == "rows") else None)
         ops.append(TpOp(names, layer, plan, m, x, y, coll, seeds, ds))
