@@ -737,10 +737,19 @@ def run_ours(args) -> None:
         del stack, xs, outs, e2e_stack, e2e_xs, e2e_outs, mats, dense, host_in, host_out, logits
         torch.cuda.synchronize()
         torch.cuda.empty_cache()
-        tp = tp_leg(args, torch, world, rank, local, device)
+        def leg(**kw):
+            # a leg that fails (the same way on every rank) leaves its error
+            # in the line instead of the line
+            try:
+                return tp_leg(args, torch, world, rank, local, device, **kw)
+            except Exception as exc:
+                torch.cuda.synchronize()
+                return {"error": f"{type(exc).__name__}: {exc}"[:300]}
+
+        tp = leg()
         # baseline config 2: Gemma-2-9B, every GEMV row-sharded, each output
         # all-gathered over NCCL (output-parallel)
-        tp_rows = tp_leg(args, torch, world, rank, local, device, config=args.tp_rows_config, split="rows")
+        tp_rows = leg(config=args.tp_rows_config, split="rows")
         if rank == 0:
             line["tp"] = tp
             line["tp_rows"] = tp_rows
