@@ -220,3 +220,71 @@ def test_lost_peer_makes_the_fused_allreduce_time_out(tmp_path):
     assert r0["timed_out"], r0
     assert r0["elapsed"] < 10.0, r0
     assert r1["status"] == 0, r1
+
+
+def _chain_allreduce_main(rank, world, port, result_path):
+    import datetime
+
+    import torch.distributed as dist
+
+    from se12_b200.chain import Se12Chain
+    from se12_b200.device import device_status
+    from se12_b200.format import make_tensor
+    from se12_b200.peers import PeerGroup
+    from se12_b200.sharding import col_range, shard_matrix
+
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", rank))
+    out = {}
+    try:
+        mats = {}
+        for name, rows, cols, seed in (("a", 1040, 4608, 8), ("b", 2304, 2048, 9)):
+            bits, _, _ = cases.synthetic_weights(rows, cols, seed=seed, outlier_rate=2e-3, outlier_scale=256.0)
+            s = oracle.encode(np.asarray(bits, dtype=np.uint16), rows, cols)
+            t = make_tensor(s.rows, s.cols, s.codebook, s.sm, s.ec, s.esc, s.fallback_bitmap, s.fallback_raw)
+            mats[name] = (bits, rows, cols, shard_matrix(t, "cols", world, rank, device=f"cuda:{rank}").matrix)
+        peers = PeerGroup(rows_cap=2304)
+        batch = 2
+        chain = Se12Chain(batch)
+        entries = []
+        for n, name in enumerate(("a", "b", "a")):
+            bits, rows, cols, m = mats[name]
+            xb = oracle.bf16_round(np.random.default_rng(10 + n).normal(size=(batch, cols)).astype(np.float32))
+            c0, c1 = col_range(cols, world, rank)
+            x = torch.from_numpy(xb.view(np.int16)).view(torch.bfloat16).cuda()[:, c0:c1].contiguous()
+            y = torch.full((batch, rows), float("nan"), device="cuda")
+            chain.add(m, x, y, peers=peers)
+            entries.append((bits, rows, cols, xb, y))
+        errs, same = [], []
+        for _ in range(2):  # two launches: the epochs continue across them
+            chain.run()
+            torch.cuda.synchronize()
+            for bits, rows, cols, xb, y in entries:
+                y64 = oracle.gemv_fp64(bits, rows, cols, oracle.bits_to_float32(xb))
+                errs.append(oracle.max_relative_error(y.cpu().numpy(), y64))
+                everyone = [torch.empty_like(y) for _ in range(world)]
+                dist.all_gather(everyone, y)
+                same.append(all(torch.equal(everyone[0], e) for e in everyone))
+        out = {"errs": errs, "same": same, "status": device_status()}
+        del chain
+        peers.close()
+    finally:
+        torch.save(out, f"{result_path}.{rank}")
+        dist.destroy_process_group()
+
+
+def test_chain_with_allreduced_ops(tmp_path):
+    """A chain whose ops are column shards all-reduced over the peer group
+    inside the persistent kernel: within 1e-3 of the fp64 oracle, the same
+    bits on every rank, over two launches."""
+    import torch.multiprocessing as mp
+
+    _need(2)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    mp.spawn(_chain_allreduce_main, args=(2, _free_port(), str(tmp_path / "chain")), nprocs=2, join=True)
+    for r in range(2):
+        res = torch.load(tmp_path / f"chain.{r}")
+        assert res["status"] == 0, res
+        assert max(res["errs"]) <= TOLERANCE, res["errs"]
+        assert all(res["same"]), res["same"]
