@@ -67,8 +67,8 @@ def parse_args():
     p.add_argument("--layers", type=int, default=None, help="override the layer count (profiling small cases)")
     p.add_argument("--no-lm-head", action="store_true")
     p.add_argument("--tp-allreduce", choices=("fused", "nccl"), default="fused",
-                   help="--tp: column-sharded layers as one GEMV + all-reduce kernel over peer memory (fused) or a "
-                        "GEMV followed by an NCCL all-reduce")
+                   help="tensor-parallel legs: the all-reduce (Megatron split) and the all-gather (row split) fused "
+                        "into the GEMV kernel over peer memory, or a GEMV followed by an NCCL collective")
     p.add_argument("--offload-gb", type=float, default=None,
                    help="weight-offload mode: decoder layers beyond this VRAM budget (GB) stream from pinned host "
                         "memory every token; SE12 and BF16 on the same pipeline")
@@ -85,7 +85,7 @@ def parse_args():
                         "as the line's tp object)")
     p.add_argument("--tp-config", default="gemma2-27b", help="model of the tensor-parallel leg (Megatron split)")
     p.add_argument("--tp-rows-config", default="gemma2-9b",
-                   help="model of the row-sharded leg (every GEMV by output rows, NCCL all-gather of each output)")
+                   help="model of the row-sharded leg (every GEMV by output rows, each output all-gathered)")
     p.add_argument("--tp-split", choices=("megatron", "rows"), default="megatron", help="--tp: how the step is sharded")
     p.add_argument("--sweep", action="store_true",
                    help="escape-stress sweep (baseline config 4): one 8192 x 28672 matrix over weight scales and "
@@ -748,7 +748,8 @@ def run_ours(args) -> None:
 
         tp = leg()
         # baseline config 2: Gemma-2-9B, every GEMV row-sharded, each output
-        # all-gathered over NCCL (output-parallel)
+        # all-gathered (output-parallel; fused into the GEMV over peer
+        # memory, or NCCL with --tp-allreduce nccl)
         tp_rows = leg(config=args.tp_rows_config, split="rows")
         if rank == 0:
             line["tp"] = tp
@@ -797,7 +798,8 @@ class TpOp:
     def __init__(self, names, layer, plan, m, x, y, coll, seeds, dims):
         self.names, self.layer, self.plan, self.m, self.x, self.y = names, layer, plan, m, x, y
         self.coll, self.seeds, self.dims = coll, seeds, dims
-        self.gathered = None  # [world, B, rows] for an all-gathered output (world > 1)
+        self.gathered = None  # the all-gathered output (world > 1): NCCL [world, B, rows], fused [B, world x rows]
+        self.fused_gather = False
 
 
 def tp_specs(shapes, group=True):
@@ -880,6 +882,10 @@ def tp_time(torch, ops, world, device, steps, warmup, fused_peers=None, sampler=
             if fused_peers is not None and op.coll == "all_reduce":
                 fused_peers.gemv_allreduce(op.m, op.x, op.y)
                 continue
+            if op.fused_gather:
+                n = op.m.rows
+                fused_peers.gemv_allgather(op.m, op.x, fused_peers.rank * n, fused_peers.world * n, out=op.gathered)
+                continue
             gemv_call(op.m, op.x, op.y)
             if world > 1 and op.coll == "all_reduce":
                 dist.all_reduce(op.y)
@@ -953,7 +959,14 @@ def tp_check(torch, ops, world, rank, device, sample_rows=1024):
                 g = torch.Generator(device="cpu").manual_seed(17 + r)
                 ids = torch.randint(0, w.shape[0], (min(sample_rows, w.shape[0]),), generator=g).to(device)
                 y64 = op.x.double() @ w[ids].double().T
-                got = (op.gathered[r] if op.gathered is not None else op.y)[:, ids]
+                if op.gathered is None:
+                    part = op.y
+                elif op.fused_gather:
+                    n = op.y.shape[1]
+                    part = op.gathered[:, r * n:(r + 1) * n]
+                else:
+                    part = op.gathered[r]
+                got = part[:, ids]
                 worst = max(worst, err(got, y64))
                 del w
         else:
@@ -984,16 +997,21 @@ def tp_measure(args, torch, shapes, world, rank, local, device, sampler=None, ch
     ops, local_bytes = tp_build(torch, shapes, layers, batch, world, rank, device, group=not args.no_group,
                                 lm_head=not args.no_lm_head, split=split)
     setup_s = time.perf_counter() - t0
+    fused = world > 1 and args.tp_allreduce == "fused" and (split == "rows" or any(op.coll == "all_reduce" for op in ops))
     if world > 1:
         for op in ops:
             if op.coll == "all_gather":
-                op.gathered = torch.empty(world, batch, op.y.shape[1], dtype=torch.float32, device=device)
-    fused = world > 1 and args.tp_allreduce == "fused" and any(op.coll == "all_reduce" for op in ops)
+                # the row split gathers inside the GEMV kernel (every rank's
+                # part the same size here: row shards of 16-row multiples)
+                op.fused_gather = fused and split == "rows"
+                shape = (batch, world * op.y.shape[1]) if op.fused_gather else (world, batch, op.y.shape[1])
+                op.gathered = torch.empty(*shape, dtype=torch.float32, device=device)
     peers = None
     if fused:
         from se12_b200.peers import PeerGroup
 
-        peers = PeerGroup(rows_cap=max(op.m.rows for op in ops if op.coll == "all_reduce"), device=device)
+        peers = PeerGroup(rows_cap=max(op.m.rows for op in ops if op.coll == "all_reduce" or op.fused_gather),
+                          device=device)
     ms, graph = tp_time(torch, ops, world, device, args.steps, args.warmup, fused_peers=peers, sampler=sampler)
     del graph
     status = device_status()
@@ -1013,6 +1031,8 @@ def tp_measure(args, torch, shapes, world, rank, local, device, sampler=None, ch
         "split": split,
         "allreduce": (("fused into the GEMV over peer memory" if fused else "NCCL")
                       if any(op.coll == "all_reduce" for op in ops) else None) if world > 1 else None,
+        "allgather": (("fused into the GEMV over peer memory" if any(op.fused_gather for op in ops) else "NCCL")
+                      if any(op.coll == "all_gather" for op in ops) else None) if world > 1 else None,
         "allgathers_per_step": sum(op.coll == "all_gather" for op in ops) if world > 1 else 0,
         "max_rel_err_vs_fp64": max_err, "setup_seconds": setup_s,
     }
@@ -1061,7 +1081,8 @@ def run_tp(args) -> None:
                                        + ("all-reduce fused into the GEMV (peer memory)" if fused else "NCCL all-reduce")
                                        + ", lm_head by rows + NCCL all-gather; one CUDA graph per step")
                        if args.tp_split == "megatron" else
-                       f"tp{world}: every GEMV by output rows + NCCL all-gather of each output; one CUDA graph per step",
+                       f"tp{world}: every GEMV by output rows + all-gather of each output ("
+                       + ("fused into the GEMV (peer memory)" if fused else "NCCL") + "); one CUDA graph per step",
                        "setup_seconds": res["setup_seconds"]},
             "tok_s": res["tok_s"], "per_gpu_gbs": res["gbs"] / world, "allreduce": res["allreduce"],
             "max_rel_err_vs_fp64": res["max_rel_err_vs_fp64"], "clocks": sampler.summary(),

@@ -204,6 +204,24 @@ int se12_gemv_allreduce(const se12_matrix* m, const uint16_t* x_dev, int batch, 
                         void* workspace_dev, size_t workspace_bytes, const se12_peer_group* peers, void* stream);
 
 /*
+ * Fused GEMV + all-gather for tensor parallelism with the output rows
+ * sharded (every GEMV row-sharded, the whole output wanted on every rank):
+ * this rank's matrix holds rows row0 .. row0 + rows - 1 of a rows_full-row
+ * output, and every rank gets the whole output in y_dev [batch][ldy >=
+ * rows_full]. No counterpart in the reference (one GPU at a time); it
+ * replaces a GEMV followed by an NCCL all-gather: each finished tile row
+ * is stored into every rank's receive buffer at its place in the whole
+ * output (each value with the call's epoch in one 64-bit word), and every
+ * CTA then unpacks its slice of the whole output once the words carry the
+ * epoch. Same peer group, ordering and error rules as se12_gemv_allreduce
+ * (the two share the group's call counter); needs rows_full <= world x
+ * rows_cap.
+ */
+int se12_gemv_allgather(const se12_matrix* m, const uint16_t* x_dev, int batch, int ldx, float* y_dev, int ldy, int row0,
+                        int rows_full, void* workspace_dev, size_t workspace_bytes, const se12_peer_group* peers,
+                        void* stream);
+
+/*
  * se12_gemv without a caller workspace, for callers that cannot allocate
  * device memory: a host that has reserved all of HBM for its own arena (so
  * cudaMalloc fails), or a binding that holds no device buffer it could keep

@@ -83,6 +83,8 @@ SIGNATURES = {
     "se12_peer_recv_bytes": (c_size_t, [c_int, c_int]),
     "se12_gemv_allreduce": (c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p, c_int, c_void_p, c_size_t,
                                     ctypes.POINTER(Se12PeerGroupStruct), c_void_p]),
+    "se12_gemv_allgather": (c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p, c_int, c_int, c_int, c_void_p, c_size_t,
+                                    ctypes.POINTER(Se12PeerGroupStruct), c_void_p]),
     "se12_decode": (c_int, [c_void_p, c_void_p, c_int, c_void_p]),
     "se12_decode_rows": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p]),
     "bf16_gemv_workspace_bytes": (c_size_t, [c_int, c_int, c_int]),

@@ -544,22 +544,28 @@ size_t se12_peer_recv_bytes(int world, int rows_cap) {
   return static_cast<size_t>(2) * world * 16 * rows_cap * sizeof(uint64_t);
 }
 
-int se12_gemv_allreduce(const se12_matrix* m, const uint16_t* x, int batch, int ldx, float* y, int ldy, void* workspace,
-                        size_t workspace_bytes, const se12_peer_group* g, void* stream) {
+}  // extern "C"
+
+static int gemv_peers(const se12_matrix* m, const uint16_t* x, int batch, int ldx, float* y, int ldy, void* workspace,
+                      size_t workspace_bytes, const se12_peer_group* g, void* stream, int gather, int row0, int rows_full) {
   if (!m || !g) return fail(SE12_ERR_INVALID_ARGUMENT, "null matrix or peer group");
   if (g->world < 2 || g->world > SE12_MAX_PEERS || g->rank < 0 || g->rank >= g->world)
     return fail(SE12_ERR_INVALID_ARGUMENT, "peer group needs 2.." + std::to_string(SE12_MAX_PEERS) +
                                                " ranks and 0 <= rank < world");
-  if (m->view.rows > g->rows_cap)
+  if (!gather && m->view.rows > g->rows_cap)
     return fail(SE12_ERR_INVALID_ARGUMENT, "matrix has " + std::to_string(m->view.rows) +
                                                " rows, the peer buffers hold " + std::to_string(g->rows_cap));
+  if (gather && (row0 < 0 || rows_full < row0 + m->view.rows ||
+                 static_cast<long long>(rows_full) > static_cast<long long>(g->world) * g->rows_cap))
+    return fail(SE12_ERR_INVALID_ARGUMENT, "gathered rows: need 0 <= row0, row0 + matrix rows <= rows_full <= world x "
+                                           "rows_cap (" + std::to_string(g->world) + " x " + std::to_string(g->rows_cap) + ")");
   if (!g->epoch) return fail(SE12_ERR_INVALID_ARGUMENT, "null epoch counter");
   for (int r = 0; r < g->world; ++r) {
     if (!g->recv[r]) return fail(SE12_ERR_INVALID_ARGUMENT, "null peer buffer");
     if (!aligned16(g->recv[r]))
       return fail(SE12_ERR_MISALIGNED, "peer buffers must be 16-byte aligned");
   }
-  int st = check_gemv_io(m->view.rows, m->view.cols, x, batch, ldx, y, ldy);
+  int st = check_gemv_io(gather ? rows_full : m->view.rows, m->view.cols, x, batch, ldx, y, ldy);
   if (st != SE12_OK) return st;
   const LaunchConfig c = choose_config(false, m->view.tiles, m->view.cols, batch, m->sm_count, false);
   const size_t need = workspace_bytes_for(m->view.tile_rows, m->sm_count);
@@ -587,10 +593,25 @@ int se12_gemv_allreduce(const se12_matrix* m, const uint16_t* x, int batch, int 
     a.peers.recv[r] = static_cast<unsigned long long*>(g->recv[r]);
   }
   a.peers.epoch = g->epoch;
+  a.peers.gather = gather;
+  a.peers.row0 = row0;
+  a.peers.rows_full = rows_full;
   cudaError_t err = se12::launch_gemv(false, m->sm_map, m->ec_map, a, c.nblocks, c.smem,
                                       static_cast<cudaStream_t>(stream), true);
-  if (err != cudaSuccess) return cuda_fail(err, "se12_gemv_allreduce launch");
+  if (err != cudaSuccess) return cuda_fail(err, gather ? "se12_gemv_allgather launch" : "se12_gemv_allreduce launch");
   return SE12_OK;
+}
+
+extern "C" {
+
+int se12_gemv_allreduce(const se12_matrix* m, const uint16_t* x, int batch, int ldx, float* y, int ldy, void* workspace,
+                        size_t workspace_bytes, const se12_peer_group* g, void* stream) {
+  return gemv_peers(m, x, batch, ldx, y, ldy, workspace, workspace_bytes, g, stream, 0, 0, 0);
+}
+
+int se12_gemv_allgather(const se12_matrix* m, const uint16_t* x, int batch, int ldx, float* y, int ldy, int row0,
+                        int rows_full, void* workspace, size_t workspace_bytes, const se12_peer_group* g, void* stream) {
+  return gemv_peers(m, x, batch, ldx, y, ldy, workspace, workspace_bytes, g, stream, 1, row0, rows_full);
 }
 
 }  // extern "C"

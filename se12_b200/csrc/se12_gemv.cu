@@ -463,9 +463,34 @@ __global__ void __launch_bounds__(gemv_threads(WIDE), WIDE ? 1 : 2) gemv_kernel(
         }
       }
     };
+    // All-gather mode: once this CTA's rows are out, it waits for its slice
+    // of the whole output (every rank's rows, this rank's included) and
+    // writes it to y as plain fp32. Slices are even cuts of the B x rows_full
+    // words over the grid, so every CTA -- one without rows included -- takes
+    // part, and a rank's call ends only when its whole output is there.
+    auto unpack_gather = [&](int ep) {
+      const size_t gbase = static_cast<size_t>(ep & 1) * 16 * P.rows_full;
+      const unsigned long long* mine = P.recv[P.rank] + gbase;
+      const long long total = static_cast<long long>(B) * P.rows_full;
+      const long long i0 = total * blockIdx.x / G, i1 = total * (blockIdx.x + 1) / G;
+      bool arrived = true;
+      for (long long i = i0 + lane; i < i1; i += 32) {
+        const int b = static_cast<int>(i / P.rows_full), row = static_cast<int>(i - static_cast<long long>(b) * P.rows_full);
+        const unsigned long long* src = mine + static_cast<size_t>(b) * P.rows_full + row;
+        const unsigned long long w = ld_word_sys(src);
+        unsigned bits = static_cast<unsigned>(w);
+        bool got = static_cast<unsigned>(w >> 32) == static_cast<unsigned>(ep);
+        if (!got) got = wait_word_sys(src, static_cast<unsigned>(ep), &bits);
+        arrived = arrived && got;
+        if (got) yg[static_cast<size_t>(b) * ldy + row] = __uint_as_float(bits);
+      }
+      __syncwarp();
+      (void)arrived;  // a word that never came left its element unwritten and raised the status word
+    };
     if (tend <= tstart) {
       if (AR) {
         grid_dependency_wait();
+        if (P.gather) unpack_gather(__ldcg(P.epoch) + 1);
         finish_call();
       }
       return;
@@ -528,7 +553,25 @@ __global__ void __launch_bounds__(gemv_threads(WIDE), WIDE ? 1 : 2) gemv_kernel(
           for (int j = 0; j < 8; ++j) v[j] += p[j];
         }
       }
-      if (AR && good) {
+      if (AR && good && P.gather) {
+        // All-gather: each value of the row, with this call's epoch in the
+        // same 64-bit word, into every rank's receive buffer at the row's
+        // place in the whole output (this rank's own included); every CTA
+        // unpacks its slice of the whole output once its rows are out.
+        const size_t gbase = static_cast<size_t>(epoch & 1) * 16 * P.rows_full;
+        const unsigned long long tag = static_cast<unsigned long long>(static_cast<unsigned>(epoch)) << 32;
+        for (int r = 0; r < P.world; ++r) {
+          unsigned long long* dst = P.recv[r] + gbase;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const int idx = lane + 32 * j;
+            const int row = idx / B, b = idx - row * B;
+            const int grow = tr * kTileRows + row;
+            if (idx < outs && grow < N)
+              st_word_sys(dst + static_cast<size_t>(b) * P.rows_full + P.row0 + grow, tag | __float_as_uint(v[j]));
+          }
+        }
+      } else if (AR && good) {
         // All-reduce of the row across the peer group: store each value,
         // with this call's epoch in the same 64-bit word, into every rank's
         // receive slot (this rank's own included) for this epoch's parity;
@@ -588,12 +631,13 @@ __global__ void __launch_bounds__(gemv_threads(WIDE), WIDE ? 1 : 2) gemv_kernel(
         if (idx < outs) {
           const int row = idx / B, b = idx - row * B;
           const int grow = tr * kTileRows + row;
-          if (grow < N && good) yg[static_cast<size_t>(b) * ldy + grow] = v[j];
+          if (grow < N && good && !(AR && P.gather)) yg[static_cast<size_t>(b) * ldy + grow] = v[j];
         }
       }
       for (int c = blockIdx.x + 1 + lane; c <= c_hi; c += 32) counters[c] = 0;
     }
     __syncwarp();
+    if (AR && P.gather) unpack_gather(epoch);
     finish_call();
     return;
   }

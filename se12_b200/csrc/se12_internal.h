@@ -53,6 +53,13 @@ struct PeerArgs {
   unsigned long long* recv[kMaxPeers];  // rank s's receive buffer (peer-mapped): [2 parities][world][16 batch][rows_cap]
                                         // words, each epoch << 32 | fp32 bits
   int* epoch;                // this rank's [call counter, CTAs finished]; a call uses counter + 1 (its last CTA bumps it)
+  // All-gather mode (gather = 1): this rank's matrix holds rows row0 ..
+  // row0 + rows - 1 of a rows_full-row output; the receive buffers are read
+  // as [2 parities][16 batch][rows_full] words (rows_full <= world x rows_cap)
+  // and y is the whole [B][rows_full] output.
+  int gather;
+  int row0;
+  int rows_full;
 };
 
 // Arguments of one fused (or dense baseline) GEMV launch: y = x . W^T.

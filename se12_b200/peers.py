@@ -110,5 +110,33 @@ class PeerGroup:
                           ctypes.byref(self.struct), ctypes.c_void_p(stream))
         return out.reshape(-1) if squeeze else out
 
+    def gemv_allgather(self, m: DeviceSe12Matrix, x: torch.Tensor, row0: int, rows_full: int,
+                       out: torch.Tensor | None = None) -> torch.Tensor:
+        """The whole rows_full-row output on every rank: this rank's ``m``
+        holds rows row0 .. row0 + m.rows - 1 of it, times ``x`` (BF16 [B,
+        m.cols]); fp32 [B, rows_full], the same bits on every rank. Batches
+        above 16 run as chunks of 16 (each chunk is a call)."""
+        if x.dtype != torch.bfloat16:
+            raise TypeError("activations must be bfloat16")
+        if rows_full > self.world * self.rows_cap:
+            raise ValueError(f"{rows_full} gathered rows, the group holds {self.world} x {self.rows_cap}")
+        squeeze = x.dim() == 1
+        x2 = x.reshape(1, -1) if squeeze else x
+        batch = x2.shape[0]
+        if out is None:
+            out = torch.empty(batch, rows_full, dtype=torch.float32, device=x.device)
+        stream = stream_handle(x.device)
+        lib = _lib.load()
+        with torch.cuda.device(x.device):
+            for b0 in range(0, batch, MAX_BATCH):
+                xb = _aligned_bf16(x2[b0:b0 + MAX_BATCH], m.cols)
+                yb = out[b0:b0 + MAX_BATCH]
+                need = lib.se12_gemv_workspace_bytes(m.handle, MAX_BATCH)
+                ws = WORKSPACES.get(x.device, stream, need)
+                _lib.call("se12_gemv_allgather", m.handle, ctypes.c_void_p(xb.data_ptr()), xb.shape[0], xb.stride(0),
+                          ctypes.c_void_p(yb.data_ptr()), yb.stride(0), int(row0), int(rows_full),
+                          ctypes.c_void_p(ws.data_ptr()), ws.numel(), ctypes.byref(self.struct), ctypes.c_void_p(stream))
+        return out.reshape(-1) if squeeze else out
+
 
 __all__ = ["MAX_PEERS", "PeerGroup"]

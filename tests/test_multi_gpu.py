@@ -288,3 +288,84 @@ def test_chain_with_allreduced_ops(tmp_path):
         assert res["status"] == 0, res
         assert max(res["errs"]) <= TOLERANCE, res["errs"]
         assert all(res["same"]), res["same"]
+
+
+def _allgather_main(rank, world, port, result_path):
+    import datetime
+
+    import torch.distributed as dist
+
+    from se12_b200.device import DeviceSe12Matrix, device_status
+    from se12_b200.peers import PeerGroup
+    from se12_b200.sharding import row_range
+
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", rank))
+    out = {}
+    try:
+        rows, cols = 128 * world, 2304  # equal 16-row-multiple shards
+        bits, _, _ = cases.synthetic_weights(rows, cols, seed=12, outlier_rate=2e-3, outlier_scale=256.0)
+        r0, r1 = row_range(rows, world, rank)
+        shard = np.asarray(bits, dtype=np.uint16).reshape(rows, cols)[r0:r1].reshape(-1)
+        s = oracle.encode(shard, r1 - r0, cols)
+
+        def up(a, dtype):
+            return torch.from_numpy(np.ascontiguousarray(a).reshape(-1).view(dtype)).cuda()
+
+        m = DeviceSe12Matrix(s.rows, s.cols, s.codebook, up(s.sm, np.uint8), up(s.ec, np.uint8), up(s.esc, np.uint8),
+                             up(s.fallback_bitmap, np.uint8), up(s.fallback_raw, np.int16))
+        peers = PeerGroup(rows_cap=r1 - r0)
+        errs, same = [], []
+        for call, batch in enumerate((1, 3, 16, 2)):
+            xb = oracle.bf16_round(np.random.default_rng(call).normal(size=(batch, cols)).astype(np.float32))
+            x = torch.from_numpy(xb.view(np.int16)).view(torch.bfloat16).cuda()
+            y = peers.gemv_allgather(m, x, r0, rows)
+            y64 = oracle.gemv_fp64(bits, rows, cols, oracle.bits_to_float32(xb))
+            errs.append(oracle.max_relative_error(y.cpu().numpy(), y64))
+            everyone = [torch.empty_like(y) for _ in range(world)]
+            dist.all_gather(everyone, y)
+            same.append(all(torch.equal(everyone[0], e) for e in everyone))
+        # from a CUDA graph, two calls per replay
+        xb = oracle.bf16_round(np.random.default_rng(99).normal(size=(4, cols)).astype(np.float32))
+        x = torch.from_numpy(xb.view(np.int16)).view(torch.bfloat16).cuda()
+        y = torch.empty(4, rows, device="cuda")
+        stream = torch.cuda.Stream()
+        stream.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(stream):
+            peers.gemv_allgather(m, x, r0, rows, out=y)
+        stream.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            peers.gemv_allgather(m, x, r0, rows, out=y)
+            peers.gemv_allgather(m, x, r0, rows, out=y)
+        y64 = oracle.gemv_fp64(bits, rows, cols, oracle.bits_to_float32(xb))
+        for _ in range(3):
+            y.zero_()
+            graph.replay()
+            torch.cuda.synchronize()
+            errs.append(oracle.max_relative_error(y.cpu().numpy(), y64))
+        del graph
+        torch.cuda.synchronize()
+        out = {"errs": errs, "same": same, "status": device_status()}
+        peers.close()
+    finally:
+        torch.save(out, f"{result_path}.{rank}")
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", WORLDS)
+def test_fused_gemv_allgather_over_peer_memory(tmp_path, world):
+    """Row shards whose GEMV and all-gather are one kernel: every rank holds
+    the whole output, within 1e-3 of the fp64 oracle and with the same bits
+    on every rank, over calls in a row and from a replayed CUDA graph."""
+    import torch.multiprocessing as mp
+
+    _need(world)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    mp.spawn(_allgather_main, args=(world, _free_port(), str(tmp_path / "ag")), nprocs=world, join=True)
+    for r in range(world):
+        res = torch.load(tmp_path / f"ag.{r}")
+        assert res["status"] == 0, res
+        assert max(res["errs"]) <= TOLERANCE, res["errs"]
+        assert all(res["same"]), res["same"]
