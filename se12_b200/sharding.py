@@ -109,7 +109,8 @@ class ShardedLinear(torch.nn.Module):
     x [B, k_local] -> fp32 [B, n_local]). With ``peers`` (a
     ``peers.PeerGroup``), a ``"cols"`` layer runs the GEMV and its
     all-reduce as one kernel over peer memory instead of a GEMV followed by
-    an NCCL all-reduce.
+    an NCCL all-reduce, and a ``"rows"`` layer its GEMV and all-gather (the
+    group's ``rows_cap`` x world must reach the layer's rows).
     """
 
     def __init__(self, kind: str, rows: int, cols: int, world: int, rank: int, matrix=None,
@@ -137,6 +138,10 @@ class ShardedLinear(torch.nn.Module):
             y = self.local(x2[:, c0:c1].contiguous()).float()
             if self.world > 1:
                 dist.all_reduce(y, group=self.group)
+            return y.reshape(*x.shape[:-1], self.rows)
+        if self.peers is not None and self.world > 1:
+            r0, _ = self.row_bounds[self.rank]
+            y = self.peers.gemv_allgather(self.matrix, x2.to(torch.bfloat16), r0, self.rows)
             return y.reshape(*x.shape[:-1], self.rows)
         y = self.local(x2).float()
         if self.world > 1:
