@@ -997,16 +997,22 @@ def tp_measure(args, torch, shapes, world, rank, local, device, sampler=None, ch
     ops, local_bytes = tp_build(torch, shapes, layers, batch, world, rank, device, group=not args.no_group,
                                 lm_head=not args.no_lm_head, split=split)
     setup_s = time.perf_counter() - t0
-    fused = world > 1 and args.tp_allreduce == "fused" and (split == "rows" or any(op.coll == "all_reduce" for op in ops))
+    fused = world > 1 and args.tp_allreduce == "fused"
     if world > 1:
+        from se12_b200.sharding import row_range
+
         for op in ops:
             if op.coll == "all_gather":
-                # the row split gathers inside the GEMV kernel (every rank's
-                # part the same size here: row shards of 16-row multiples)
-                op.fused_gather = fused and split == "rows"
+                # gathered inside the GEMV kernel when every rank's part has
+                # the same size (the whole output is then the ranks' parts
+                # in rank order), else by NCCL
+                equal = all(len({(lambda a, b: b - a)(*row_range(rows, world, r)) for r in range(world)}) == 1
+                            for rows, _ in op.dims)
+                op.fused_gather = fused and equal
                 shape = (batch, world * op.y.shape[1]) if op.fused_gather else (world, batch, op.y.shape[1])
                 op.gathered = torch.empty(*shape, dtype=torch.float32, device=device)
     peers = None
+    fused = fused and any(op.coll == "all_reduce" or op.fused_gather for op in ops)
     if fused:
         from se12_b200.peers import PeerGroup
 
