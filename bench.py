@@ -1003,12 +1003,14 @@ def tp_measure(args, torch, shapes, world, rank, local, device, sampler=None, ch
 
         for op in ops:
             if op.coll == "all_gather":
-                # gathered inside the GEMV kernel when every rank's part has
-                # the same size (the whole output is then the ranks' parts
-                # in rank order), else by NCCL
+                # the row split gathers inside the GEMV kernel when every
+                # rank's part has the same size (the whole output is then the
+                # ranks' parts in rank order). The Megatron split's one
+                # gather (the LM head) stays with NCCL: the gathering kernel
+                # has no wide layout, which that GEMV runs faster in.
                 equal = all(len({(lambda a, b: b - a)(*row_range(rows, world, r)) for r in range(world)}) == 1
                             for rows, _ in op.dims)
-                op.fused_gather = fused and equal
+                op.fused_gather = fused and equal and split == "rows"
                 shape = (batch, world * op.y.shape[1]) if op.fused_gather else (world, batch, op.y.shape[1])
                 op.gathered = torch.empty(*shape, dtype=torch.float32, device=device)
     peers = None
