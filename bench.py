@@ -743,7 +743,10 @@ def run_ours(args) -> None:
             try:
                 return tp_leg(args, torch, world, rank, local, device, **kw)
             except Exception as exc:
-                torch.cuda.synchronize()
+                try:
+                    torch.cuda.synchronize()
+                except Exception:  # a CUDA error stays with the context; report the first one
+                    pass
                 return {"error": f"{type(exc).__name__}: {exc}"[:300]}
 
         tp = leg()
