@@ -1080,7 +1080,9 @@ def run_tp(args) -> None:
     sampler = ClockSampler(local)
     res = tp_measure(args, torch, shapes, world, rank, local, device, sampler=sampler, split=args.tp_split)
     if rank == 0:
-        fused = res["allreduce"] is not None and res["allreduce"].startswith("fused")
+        # the Megatron split's collective is its all-reduce, the row split's its all-gather
+        coll = res["allreduce"] if args.tp_split == "megatron" else res["allgather"]
+        fused = coll is not None and coll.startswith("fused")
         line = {
             "metric": METRIC, "value": res["gbs"], "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": res["ms_per_step"], "higher_is_better": True, "scaling": "strong",
@@ -1096,7 +1098,8 @@ def run_tp(args) -> None:
                        + ("fused into the GEMV (peer memory)" if fused else "NCCL") + "); one CUDA graph per step",
                        "setup_seconds": res["setup_seconds"]},
             "tok_s": res["tok_s"], "per_gpu_gbs": res["gbs"] / world, "allreduce": res["allreduce"],
-            "max_rel_err_vs_fp64": res["max_rel_err_vs_fp64"], "clocks": sampler.summary(),
+            "allgather": res["allgather"], "max_rel_err_vs_fp64": res["max_rel_err_vs_fp64"],
+            "clocks": sampler.summary(),
         }
         print(json.dumps(line), flush=True)
     if world > 1:
