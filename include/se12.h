@@ -136,8 +136,7 @@ typedef struct se12_launch_config {
   int stages;        /* pipeline depth */
   int x_resident;    /* 1: all of x in shared memory; 0: staged per stage */
   int row_mode;      /* 1: whole tile rows per CTA; 0: stream-K with split rows */
-  int wide;          /* 1: one CTA per SM whose warp groups take 4-tile stages in turn;
-                        2: one CTA per SM, 8-tile stages, two consumer warps per tile */
+  int wide;          /* 1: one CTA per SM whose warp groups take 4-tile stages in turn */
 } se12_launch_config;
 
 int se12_gemv_launch_config(const se12_matrix* m, int batch, se12_launch_config* out);

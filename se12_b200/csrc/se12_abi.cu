@@ -237,27 +237,20 @@ LaunchConfig choose_config(bool raw, int tiles, int cols, int batch, int sm_coun
     if (!best.stages || cost < best_cost) {
       best_cost = cost;
       best.full_tiles = 0;
-      best.wide = se12::kLayoutWide;
+      best.wide = 1;
       best.x_resident = 1;
       best.stages = memw.stages;
       best.row_mode = 1;
       best.grid = grid_rows;
     }
   }
-  // 8-tile stages whose shared memory holds one CTA per SM (x resident at
-  // batch 9..16) run as tile pairs, two consumer warps to a tile: twice the
-  // warps on the SM at the same register budget.
-  if (!raw && allow_wide && best.stages && best.full_tiles && best.x_resident && !best.wide && mem8.per_sm == 1 &&
-      se12::gemv_smem_bytes(false, true, true, best.stages, batch, cols, se12::kLayoutPairs) + 1024 <=
-          se12::kMaxSmemPerCta)
-    best.wide = se12::kLayoutPairs;
   if (!best.stages) {  // not reached for batch <= 16: 4-tile stages with staged x, 2 stages, fit one CTA per SM
     best.stages = 2;
     best.grid = std::max(1, std::min((tiles + 3) / 4, sm_count));
   }
   best.nblocks = batch <= 8 ? 1 : 2;
   best.smem = se12::gemv_smem_bytes(raw, best.full_tiles != 0, best.x_resident != 0, best.stages, batch, cols,
-                                    best.wide);
+                                    best.wide != 0);
   return best;
 }
 
@@ -411,7 +404,7 @@ static int check_gemv_io(int rows, int cols, const uint16_t* x, int batch, int l
 
 static void fill_launch_config(const LaunchConfig& c, se12_launch_config* out) {
   out->grid = c.grid;
-  out->threads = se12::gemv_threads(c.wide);
+  out->threads = se12::gemv_threads(c.wide != 0);
   out->smem_bytes = static_cast<int>(c.smem);
   out->ctas_per_sm = (c.smem <= se12::kCoResidentSmem && !c.wide) ? 2 : 1;
   out->stage_tiles = se12::stage_tiles(c.full_tiles != 0);

@@ -31,10 +31,7 @@
 //   order is permuted per thread the same way for x. Every shared-memory
 //   read is bank-conflict free.
 // * Two CTAs per SM (shared memory under half an SM, 96 registers a
-//   thread): the second CTA's warps hide the first one's latencies. Where
-//   shared memory holds one CTA only (resident x of batch 9..16 with 8-tile
-//   stages), the CTA runs tile pairs instead: 16 consumer warps, two to a
-//   tile, at the same 96 registers.
+//   thread): the second CTA's warps hide the first one's latencies.
 // * Programmatic dependent launch: the kernel lets the next kernel in the
 //   stream launch at once; its CTAs start as SMs free up, prefetch their
 //   first stages of weights, and wait (griddepcontrol.wait) only before
@@ -167,25 +164,21 @@ __device__ __forceinline__ void add_acc(float (&acc)[2][NB][4], const float (&pa
       for (int q = 0; q < 4; ++q) acc[h][nb][q] += part[h][nb][q];
 }
 
-template <int NB, bool RAW, bool XRES, bool FULL, bool AR, int LAYOUT>
-__global__ void __launch_bounds__(gemv_threads(LAYOUT), LAYOUT ? 1 : 2) gemv_kernel(const __grid_constant__ CUtensorMap map0,
-                                                                                    const __grid_constant__ CUtensorMap map1,
-                                                                                    const GemvArgs a) {
-  constexpr bool WIDE = LAYOUT == kLayoutWide;
-  constexpr bool PAIRS = LAYOUT == kLayoutPairs;
+template <int NB, bool RAW, bool XRES, bool FULL, bool AR, bool WIDE>
+__global__ void __launch_bounds__(gemv_threads(WIDE), WIDE ? 1 : 2) gemv_kernel(const __grid_constant__ CUtensorMap map0,
+                                                                                const __grid_constant__ CUtensorMap map1,
+                                                                                const GemvArgs a) {
   static_assert(!(RAW && FULL), "the dense baseline runs 4-tile stages");
   static_assert(!WIDE || (!RAW && XRES && !FULL && !AR), "the wide layout is SE12 with x resident");
-  static_assert(!PAIRS || (!RAW && XRES && FULL && !AR), "tile pairs are SE12 8-tile stages with x resident");
   constexpr int kWeightBytes = stage_weight_bytes(RAW, FULL);
   constexpr int kStage = stage_tiles(FULL);             // tiles per stage
   constexpr int kRecStages = kRecGroupTiles / kStage;   // stages per escape-record slot
-  constexpr bool kTilePerWarp = (FULL && !PAIRS) || WIDE;  // a consumer warp multiplies whole tiles
-  constexpr int kHalves = kTilePerWarp ? 2 : 1;         // 128-column halves a warp multiplies per tile
-  constexpr int kCons = consumer_warps(LAYOUT);         // consumer warps
-  constexpr int kStageWarps = WIDE ? kStage : kCons;    // consumer warps that take each stage
+  constexpr bool kTilePerWarp = FULL || WIDE;           // a consumer warp multiplies whole tiles
+  constexpr int kCons = consumer_warps(WIDE);           // consumer warps
+  constexpr int kStageWarps = WIDE ? kStage : kConsumerWarps;  // consumer warps that take each stage
   constexpr int kProducer = kCons;                      // TMA / bulk copies
   constexpr int kReducer = kCons + 1;                   // sums the consumers' row partials
-  constexpr int kRS = rec_slots(LAYOUT);                // escape-record slots
+  constexpr int kRS = rec_slots(WIDE);                  // escape-record slots
   static_assert(!WIDE || kWideGroups >= kRecStages, "a wide-layout warp takes at most one stage of a record group");
   extern __shared__ __align__(1024) uint8_t smem_dynamic[];
   // All dynamic shared memory is addressed as smem_dynamic + 32-bit offset,
@@ -651,10 +644,10 @@ __global__ void __launch_bounds__(gemv_threads(LAYOUT), LAYOUT ? 1 : 2) gemv_ker
 
   // -------------------------------------------------------------- consumers
   // 8-tile stages (FULL): warp w decodes tile w of every stage, its two
-  // 128-column halves in turn. 4-tile stages, and 8-tile stages in tile
-  // pairs: warp w takes half w % 2 of tile w / 2. Wide layout: warp w
-  // decodes tile w % 4 of the stages of its group w / 4, both halves in turn.
-  const int jw = WIDE ? (warp & 3) : (kTilePerWarp ? warp : (warp >> 1));  // tile of the stage this warp multiplies
+  // 128-column halves in turn. 4-tile stages: warp w takes half w % 2 of
+  // tile w / 2. Wide layout: warp w decodes tile w % 4 of the stages of its
+  // group w / 4, both halves in turn.
+  const int jw = FULL ? warp : (WIDE ? (warp & 3) : (warp >> 1));  // tile of the stage this warp multiplies
   const int hw = kTilePerWarp ? 0 : (warp & 1);                     // its (first) half
   const int g = lane >> 2, t = lane & 3;
   // decode table of the current tile's segment (seg_tab[cur_seg]), loaded
@@ -1111,16 +1104,15 @@ __global__ void __launch_bounds__(gemv_threads(LAYOUT), LAYOUT ? 1 : 2) gemv_ker
             // The two halves run as a loop, not unrolled: one copy of the
             // decode in the instruction cache. The escape products come
             // after half 0, so that their record is dead during half 1.
-            // (Tile pairs: the warp's one half.)
             if (plain) {
   #pragma unroll 1
-              for (int h = 0; h < kHalves; ++h) {
+              for (int h = 0; h < 2; ++h) {
                 decode_mma(s, kt_mine, h);
                 if (h == 0) fix_escapes(s, kt_mine, esc_rec);
               }
             } else {
   #pragma unroll 1
-              for (int h = 0; h < kHalves; ++h) {
+              for (int h = 0; h < 2; ++h) {
                 if (!(kPredecodeFirst && i == 0 && h == 0)) load_frags(s, kt_mine, fbi, h);
                 mma_tile(s, kt_mine, h);
                 if (h == 0 && fbi < 0) fix_escapes(s, kt_mine, esc_rec);
@@ -1190,28 +1182,21 @@ cudaError_t launch_gemv(bool raw, const CUtensorMap& map0, const CUtensorMap& ma
        {nullptr, gemv_kernel<2, false, true, true, true, false>}}};
   // the wide layout (SE12, x resident, no all-reduce, batch <= 8: at 80
   // registers the two-block accumulators spill)
-  static const Kernel table_wide[2] = {gemv_kernel<1, false, true, false, false, kLayoutWide>, nullptr};
-  // tile pairs (SE12, 8-tile stages, x resident, no all-reduce)
-  static const Kernel table_pairs[2] = {gemv_kernel<1, false, true, true, false, kLayoutPairs>,
-                                        gemv_kernel<2, false, true, true, false, kLayoutPairs>};
+  static const Kernel table_wide[2] = {gemv_kernel<1, false, true, false, false, true>, nullptr};
   const int kind = raw ? 2 : (a.full_tiles ? 1 : 0);
   const int blocks = nblocks == 1 ? 0 : 1;
   const bool ar = a.peers.world > 1;
   if (ar && raw) return cudaErrorInvalidValue;
-  if (a.wide < kLayoutClassic || a.wide > kLayoutPairs) return cudaErrorInvalidValue;
-  if (a.wide == kLayoutWide && (raw || ar || a.full_tiles || !a.x_resident || a.stages <= kWideGroups))
-    return cudaErrorInvalidValue;
-  if (a.wide == kLayoutPairs && (raw || ar || !a.full_tiles || !a.x_resident)) return cudaErrorInvalidValue;
-  const Kernel kernel = a.wide == kLayoutWide    ? table_wide[blocks]
-                        : a.wide == kLayoutPairs ? table_pairs[blocks]
-                        : ar                     ? table_ar[blocks][kind][a.x_resident ? 1 : 0]
-                                                 : table[blocks][kind][a.x_resident ? 1 : 0];
+  if (a.wide && (raw || ar || a.full_tiles || !a.x_resident || a.stages <= kWideGroups)) return cudaErrorInvalidValue;
+  const Kernel kernel = a.wide ? table_wide[blocks]
+                        : ar   ? table_ar[blocks][kind][a.x_resident ? 1 : 0]
+                               : table[blocks][kind][a.x_resident ? 1 : 0];
   if (!kernel) return cudaErrorInvalidValue;
   cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (err != cudaSuccess) return err;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.grid);
-  cfg.blockDim = dim3(gemv_threads(a.wide));
+  cfg.blockDim = dim3(gemv_threads(a.wide != 0));
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];

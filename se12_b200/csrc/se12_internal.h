@@ -78,7 +78,7 @@ struct GemvArgs {
   int x_resident;      // 1: all of x in shared memory; 0: x staged per stage
   int row_mode;        // 1: each CTA owns whole tile rows; 0: stream-K over stages
   int full_tiles;      // SE12: 1 = 8-tile stages, a warp per tile; 0 = 4-tile stages, a warp per half tile
-  int wide;            // layout: kLayoutClassic, kLayoutWide (SE12, x resident, 4-tile stages, one CTA per SM: kWideGroups groups of 4 warps take the stages in turn) or kLayoutPairs
+  int wide;            // SE12, x resident: 1 = one CTA per SM, kWideGroups groups of 4 warps taking 4-tile stages in turn
   PeerArgs peers;      // world == 1: plain GEMV
 };
 
@@ -105,26 +105,14 @@ __host__ __device__ constexpr int stage_weight_bytes(bool raw, bool full_tiles) 
   return stage_tiles(full_tiles) * (raw ? 8192 : 6144);
 }
 constexpr int kXRowStride = 576;        // bytes per (tile, batch row) x slice when staged: 512 + 64 pad
-// A GEMV CTA: its consumer warps (8, 20 in the wide layout, 16 in tile
-// pairs), then the producer warp (TMA / bulk copies), then the reducer warp
-// (sums the consumers' row partials).
+// A GEMV CTA: its consumer warps (8, or 20 in the wide layout), then the
+// producer warp (TMA / bulk copies), then the reducer warp (sums the
+// consumers' row partials).
 constexpr int kConsumerWarps = 8;
 constexpr int kWideGroups = 5;
 constexpr int kMaxWideStages = kWideGroups + 4;  // the deepest wide pipeline the launch table picks
-// Layouts of a GEMV CTA (GemvArgs::wide): the classic one (8 consumer
-// warps, two CTAs per SM where shared memory allows), the wide layout
-// above, and tile pairs: 8-tile stages with x resident, one CTA per SM, 16
-// consumer warps, two to a tile (warp w takes half w % 2 of tile w / 2).
-// 18 warps keep 96 registers a thread (5 warps on some SM sub-partition),
-// the classic layout's budget, with twice its consumer warps on the SM
-// when shared memory holds only one CTA (batch 9..16, x resident).
-constexpr int kLayoutClassic = 0;
-constexpr int kLayoutWide = 1;
-constexpr int kLayoutPairs = 2;
-__host__ __device__ constexpr int consumer_warps(int layout) {
-  return layout == kLayoutWide ? kWideGroups * 4 : layout == kLayoutPairs ? 2 * kConsumerWarps : kConsumerWarps;
-}
-__host__ __device__ constexpr int gemv_threads(int layout) { return (consumer_warps(layout) + 2) * 32; }
+__host__ __device__ constexpr int consumer_warps(bool wide) { return wide ? kWideGroups * 4 : kConsumerWarps; }
+__host__ __device__ constexpr int gemv_threads(bool wide) { return (consumer_warps(wide) + 2) * 32; }
 // Escape records (escape positions, escape slots, fallback indices) of
 // kRecGroupTiles consecutive tiles (two SE12 stages) are copied into shared
 // memory together, into one of kRecSlots slots: [16 tiles][16] u16
@@ -133,7 +121,7 @@ constexpr int kRecGroupTiles = 16;
 constexpr int kRecSlots = 3;
 // The wide layout keeps more stages in flight (its record groups are 4
 // stages, up to 3 of them live at once, plus the one issued ahead).
-__host__ __device__ constexpr int rec_slots(int layout) { return layout == kLayoutWide ? 4 : kRecSlots; }
+__host__ __device__ constexpr int rec_slots(bool wide) { return wide ? 4 : kRecSlots; }
 constexpr int kRecPosOffset = 0;
 constexpr int kRecEscOffset = kRecGroupTiles * 32;
 constexpr int kRecFbOffset = kRecEscOffset + kRecGroupTiles * 16;
@@ -151,16 +139,15 @@ inline size_t x_stage_bytes(bool full_tiles, int batch) {
   return ((size_t)stage_tiles(full_tiles) * batch * kXRowStride + 127) / 128 * 128;
 }
 
-// (layout: kLayoutWide, whose stages are 4 tiles: full_tiles must be false;
-// kLayoutPairs: 8-tile stages, full_tiles true)
+// (wide: the wide layout, whose stages are 4 tiles: full_tiles must be false)
 inline size_t gemv_smem_bytes(bool raw, bool full_tiles, bool x_resident, int stages, int batch, int cols,
-                              int layout = kLayoutClassic) {
+                              bool wide = false) {
   size_t per_stage = stage_weight_bytes(raw, full_tiles) + (x_resident ? 0 : x_stage_bytes(full_tiles, batch));
   size_t bytes = 1024;                                                  // alignment slack
   bytes += (size_t)stages * per_stage;
   if (x_resident) bytes += (size_t)batch * x_resident_stride(cols);
-  bytes += 2 * (size_t)consumer_warps(layout) * 16 * batch * 4;        // two row-reduction buffers
-  if (!raw) bytes += (size_t)rec_slots(layout) * kRecSlotBytes;         // escape records
+  bytes += 2 * (size_t)consumer_warps(wide) * 16 * batch * 4;          // two row-reduction buffers
+  if (!raw) bytes += (size_t)rec_slots(wide) * kRecSlotBytes;           // escape records
   bytes += (size_t)stages * 16 + 128;                                   // barriers
   return bytes;
 }

@@ -197,10 +197,9 @@ def test_fused_gemv_matches_fp64_oracle(kind, rows, cols, batch):
 def test_launch_table_reaches_every_configuration():
     """The parity shapes above run every kernel configuration: 4-tile stages
     with x resident or staged, 8-tile stages (x always resident), each in row
-    mode and stream-K, 8-tile stages with a pipeline deeper than 2, the
+    mode and stream-K, 8-tile stages with a pipeline deeper than 2, and the
     wide layout (one CTA per SM, x resident, 4-tile stages taken in turn by
-    its warp groups; row mode only) and tile pairs (one CTA per SM, 8-tile
-    stages, two consumer warps per tile)."""
+    its warp groups; row mode only)."""
     from se12_b200 import _lib
 
     sms = torch.cuda.get_device_properties(0).multi_processor_count
@@ -213,21 +212,18 @@ def test_launch_table_reaches_every_configuration():
             cfg = _lib.Se12LaunchConfigStruct()
             assert _lib.load().se12_gemv_plan(rows, cols, batch, sms, ctypes.byref(cfg)) == 0
             assert {name: getattr(cfg, name) for name, _ in cfg._fields_} == c
-            if c["wide"] == 1:
+            if c["wide"]:
                 assert c["threads"] == 704 and c["stage_tiles"] == 4 and c["x_resident"] == 1 and c["stages"] >= 7
                 assert c["ctas_per_sm"] == 1 and 1 <= c["grid"] <= sms and batch <= 8 and c["row_mode"] == 1
-            elif c["wide"] == 2:
-                assert c["threads"] == 576 and c["stage_tiles"] == 8 and c["x_resident"] == 1
-                assert c["ctas_per_sm"] == 1 and 1 <= c["grid"] <= sms
             else:
                 assert c["threads"] == 320 and 1 <= c["grid"] <= 2 * sms
-            layout = {1: "wide", 2: "pairs"}.get(c["wide"], c["stage_tiles"])
+            layout = "wide" if c["wide"] else c["stage_tiles"]
             seen.add((layout, c["x_resident"], c["row_mode"]))
             deep = deep or (c["stage_tiles"] == 8 and c["stages"] > 2)
     if sms != 148:
         pytest.skip("the shapes are chosen for 148 SMs")
-    assert all(x == 1 for t, x, _ in seen if t in (8, "wide", "pairs")), "8-tile stages or the wide layout with staged x"
-    missing = {(4, x, r) for x in (0, 1) for r in (0, 1)} | {(8, 1, r) for r in (0, 1)} | {("wide", 1, 1), ("pairs", 1, 1)}
+    assert all(x == 1 for t, x, _ in seen if t in (8, "wide")), "8-tile stages or the wide layout with staged x"
+    missing = {(4, x, r) for x in (0, 1) for r in (0, 1)} | {(8, 1, r) for r in (0, 1)} | {("wide", 1, 1)}
     missing -= seen
     assert not missing, f"configurations no parity shape reaches: {sorted(missing, key=str)}"
     assert deep
