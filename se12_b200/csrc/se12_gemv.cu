@@ -164,10 +164,14 @@ __device__ __forceinline__ void add_acc(float (&acc)[2][NB][4], const float (&pa
       for (int q = 0; q < 4; ++q) acc[h][nb][q] += part[h][nb][q];
 }
 
-template <int NB, bool RAW, bool XRES, bool FULL, bool AR, bool WIDE>
-__global__ void __launch_bounds__(gemv_threads(WIDE), WIDE ? 1 : 2) gemv_kernel(const __grid_constant__ CUtensorMap map0,
-                                                                                const __grid_constant__ CUtensorMap map1,
-                                                                                const GemvArgs a) {
+// LAYOUT: kLayoutClassic (two CTAs per SM: 96 registers a thread),
+// kLayoutWide, or kLayoutSolo (the classic layout in a configuration whose
+// shared memory holds one CTA per SM: compiled for one CTA per SM, so the
+// two-block accumulators of batch 9..16 need not spill).
+template <int NB, bool RAW, bool XRES, bool FULL, bool AR, int LAYOUT>
+__global__ void __launch_bounds__(gemv_threads(LAYOUT == kLayoutWide), LAYOUT == kLayoutClassic ? 2 : 1)
+    gemv_kernel(const __grid_constant__ CUtensorMap map0, const __grid_constant__ CUtensorMap map1, const GemvArgs a) {
+  constexpr bool WIDE = LAYOUT == kLayoutWide;
   static_assert(!(RAW && FULL), "the dense baseline runs 4-tile stages");
   static_assert(!WIDE || (!RAW && XRES && !FULL && !AR), "the wide layout is SE12 with x resident");
   constexpr int kWeightBytes = stage_weight_bytes(RAW, FULL);
@@ -1182,13 +1186,23 @@ cudaError_t launch_gemv(bool raw, const CUtensorMap& map0, const CUtensorMap& ma
        {nullptr, gemv_kernel<2, false, true, true, true, false>}}};
   // the wide layout (SE12, x resident, no all-reduce, batch <= 8: at 80
   // registers the two-block accumulators spill)
-  static const Kernel table_wide[2] = {gemv_kernel<1, false, true, false, false, true>, nullptr};
+  static const Kernel table_wide[2] = {gemv_kernel<1, false, true, false, false, kLayoutWide>, nullptr};
+  // SE12 without the all-reduce, one CTA per SM: [batch blocks][4-tile,
+  // 8-tile][x resident]; the configurations the launch table picks with one
+  // CTA per SM (4-tile stages at batch <= 8 never are: they run the classic build)
+  static const Kernel table_solo[2][2][2] = {
+      {{nullptr, nullptr}, {nullptr, gemv_kernel<1, false, true, true, false, kLayoutSolo>}},
+      {{gemv_kernel<2, false, false, false, false, kLayoutSolo>, gemv_kernel<2, false, true, false, false, kLayoutSolo>},
+       {nullptr, gemv_kernel<2, false, true, true, false, kLayoutSolo>}}};
   const int kind = raw ? 2 : (a.full_tiles ? 1 : 0);
   const int blocks = nblocks == 1 ? 0 : 1;
   const bool ar = a.peers.world > 1;
   if (ar && raw) return cudaErrorInvalidValue;
   if (a.wide && (raw || ar || a.full_tiles || !a.x_resident || a.stages <= kWideGroups)) return cudaErrorInvalidValue;
+  const Kernel solo =
+      (!a.wide && !raw && !ar && smem > kCoResidentSmem) ? table_solo[blocks][kind][a.x_resident ? 1 : 0] : nullptr;
   const Kernel kernel = a.wide ? table_wide[blocks]
+                        : solo ? solo
                         : ar   ? table_ar[blocks][kind][a.x_resident ? 1 : 0]
                                : table[blocks][kind][a.x_resident ? 1 : 0];
   if (!kernel) return cudaErrorInvalidValue;

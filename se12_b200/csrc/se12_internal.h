@@ -110,6 +110,12 @@ constexpr int kXRowStride = 576;        // bytes per (tile, batch row) x slice w
 // consumers' row partials).
 constexpr int kConsumerWarps = 8;
 constexpr int kWideGroups = 5;
+// Kernel builds (the GEMV kernel's LAYOUT): classic (up to two CTAs per SM),
+// wide, and solo (the classic layout where shared memory holds one CTA per
+// SM, built for one CTA per SM).
+constexpr int kLayoutClassic = 0;
+constexpr int kLayoutWide = 1;
+constexpr int kLayoutSolo = 2;
 constexpr int kMaxWideStages = kWideGroups + 4;  // the deepest wide pipeline the launch table picks
 __host__ __device__ constexpr int consumer_warps(bool wide) { return wide ? kWideGroups * 4 : kConsumerWarps; }
 __host__ __device__ constexpr int gemv_threads(bool wide) { return (consumer_warps(wide) + 2) * 32; }

@@ -199,11 +199,14 @@ def test_launch_table_reaches_every_configuration():
     with x resident or staged, 8-tile stages (x always resident), each in row
     mode and stream-K, 8-tile stages with a pipeline deeper than 2, and the
     wide layout (one CTA per SM, x resident, 4-tile stages taken in turn by
-    its warp groups; row mode only)."""
+    its warp groups; row mode only). Configurations with one CTA per SM run
+    the kernel builds made for one CTA per SM (more registers): the shapes
+    reach each of them (8-tile stages at batch <= 8; 4-tile stages with x
+    resident or staged and 8-tile stages at batch 9..16)."""
     from se12_b200 import _lib
 
     sms = torch.cuda.get_device_properties(0).multi_processor_count
-    seen, deep = set(), False
+    seen, deep, solo = set(), False, set()
     for kind, rows, cols in GEMV_SHAPES:
         m = gemv_fixture(kind, rows, cols)[2]
         for batch in (1, 2, 4, 8, 16):
@@ -219,6 +222,8 @@ def test_launch_table_reaches_every_configuration():
                 assert c["threads"] == 320 and 1 <= c["grid"] <= 2 * sms
             layout = "wide" if c["wide"] else c["stage_tiles"]
             seen.add((layout, c["x_resident"], c["row_mode"]))
+            if not c["wide"] and c["ctas_per_sm"] == 1:
+                solo.add((1 if batch <= 8 else 2, c["stage_tiles"], c["x_resident"]))
             deep = deep or (c["stage_tiles"] == 8 and c["stages"] > 2)
     if sms != 148:
         pytest.skip("the shapes are chosen for 148 SMs")
@@ -227,6 +232,7 @@ def test_launch_table_reaches_every_configuration():
     missing -= seen
     assert not missing, f"configurations no parity shape reaches: {sorted(missing, key=str)}"
     assert deep
+    assert solo >= {(1, 8, 1), (2, 4, 0), (2, 4, 1), (2, 8, 1)}, sorted(solo)
 
 
 @pytest.mark.parametrize("batch", [3, 9, 20])
