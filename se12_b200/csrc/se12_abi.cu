@@ -138,8 +138,10 @@ int tiles_of(int rows, int cols) {
 //    stage time + the stream-K fixup. In units of a 4-tile stage's overhead-
 //    inclusive half-tile time: a 4-tile stage (two CTAs per SM) costs 1.65,
 //    an 8-tile stage 2.0 (each warp does a whole tile, decoding it group by
-//    group); x 0.95 when one CTA has the SM to itself, x 1.5 when x is
-//    staged; a fixup 3.0 (a round trip through L2 on a loaded GPU). The
+//    group); x 0.95 when one CTA has the SM to itself, x 1.6 for two CTAs
+//    per SM at batch 9..16 (their build spills, the one-CTA build does
+//    not), x 1.5 when x is staged; a fixup 3.0 (a round trip through L2 on
+//    a loaded GPU). The
 //    wide layout (SE12, x resident, one CTA per SM with kWideGroups 4-tile
 //    stages in work at once, row mode only) costs 3.0 per CTA (its longer
 //    fill and drain) + 0.48 per 4-tile stage: it streams a little faster and
@@ -196,6 +198,9 @@ LaunchConfig choose_config(bool raw, int tiles, int cols, int batch, int sm_coun
   constexpr double kStageCost8 = 2.0;   // an 8-tile stage
   constexpr double kAloneFactor = 0.95;
   constexpr double kStagedXFactor = 1.5;
+  // batch 9..16 with two CTAs per SM: that build (96 registers) spills its
+  // two-block accumulators, the one-CTA build does not
+  constexpr double kSharedTwoBlocks = 1.6;
   constexpr double kFixup = 3.0;
   constexpr double kWideFixed = 3.0;   // the wide layout: a longer pipeline fill and drain per CTA,
   constexpr double kWideStage = 0.48;  // then a 4-tile stage (kWideGroups in work at once, one CTA per SM)
@@ -205,7 +210,8 @@ LaunchConfig choose_config(bool raw, int tiles, int cols, int batch, int sm_coun
     const MemoryChoice& mem = full ? mem8 : mem4;
     if (!mem.per_sm) continue;
     const int stage = se12::stage_tiles(full);
-    const double stage_cost = (full ? kStageCost8 : kStageCost4) * (mem.per_sm == 1 ? kAloneFactor : 1.0) *
+    const double stage_cost = (full ? kStageCost8 : kStageCost4) *
+                              (mem.per_sm == 1 ? kAloneFactor : (batch > 8 ? kSharedTwoBlocks : 1.0)) *
                               (mem.x_resident ? 1.0 : kStagedXFactor);
     const int slots = mem.per_sm * sm_count;
     const int units = (tiles + stage - 1) / stage;

@@ -328,15 +328,38 @@ __global__ void __launch_bounds__(gemv_threads(LAYOUT == kLayoutWide), LAYOUT ==
       }
       __syncwarp();
     };
-    // staged x of stage i: lane l copies 16-byte chunk l (columns 8 l .. 8 l
-    // + 7) of every (tile, batch row) slice; columns past K are written as
-    // zeros (the chunk holding column K with a plain load and a mask)
-    auto issue_x = [sm8, o_x, full, xg, ldx, xstage, tend, KT, K, B, tstart, lane](int i, int s) {
+    // staged x of stage i. A tile column whose 256 columns all lie inside K:
+    // one 512-byte bulk copy per (tile, batch row) slice, the slices spread
+    // over the lanes (x rows start 16-byte aligned: ldx % 8 == 0). The
+    // ragged last tile column: lane l copies 16-byte chunk l (columns 8 l ..
+    // 8 l + 7) of each slice with cp.async, columns past K written as zeros
+    // (the chunk holding column K with a plain load and a mask).
+    auto issue_x = [sm8, o_x, full, xg, ldx, xstage, tend, KT, K, B, tstart, lane, pol_x](int i, int s) {
       const int tile0 = tstart + i * kStage;
       const int ntl = min(kStage, tend - tile0);
-      int kt = tile0 % KT;
-      for (int j = 0; j < ntl; ++j) {
+      const int kt0 = tile0 % KT;
+      int whole = 0;  // tiles of the stage whose columns all lie inside K
+      bool ragged = false;
+      for (int j = 0, kt = kt0; j < ntl; ++j) {
+        if ((kt + 1) * kTileCols <= K) ++whole;
+        else ragged = true;
+        if (++kt == KT) kt = 0;
+      }
+      if (lane == 0 && whole) mbar_expect_tx(&full[s], static_cast<uint32_t>(whole * B) * 512u);
+      __syncwarp();
+      for (int q = lane; q < ntl * B; q += 32) {
+        const int j = q / B, b = q - j * B;
+        int kt = kt0 + j;
+        if (kt >= KT) kt -= KT;
+        if ((kt + 1) * kTileCols <= K)
+          bulk_load(sm8 + o_x + s * xstage + (j * B + b) * kXRowStride,
+                    xg + static_cast<size_t>(b) * ldx + kt * kTileCols, 512u, &full[s], pol_x);
+      }
+      int kt = kt0;
+      for (int j = 0; ragged && j < ntl; ++j) {
         const int col = kt * kTileCols + lane * 8;
+        if (++kt == KT) kt = 0;
+        if (col - lane * 8 + kTileCols <= K) continue;  // a whole tile: copied above
         for (int b = 0; b < B; ++b) {
           uint8_t* dst = sm8 + o_x + s * xstage + (j * B + b) * kXRowStride + lane * 16;
           const uint16_t* src = xg + static_cast<size_t>(b) * ldx + col;
@@ -356,9 +379,8 @@ __global__ void __launch_bounds__(gemv_threads(LAYOUT == kLayoutWide), LAYOUT ==
             *reinterpret_cast<uint4*>(dst) = v;
           }
         }
-        if (++kt == KT) kt = 0;
       }
-      cp_async_mbar_arrive(&full[s]);
+      if (ragged) cp_async_mbar_arrive(&full[s]);
       __syncwarp();
       if (lane == 0) mbar_arrive(&full[s]);
       __syncwarp();

@@ -148,6 +148,10 @@ GEMV_SHAPES = [
     ("synthetic", 16, 3584),       # 4-tile stages, row mode, staged x (batch 8)
     ("synthetic", 1024, 5120),     # 8-tile stages, stream-K (batch 1)
     ("synthetic", 4096, 1792),     # 8-tile stages, 3-deep pipeline, one CTA per SM (batch 16)
+    # staged x with a ragged last tile column (batch >= 4 / 8): whole tiles by
+    # bulk copy, the last one by cp.async with zeros past K (K % 8 != 0 too)
+    ("synthetic", 16, 20000),
+    ("synthetic", 32, 12300),
 ]
 
 
