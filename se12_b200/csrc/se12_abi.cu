@@ -182,7 +182,7 @@ MemoryChoice choose_memory(bool raw, bool full, int batch, int cols) {
 // that fits (with 1 KB to spare for the kernel's static shared memory), so
 // that two stages or more are in flight.
 MemoryChoice choose_memory_wide(int batch, int cols) {
-  if (batch > 8) return {0, 0, 0};  // one block of 8 batch columns (more spill at 80 registers)
+  if (batch > 8) return {0, 0, 0};  // one block of 8 batch columns (two spill at 96 registers)
   for (int stages = se12::kMaxWideStages; stages >= se12::kWideGroups + 2; --stages)
     if (se12::gemv_smem_bytes(false, false, true, stages, batch, cols, true) + 1024 <= se12::kMaxSmemPerCta)
       return {1, stages, 1};

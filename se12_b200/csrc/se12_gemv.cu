@@ -1206,7 +1206,7 @@ cudaError_t launch_gemv(bool raw, const CUtensorMap& map0, const CUtensorMap& ma
        {nullptr, gemv_kernel<1, false, true, true, true, false>}},
       {{gemv_kernel<2, false, false, false, true, false>, gemv_kernel<2, false, true, false, true, false>},
        {nullptr, gemv_kernel<2, false, true, true, true, false>}}};
-  // the wide layout (SE12, x resident, no all-reduce, batch <= 8: at 80
+  // the wide layout (SE12, x resident, no all-reduce, batch <= 8: at 96
   // registers the two-block accumulators spill)
   static const Kernel table_wide[2] = {gemv_kernel<1, false, true, false, false, kLayoutWide>, nullptr};
   // SE12 without the all-reduce, one CTA per SM: [batch blocks][4-tile,

@@ -90,8 +90,8 @@ struct GemvArgs {
 //   4 tiles in the wide layout (SE12 with x resident, one CTA per SM):
 //   kWideGroups groups of 4 consumer warps take the stages in turn (group
 //   c the stages i with i % kWideGroups == c), warp w taking tile w % 4.
-//   22 warps leave 80 registers a thread, with 5 consumer warps per SM
-//   sub-partition instead of 4.
+//   18 warps (16 consumers) leave 96 registers a thread. (5 groups, 22
+//   warps, leave 80 and spill more: batch 4 and 8 steps 2-3 % slower.)
 // SE12 weights arrive as 3-D TMA boxes [64 rows][2 halves][128 B] of sm
 // (16 KB) and 2-D boxes [64 rows][128 B] of ec (8 KB), both with the 128-byte
 // swizzle: one of each per 4 tiles, the ec boxes after the stage's sm boxes.
@@ -109,7 +109,7 @@ constexpr int kXRowStride = 576;        // bytes per (tile, batch row) x slice w
 // producer warp (TMA / bulk copies), then the reducer warp (sums the
 // consumers' row partials).
 constexpr int kConsumerWarps = 8;
-constexpr int kWideGroups = 5;
+constexpr int kWideGroups = 4;
 // Kernel builds (the GEMV kernel's LAYOUT): classic (up to two CTAs per SM),
 // wide, and solo (the classic layout where shared memory holds one CTA per
 // SM, built for one CTA per SM).

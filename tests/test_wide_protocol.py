@@ -1,8 +1,8 @@
 """A model of the wide-layout GEMV's barrier protocol (se12_b200/csrc/se12_gemv.cu,
-gemv_kernel<..., WIDE = true>), checked on the CPU under random interleavings.
+gemv_kernel<..., LAYOUT = kLayoutWide>), checked on the CPU under random interleavings.
 
-In the wide layout one CTA has a producer warp, 5 groups of 4 consumer warps
-that take the pipeline stages in turn (group c the stages i with i % 5 == c),
+In the wide layout one CTA has a producer warp, 4 groups of 4 consumer warps
+that take the pipeline stages in turn (group c the stages i with i % 4 == c),
 and a reducer warp. The waits are mbarrier parity waits, and a parity wait is
 exact only while the barrier is at most one phase away from the phase
 waited for. A group never waits on the stage that used its slot before (that
@@ -17,7 +17,7 @@ exact. The model follows the kernel's steps:
   warps, every row, in order: the reducer's buffer is free once row r - 2 is
   summed), settle the record groups in order, wait for stage i - S consumed,
   wait for stage i landed, release the stage and the records;
-* reducer: per row, wait for all 20 deposits, sum, free the buffer.
+* reducer: per row, wait for all 16 deposits, sum, free the buffer.
 
 The barriers keep arrival counts and phases and answer parity waits as the
 hardware does. The test fails if a parity wait passes before its phase
@@ -32,7 +32,7 @@ import random
 
 import pytest
 
-GROUPS, STAGE_WARPS, CONSUMERS, REC_SLOTS, REC_STAGES = 5, 4, 20, 4, 4
+GROUPS, STAGE_WARPS, CONSUMERS, REC_SLOTS, REC_STAGES = 4, 4, 16, 4, 4
 
 
 class ProtocolError(Exception):
@@ -193,8 +193,8 @@ def simulate(tile_cols, rows, stages, seed, land_probability, wait_previous_stag
 
 
 # (tile columns per row, rows in the CTA, pipeline stages): 1-tile rows,
-# rows shorter and longer than a round of 20 tiles, depths 7..9
-CASES = [(9, 12, 8), (1, 40, 8), (36, 3, 8), (2, 20, 7), (5, 9, 9), (18, 6, 8)]
+# rows shorter and longer than a round of 16 tiles, depths 6..8
+CASES = [(9, 12, 8), (1, 40, 8), (36, 3, 7), (2, 20, 6), (5, 9, 8), (18, 6, 7)]
 
 
 @pytest.mark.parametrize("tile_cols,rows,stages", CASES)
