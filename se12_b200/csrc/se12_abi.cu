@@ -29,7 +29,12 @@ int fail(int status, const std::string& message) {
   return status;
 }
 
+// A CUDA call of this library failed: report it and take it out of the
+// thread's last-error state, so that the next call (whose launch checks
+// cudaGetLastError) is not blamed for it. A sticky error (a lost context)
+// stays, as CUDA keeps it.
 int cuda_fail(cudaError_t err, const char* what) {
+  (void)cudaGetLastError();
   return fail(SE12_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(err));
 }
 
@@ -168,24 +173,34 @@ struct MemoryChoice {
 MemoryChoice choose_memory(bool raw, bool full, int batch, int cols) {
   // (x resident?, stages) in order of preference
   static const int kOrder[][2] = {{1, 4}, {1, 3}, {0, 4}, {0, 3}, {1, 2}, {0, 2}};
-  for (const size_t limit : {se12::kCoResidentSmem, se12::kMaxSmemPerCta})
+  for (const size_t limit : {se12::kCoResidentSmem, se12::kMaxSmemPerCta}) {
+    // 8-tile stages in one CTA per SM: two stages, which measured faster
+    // than three or four at batch 1-4 (the 2B down projection at batch 4
+    // 12.5 against 13.1 us; q/k/v, gate/up and the 9B shapes by 1-5 %)
+    if (full && limit == se12::kMaxSmemPerCta) {
+      if (se12::gemv_smem_bytes(raw, true, true, 2, batch, cols) + 1024 <= limit) return {1, 2, 1};
+      break;
+    }
     for (const auto& cand : kOrder) {
       if (full && !cand[0]) continue;
       if (se12::gemv_smem_bytes(raw, full, cand[0] != 0, cand[1], batch, cols) <= limit)
         return {cand[0], cand[1], limit == se12::kCoResidentSmem ? 2 : 1};
     }
+  }
   return {0, 0, 0};
 }
 
 // The wide layout (one CTA per SM, kWideGroups stages in work at once):
-// x resident and the deepest pipeline of at least kWideGroups + 2 stages
-// that fits (with 1 KB to spare for the kernel's static shared memory), so
-// that two stages or more are in flight.
+// x resident and a pipeline of kWideGroups + 2 stages, so that two stages
+// are in flight, if it fits (with 1 KB to spare for the kernel's static
+// shared memory). Deeper pipelines measured slower with 4 groups (the 2B
+// lm_head 195.0 / 195.3 / 195.8 us at 6 / 7 / 8 stages; down 12.4 / 12.8 /
+// 13.0 us; gate/up at batch 4 20.0 / 20.3 / 20.5 us).
 MemoryChoice choose_memory_wide(int batch, int cols) {
   if (batch > 8) return {0, 0, 0};  // one block of 8 batch columns (two spill at 96 registers)
-  for (int stages = se12::kMaxWideStages; stages >= se12::kWideGroups + 2; --stages)
-    if (se12::gemv_smem_bytes(false, false, true, stages, batch, cols, true) + 1024 <= se12::kMaxSmemPerCta)
-      return {1, stages, 1};
+  const int stages = se12::kWideGroups + 2;
+  if (se12::gemv_smem_bytes(false, false, true, stages, batch, cols, true) + 1024 <= se12::kMaxSmemPerCta)
+    return {1, stages, 1};
   return {0, 0, 0};
 }
 

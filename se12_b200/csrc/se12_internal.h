@@ -116,7 +116,6 @@ constexpr int kWideGroups = 4;
 constexpr int kLayoutClassic = 0;
 constexpr int kLayoutWide = 1;
 constexpr int kLayoutSolo = 2;
-constexpr int kMaxWideStages = kWideGroups + 4;  // the deepest wide pipeline the launch table picks
 __host__ __device__ constexpr int consumer_warps(bool wide) { return wide ? kWideGroups * 4 : kConsumerWarps; }
 __host__ __device__ constexpr int gemv_threads(bool wide) { return (consumer_warps(wide) + 2) * 32; }
 // Escape records (escape positions, escape slots, fallback indices) of
