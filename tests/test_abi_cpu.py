@@ -177,6 +177,31 @@ def test_launch_table_choices_for_gemma2_2b(lib):
     assert layout == {"lm_head": "wide", "down": "wide", "gate_up": 8, "qkv": 8, "o": 8}
 
 
+def test_launch_table_choices_beyond_batch_1(lib):
+    """The choices measured best on one B200 (148 SMs), each against forced
+    alternatives in stacks of the Gemma-2-2B shapes:
+    * the wide layout runs a 6-stage pipeline (lm_head 195.0 us against
+      195.8 at 8 stages);
+    * 8-tile stages in one CTA per SM run 2 stages (down at batch 4: 12.5
+      against 13.1 us at 3);
+    * at batch 9 an x-resident GEMV runs one CTA per SM with 8-tile stages,
+      not the two-CTA build that spills (gate/up 24.5 against 37.0 us,
+      lm_head 255 against 434 us); the staged-x down projection keeps two
+      CTAs per SM (23.2 against 25.6 us)."""
+    def layout(rows, cols, batch):
+        status, c = plan(lib, rows, cols, batch, 148)
+        assert status == 0
+        return ("wide" if c["wide"] else c["stage_tiles"], c["stages"], c["ctas_per_sm"], c["x_resident"])
+
+    assert layout(256000, 2304, 1) == ("wide", 6, 1, 1)
+    assert layout(2304, 9216, 1) == ("wide", 6, 1, 1)
+    assert layout(2304, 9216, 4) == (8, 2, 1, 1)
+    assert layout(18432, 2304, 9) == (8, 2, 1, 1)
+    assert layout(256000, 2304, 9) == (8, 2, 1, 1)
+    assert layout(2304, 9216, 9) == (4, 2, 2, 0)
+    assert layout(18432, 2304, 16) == (8, 2, 1, 1)
+
+
 def test_plan_rejects_bad_arguments(lib):
     from se12_b200 import _lib
 
