@@ -246,7 +246,13 @@ LaunchConfig choose_config(bool raw, int tiles, int cols, int batch, int sm_coun
       best.grid = row_mode ? grid_rows : grid_sk;
     }
   }
-  const MemoryChoice memw = (raw || !allow_wide) ? MemoryChoice{0, 0, 0} : choose_memory_wide(batch, cols);
+  // Every tile row in one wave of one CTA per SM, and 8-tile stages that
+  // hold one CTA per SM: those run faster than the wide layout (the 2B down
+  // projection, 144 rows of 36 tiles: 12.16 against 12.37 us at batch 1,
+  // 12.23 against 12.52 at batch 2)
+  const bool one_wave_full = !raw && mem8.per_sm == 1 && tile_rows <= sm_count;
+  const MemoryChoice memw =
+      (raw || !allow_wide || one_wave_full) ? MemoryChoice{0, 0, 0} : choose_memory_wide(batch, cols);
   if (memw.per_sm) {
     // row mode only: with the fixup, stream-K in the wide layout never
     // beats stream-K in the others (finer grained, two CTAs per SM)

@@ -165,23 +165,26 @@ def test_launch_table_stays_within_the_hardware(lib, sm_count):
 
 def test_launch_table_choices_for_gemma2_2b(lib):
     """On 148 SMs at batch 1 the table follows the measured stacked timings:
-    the wide layout for the lm_head (197 us against 199 us) and the down
-    projection (12.6 against 13.8 us), 8-tile stages with two CTAs per SM for
-    q/k/v, o and gate_up (where the wide layout measured 1.8-2 us slower)."""
+    the wide layout for the lm_head (195 us against 199 us), 8-tile stages
+    in one CTA per SM for the down projection, whose 144 tile rows fit one
+    wave (12.16 against 12.37 us wide), 8-tile stages with two CTAs per SM
+    for q/k/v, o and gate_up (where the wide layout measured 1.3-1.8 us
+    slower)."""
     layout = {}
     for name, rows, cols in [("lm_head", 256000, 2304), ("down", 2304, 9216), ("gate_up", 18432, 2304),
                              ("qkv", 4096, 2304), ("o", 2304, 2048)]:
         status, c = plan(lib, rows, cols, 1, 148)
         assert status == 0
         layout[name] = "wide" if c["wide"] else c["stage_tiles"]
-    assert layout == {"lm_head": "wide", "down": "wide", "gate_up": 8, "qkv": 8, "o": 8}
+    assert layout == {"lm_head": "wide", "down": 8, "gate_up": 8, "qkv": 8, "o": 8}
 
 
 def test_launch_table_choices_beyond_batch_1(lib):
     """The choices measured best on one B200 (148 SMs), each against forced
     alternatives in stacks of the Gemma-2-2B shapes:
     * the wide layout runs a 6-stage pipeline (lm_head 195.0 us against
-      195.8 at 8 stages);
+      195.8 at 8 stages); a matrix whose tile rows fit one wave of one CTA
+      per SM runs 8-tile stages instead (the 2B down projection);
     * 8-tile stages in one CTA per SM run 2 stages (down at batch 4: 12.5
       against 13.1 us at 3);
     * at batch 9 an x-resident GEMV runs one CTA per SM with 8-tile stages,
@@ -194,7 +197,8 @@ def test_launch_table_choices_beyond_batch_1(lib):
         return ("wide" if c["wide"] else c["stage_tiles"], c["stages"], c["ctas_per_sm"], c["x_resident"])
 
     assert layout(256000, 2304, 1) == ("wide", 6, 1, 1)
-    assert layout(2304, 9216, 1) == ("wide", 6, 1, 1)
+    assert layout(2304, 9216, 1) == (8, 2, 1, 1)
+    assert layout(18432, 2304, 4) == ("wide", 6, 1, 1)
     assert layout(2304, 9216, 4) == (8, 2, 1, 1)
     assert layout(18432, 2304, 9) == (8, 2, 1, 1)
     assert layout(256000, 2304, 9) == (8, 2, 1, 1)

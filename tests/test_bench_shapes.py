@@ -101,9 +101,11 @@ def test_bench_shape_matches_fp64(name, batch):
 def test_bench_shapes_reach_the_benchmark_layouts():
     """The matrices above run the launch configurations the benchmark uses
     for them (so the parity covers the timed kernels): on a 148-SM B200 the
-    LM head and the down projection take the wide layout at batch 1."""
+    LM head takes the wide layout at batch 1, and the down projection (144
+    tile rows, one wave) 8-tile stages in one CTA per SM."""
     if torch.cuda.get_device_properties(0).multi_processor_count != 148:
         pytest.skip("launch choices are stated for 148 SMs")
     assert bench_matrix("lm_head")[0].launch_config(1)["wide"] == 1
-    assert bench_matrix("down_proj")[0].launch_config(1)["wide"] == 1
+    down = bench_matrix("down_proj")[0].launch_config(1)
+    assert down["wide"] == 0 and down["stage_tiles"] == 8 and down["ctas_per_sm"] == 1
     assert bench_matrix("gate_up_grouped")[0].launch_config(1)["stage_tiles"] == 8

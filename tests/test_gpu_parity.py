@@ -152,6 +152,7 @@ GEMV_SHAPES = [
     # bulk copy, the last one by cp.async with zeros past K (K % 8 != 0 too)
     ("synthetic", 16, 20000),
     ("synthetic", 32, 12300),
+    ("synthetic", 4816, 2304),     # the wide layout (batch 4, 8)
 ]
 
 
